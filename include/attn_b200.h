@@ -1,0 +1,154 @@
+/*
+ * attn_b200.h — C ABI of the B200 (sm_100a) causal multi-head attention library.
+ *
+ * Replaces the kernels and host NumPy that llm-gpu-5's MultiHeadAttention runs today:
+ *   - fused_attention_forward_kernel   core/mha_kernels.py:404-521  (launched at model/gpt.py:587-592)
+ *   - the NumPy attention backward     model/gpt.py:652-689
+ *   - matmul_2d_kernel projections     core/kernels.py:119-140      (model/gpt.py:558, :629)
+ *   - split_heads_kernel / merge_heads_kernel  core/mha_kernels.py:534-584 (model/gpt.py:578-598)
+ *   - the unwired GPU grad kernels     core/mha_kernels.py:195-236, 592-680
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are raw device addresses; buffers are allocated by the caller.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Return value: ATTN_OK (0) or a negative ATTN_ERR_* code.  On a bad argument nothing is
+ *     launched.  attn_last_error_string() describes the last failure of the calling thread.
+ *   - Attention tensors are addressed by element strides: element (b, t, h, d) of Q/K/V/dQ/dK/dV
+ *     lives at ptr[b*sb + t*st + h*sh + d] (d contiguous).  Both the reference's split layout
+ *     [B*NH, T, D] (sb = NH*T*D, st = D, sh = T*D) and the token layout of the fused projection
+ *     [B*T, 3C] (sb = T*3C, st = 3C, sh = D, K at +C, V at +2C) are expressible, so the head
+ *     split/merge of the reference can be folded into addressing.
+ *   - lse is float32 [B, NH, T] (natural-log log-sum-exp of the scaled causal scores per row);
+ *     the backward recomputes P = exp(scale*q.k - lse) instead of storing the T x T matrix.
+ */
+#ifndef ATTN_B200_H
+#define ATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ATTN_OK 0
+#define ATTN_ERR_ARG (-1)         /* invalid argument: null pointer, bad shape, bad stride   */
+#define ATTN_ERR_UNSUPPORTED (-2) /* valid but not implemented (e.g. head_dim > 128)          */
+#define ATTN_ERR_CUDA (-3)        /* a CUDA runtime/driver call failed                        */
+#define ATTN_ERR_WORKSPACE (-4)   /* workspace missing or smaller than *_workspace_size()     */
+
+#define ATTN_F32 0  /* float32                       */
+#define ATTN_BF16 1 /* bfloat16 (stored as uint16_t) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int attn_version(void);
+
+/* Text of the last error raised on the calling thread ("" if none). */
+const char* attn_last_error_string(void);
+
+/* Number of kernels this library has launched in this process (all entry points). */
+uint64_t attn_launch_count(void);
+
+/*
+ * Causal attention forward: O = softmax(scale * Q K^T + causal mask) V, plus lse.
+ * Replaces fused_attention_forward_kernel (core/mha_kernels.py:404-521); instead of writing the
+ * normalised probabilities Scores[B*NH,T,T] it writes lse[B,NH,T].
+ * dtype ATTN_F32: CUDA-core fp32 path (any D <= 128, D % 4 == 0).
+ * dtype ATTN_BF16: tcgen05 tensor-core path for D == 64 (TMA-staged K/V, TMEM accumulators),
+ *                  CUDA-core path otherwise; fp32 softmax statistics and accumulation.
+ * Q/K/V share the input strides; O uses the output strides.
+ */
+int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+             int B, int NH, int T, int D,
+             int64_t in_sb, int64_t in_st, int64_t in_sh,
+             int64_t out_sb, int64_t out_st, int64_t out_sh,
+             float scale, int dtype, void* stream);
+
+/* Bytes of workspace attn_bwd needs for this problem (row dots dO.O, dQ accumulators). */
+size_t attn_bwd_workspace_size(int B, int NH, int T, int D, int dtype);
+
+/*
+ * Causal attention backward (the softmax VJP with the scale applied to dS, then dQ/dK/dV).
+ * Replaces the NumPy steps of model/gpt.py:669-680 and the unwired kernels
+ * softmax_fused_backward / matmul_grad_{q,k,v} (core/mha_kernels.py:195-236, 592-680).
+ * q, k, v, dq, dk, dv use the input strides; o and dout use the output strides.
+ * workspace: device buffer of at least attn_bwd_workspace_size() bytes.
+ */
+int attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+             const float* lse, void* dq, void* dk, void* dv,
+             void* workspace, size_t workspace_bytes,
+             int B, int NH, int T, int D,
+             int64_t in_sb, int64_t in_st, int64_t in_sh,
+             int64_t out_sb, int64_t out_st, int64_t out_sh,
+             float scale, int dtype, void* stream);
+
+/*
+ * Debug/test accessor: rebuild the normalised causal probabilities from lse,
+ * P[b, h, i, j] = exp(scale * q_i . k_j - lse[b, h, i]) for j <= i, else 0, into a float32
+ * [B, NH, T, T] buffer.  This is the cache_attn_weights matrix the reference forward writes
+ * (core/mha_kernels.py:492-498, downloaded at model/gpt.py:612-614); the training path never
+ * materialises it.  q/k use the input strides of attn_fwd.
+ */
+int attn_probs(const void* q, const void* k, const float* lse, float* probs,
+               int B, int NH, int T, int D, int64_t in_sb, int64_t in_st, int64_t in_sh,
+               float scale, int dtype, void* stream);
+
+/* Bytes of workspace attn_decode needs (per-split partial softmax states). */
+size_t attn_decode_workspace_size(int B, int NH, int L, int D);
+
+/*
+ * Single-query decode: one new query row per (b, h) attending over an L-token K/V prefix
+ * (every cached key is visible).  Equals the last row of the causal forward that
+ * GenerationSession.generate re-runs per token (generate.py:611-628).
+ * q, o: element (b, h, d) at ptr[b*q_sb + h*q_sh + d].  K/V cache: element (b, l, h, d) at
+ * ptr[b*kv_sb + l*kv_sl + h*kv_sh + d].  lse may be NULL.  Split over L, then combined.
+ */
+int attn_decode(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
+                int B, int NH, int L, int D,
+                int64_t q_sb, int64_t q_sh,
+                int64_t kv_sb, int64_t kv_sl, int64_t kv_sh,
+                float scale, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Projection GEMM: C[M,N] = op(A)[M,K] . op(B)[K,N] (+ bias[N]) ; with accumulate, C += ...
+ * Replaces matmul_2d_kernel (core/kernels.py:119-140) and the projection-gradient GEMMs of
+ * model/gpt.py:666-689 (dWo = ctx^T dY, dCtx = dY Wo^T, dWqkv = x^T dQKV, dX = dQKV Wqkv^T).
+ *   a_trans = 0: A stored row-major [M][lda] (K contiguous);  1: stored [K][lda] (A = X^T).
+ *   b_trans = 0: B stored row-major [K][ldb] (N contiguous);  1: stored [N][ldb] (B = W^T).
+ * a_dtype == b_dtype.  ATTN_BF16 operands run on tcgen05 tensor cores (fp32 accumulate);
+ * ATTN_F32 operands on the CUDA-core fp32 path.  C is ATTN_F32 or ATTN_BF16; accumulate
+ * requires ATTN_F32 C.  bias is float32 or NULL.
+ */
+int attn_gemm(const void* A, int64_t lda, int a_trans,
+              const void* B, int64_t ldb, int b_trans, int ab_dtype,
+              void* C, int64_t ldc, int c_dtype, const float* bias,
+              int M, int N, int K, int accumulate, void* stream);
+
+/* Bytes of workspace attn_colsum needs. */
+size_t attn_colsum_workspace_size(int M, int N);
+
+/*
+ * Column sum out[n] = sum_m X[m, n] (accumulate: out[n] += ...), X row-major [M][ldx] of
+ * ATTN_F32 or ATTN_BF16; out float32.  The bias gradients of model/gpt.py:667 and :688.
+ * Deterministic (fixed split of rows, fixed combine order).
+ */
+int attn_colsum(const void* X, int x_dtype, int64_t ldx, int M, int N, float* out,
+                int accumulate, void* workspace, size_t workspace_bytes, void* stream);
+
+/* y[i] = bf16(x[i]) (round to nearest even), n elements. */
+int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream);
+
+/*
+ * Layout adapters with the reference's semantics (float32):
+ * split_heads_kernel (core/mha_kernels.py:534-558): QKV[B*T, 3C] -> Q/K/V[B*NH, T, HD];
+ * merge_heads_kernel (core/mha_kernels.py:567-584): ContextHeads[B*NH, T, HD] -> Context[B*T, C].
+ */
+int attn_split_heads(const float* qkv, float* q, float* k, float* v,
+                     int B, int T, int NH, int HD, void* stream);
+int attn_merge_heads(const float* ctx_heads, float* ctx, int B, int T, int NH, int HD,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATTN_B200_H */

@@ -1,0 +1,18 @@
+"""B200-native (sm_100a) causal multi-head attention for llm-gpu-5.
+
+Import by name (the directory name is not an identifier):
+
+    pkg = importlib.import_module("llm-gpu-5_b200")
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=768, num_heads=12,
+                                                attention_precision="bf16"))
+
+All compute runs in ``libattn_b200.so`` (C ABI: ``include/attn_b200.h``); importing fails if the
+library has not been built.
+"""
+from ._lib import AttnError, LIB_PATH, launch_count, lib  # noqa: F401  (fails loudly if unbuilt)
+from . import mha_ops  # noqa: F401
+from .mha import DeviceBuffer, GPTConfig, MultiHeadAttention, Parameter  # noqa: F401
+from .mha_ops import get_shared_mha_module, THREADS_PER_BLOCK, SOFTMAX_BLOCK_THREADS  # noqa: F401
+
+__all__ = ["MultiHeadAttention", "GPTConfig", "Parameter", "DeviceBuffer", "mha_ops", "AttnError",
+           "get_shared_mha_module", "launch_count"]

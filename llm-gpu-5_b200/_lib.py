@@ -1,0 +1,88 @@
+"""ctypes binding of libattn_b200.so (the C ABI declared in include/attn_b200.h).
+
+The library is the only compute path: if it is missing or fails to load, importing this module
+raises.  There is no fallback implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libattn_b200.so")
+
+ATTN_OK = 0
+ATTN_ERR_ARG = -1
+ATTN_ERR_UNSUPPORTED = -2
+ATTN_ERR_CUDA = -3
+ATTN_ERR_WORKSPACE = -4
+ATTN_F32 = 0
+ATTN_BF16 = 1
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_i64 = ctypes.c_int64
+_f = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); every function include/attn_b200.h declares
+SIGNATURES = {
+    "attn_version": (_i, []),
+    "attn_last_error_string": (ctypes.c_char_p, []),
+    "attn_launch_count": (ctypes.c_uint64, []),
+    "attn_fwd": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i, _p]),
+    "attn_bwd_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "attn_bwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _i, _i, _i, _i,
+                      _i64, _i64, _i64, _i64, _i64, _i64, _f, _i, _p]),
+    "attn_decode_workspace_size": (_sz, [_i, _i, _i, _i]),
+    "attn_decode": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _f, _i,
+                         _p, _sz, _p]),
+    "attn_probs": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _f, _i, _p]),
+    "attn_gemm": (_i, [_p, _i64, _i, _p, _i64, _i, _i, _p, _i64, _i, _p, _i, _i, _i, _i, _p]),
+    "attn_colsum_workspace_size": (_sz, [_i, _i]),
+    "attn_colsum": (_i, [_p, _i, _i64, _i, _i, _p, _i, _p, _sz, _p]),
+    "attn_cast_f32_to_bf16": (_i, [_p, _p, _i64, _p]),
+    "attn_split_heads": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p]),
+    "attn_merge_heads": (_i, [_p, _p, _i, _i, _i, _i, _p]),
+}
+
+
+class AttnError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, fn, code, msg):
+        super().__init__(f"{fn} failed with status {code}: {msg}")
+        self.code = code
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python llm-gpu-5_b200/build.py` "
+                          "(or __graft_entry__.build()); there is no non-CUDA fallback")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    s = lib.attn_last_error_string()
+    return s.decode() if s else ""
+
+
+def call(name, *args):
+    """Call a status-returning entry point and raise AttnError on failure."""
+    rc = getattr(lib, name)(*args)
+    if rc != ATTN_OK:
+        raise AttnError(name, rc, last_error())
+    return rc
+
+
+def launch_count() -> int:
+    return int(lib.attn_launch_count())

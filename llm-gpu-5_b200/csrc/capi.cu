@@ -1,0 +1,252 @@
+// extern "C" entry points of libattn_b200.so (declared in include/attn_b200.h).
+//
+// Every entry point validates its arguments before launching anything: a null pointer, a bad
+// shape, a misaligned or inconsistent stride, or a short workspace returns a negative code and
+// sets the per-thread error string; no kernel runs.  This mirrors the reference's failure
+// behaviour at the API level (MultiHeadAttention raises before touching the GPU when its caches
+// are missing, model/gpt.py:649-650) while keeping the ABI free of exceptions.
+#include "common.cuh"
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+namespace attn {
+
+static thread_local std::string g_last_error;
+static std::atomic<uint64_t> g_launches{0};
+
+void set_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+void clear_error() { g_last_error.clear(); }
+void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s launch failed: %s", what, cudaGetErrorString(e));
+    return ATTN_ERR_CUDA;
+  }
+  return ATTN_OK;
+}
+
+static int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// implemented in the kernel translation units
+int attn_fwd_simt(const void*, const void*, const void*, void*, float*, int, int, int, int,
+                  const int64_t*, float, int, cudaStream_t);
+int attn_bwd_simt(const void*, const void*, const void*, const void*, const void*, const float*,
+                  void*, void*, void*, float*, int, int, int, int, const int64_t*, float, int,
+                  cudaStream_t);
+int gemm_simt(const void*, int64_t, int, const void*, int64_t, int, int, void*, int64_t, int,
+              const float*, int, int, int, int, cudaStream_t);
+int split_heads(const float*, float*, float*, float*, int, int, int, int, cudaStream_t);
+int merge_heads(const float*, float*, int, int, int, int, cudaStream_t);
+int cast_f32_bf16(const float*, void*, int64_t, cudaStream_t, int);
+size_t colsum_ws(int, int);
+int colsum(const void*, int, int64_t, int, int, float*, int, void*, cudaStream_t);
+int attn_probs_launch(const void*, const void*, const float*, float*, int, int, int, int, int64_t,
+                      int64_t, int64_t, float, int, cudaStream_t);
+size_t decode_ws(int, int, int, int);
+int decode(const void*, const void*, const void*, void*, float*, int, int, int, int, int64_t,
+           int64_t, int64_t, int64_t, int64_t, float, int, float*, cudaStream_t);
+bool tc_fwd_supported(int D, int dtype);
+int attn_fwd_tc(const void*, const void*, const void*, void*, float*, int, int, int, int,
+                const int64_t*, float, cudaStream_t);
+bool tc_bwd_supported(int D, int dtype);
+size_t attn_bwd_tc_ws(int B, int NH, int T, int D);
+int attn_bwd_tc(const void*, const void*, const void*, const void*, const void*, const float*,
+                void*, void*, void*, void*, int, int, int, int, const int64_t*, float,
+                cudaStream_t);
+bool tc_gemm_supported(int M, int N, int K, int64_t lda, int a_trans, int64_t ldb, int b_trans,
+                       const void* A, const void* B);
+int gemm_tc(const void*, int64_t, int, const void*, int64_t, int, void*, int64_t, int,
+            const float*, int, int, int, int, cudaStream_t);
+
+static size_t elem_size(int dtype) { return dtype == ATTN_F32 ? 4 : 2; }
+
+static int check_attn_args(const char* fn, int B, int NH, int T, int D, int dtype,
+                           const int64_t* st) {
+  ATTN_REQUIRE(dtype == ATTN_F32 || dtype == ATTN_BF16, "%s: dtype must be ATTN_F32 or ATTN_BF16", fn);
+  ATTN_REQUIRE(B > 0 && NH > 0 && T > 0 && D > 0, "%s: B, NH, T, D must be positive (got %d %d %d %d)",
+               fn, B, NH, T, D);
+  ATTN_REQUIRE(D % 4 == 0, "%s: head_dim %d must be a multiple of 4", fn, D);
+  for (int i = 0; i < 6; ++i)
+    ATTN_REQUIRE(st[i] >= 0 && st[i] % 4 == 0,
+                 "%s: strides must be non-negative multiples of 4 elements (stride %d = %lld)", fn, i,
+                 (long long)st[i]);
+  ATTN_REQUIRE(st[1] >= D && st[4] >= D, "%s: row strides must be >= head_dim", fn);
+  return ATTN_OK;
+}
+
+}  // namespace attn
+
+using namespace attn;
+
+extern "C" {
+
+int attn_version(void) { return 100; }
+
+const char* attn_last_error_string(void) { return g_last_error.c_str(); }
+
+uint64_t attn_launch_count(void) { return g_launches.load(); }
+
+int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int NH, int T,
+             int D, int64_t in_sb, int64_t in_st, int64_t in_sh, int64_t out_sb, int64_t out_st,
+             int64_t out_sh, float scale, int dtype, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(q && k && v && o && lse, "attn_fwd: null pointer argument");
+  const int64_t st[6] = {in_sb, in_st, in_sh, out_sb, out_st, out_sh};
+  if (int rc = check_attn_args("attn_fwd", B, NH, T, D, dtype, st)) return rc;
+  const size_t a = 4 * elem_size(dtype);
+  ATTN_REQUIRE(aligned(q, a) && aligned(k, a) && aligned(v, a) && aligned(o, a),
+               "attn_fwd: q/k/v/o must be %zu-byte aligned", a);
+  if (tc_fwd_supported(D, dtype))
+    return attn_fwd_tc(q, k, v, o, lse, B, NH, T, D, st, scale, as_stream(stream));
+  return attn_fwd_simt(q, k, v, o, lse, B, NH, T, D, st, scale, dtype, as_stream(stream));
+}
+
+size_t attn_bwd_workspace_size(int B, int NH, int T, int D, int dtype) {
+  if (B <= 0 || NH <= 0 || T <= 0 || D <= 0) return 0;
+  size_t ws = (size_t)B * NH * T * sizeof(float);  // delta = rowsum(dO * O)
+  if (tc_bwd_supported(D, dtype)) ws = attn_bwd_tc_ws(B, NH, T, D);
+  return ws;
+}
+
+int attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+             const float* lse, void* dq, void* dk, void* dv, void* workspace,
+             size_t workspace_bytes, int B, int NH, int T, int D, int64_t in_sb, int64_t in_st,
+             int64_t in_sh, int64_t out_sb, int64_t out_st, int64_t out_sh, float scale, int dtype,
+             void* stream) {
+  clear_error();
+  ATTN_REQUIRE(q && k && v && o && dout && lse && dq && dk && dv, "attn_bwd: null pointer argument");
+  const int64_t st[6] = {in_sb, in_st, in_sh, out_sb, out_st, out_sh};
+  if (int rc = check_attn_args("attn_bwd", B, NH, T, D, dtype, st)) return rc;
+  const size_t need = attn_bwd_workspace_size(B, NH, T, D, dtype);
+  if (!workspace || workspace_bytes < need) {
+    set_error("attn_bwd: workspace of %zu bytes required, %zu given", need,
+              workspace ? workspace_bytes : (size_t)0);
+    return ATTN_ERR_WORKSPACE;
+  }
+  ATTN_REQUIRE(aligned(workspace, 256), "attn_bwd: workspace must be 256-byte aligned");
+  const size_t a = 4 * elem_size(dtype);
+  ATTN_REQUIRE(aligned(q, a) && aligned(k, a) && aligned(v, a) && aligned(o, a) && aligned(dout, a) &&
+                   aligned(dq, a) && aligned(dk, a) && aligned(dv, a),
+               "attn_bwd: tensors must be %zu-byte aligned", a);
+  if (tc_bwd_supported(D, dtype))
+    return attn_bwd_tc(q, k, v, o, dout, lse, dq, dk, dv, workspace, B, NH, T, D, st, scale,
+                       as_stream(stream));
+  return attn_bwd_simt(q, k, v, o, dout, lse, dq, dk, dv, (float*)workspace, B, NH, T, D, st, scale,
+                       dtype, as_stream(stream));
+}
+
+int attn_probs(const void* q, const void* k, const float* lse, float* probs, int B, int NH, int T,
+               int D, int64_t in_sb, int64_t in_st, int64_t in_sh, float scale, int dtype,
+               void* stream) {
+  clear_error();
+  ATTN_REQUIRE(q && k && lse && probs, "attn_probs: null pointer argument");
+  ATTN_REQUIRE(dtype == ATTN_F32 || dtype == ATTN_BF16, "attn_probs: bad dtype");
+  ATTN_REQUIRE(B > 0 && NH > 0 && T > 0 && D > 0, "attn_probs: sizes must be positive");
+  ATTN_REQUIRE(in_sb >= 0 && in_st >= D && in_sh >= 0, "attn_probs: bad strides");
+  return attn_probs_launch(q, k, lse, probs, B, NH, T, D, in_sb, in_st, in_sh, scale, dtype,
+                           as_stream(stream));
+}
+
+size_t attn_decode_workspace_size(int B, int NH, int L, int D) {
+  if (B <= 0 || NH <= 0 || L <= 0 || D <= 0) return 0;
+  return decode_ws(B, NH, L, D);
+}
+
+int attn_decode(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse, int B,
+                int NH, int L, int D, int64_t q_sb, int64_t q_sh, int64_t kv_sb, int64_t kv_sl,
+                int64_t kv_sh, float scale, int dtype, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  clear_error();
+  ATTN_REQUIRE(q && k_cache && v_cache && o, "attn_decode: null pointer argument");
+  ATTN_REQUIRE(dtype == ATTN_F32 || dtype == ATTN_BF16, "attn_decode: bad dtype");
+  ATTN_REQUIRE(B > 0 && NH > 0 && L > 0 && D > 0, "attn_decode: sizes must be positive");
+  const int vec = 16 / (int)elem_size(dtype);
+  ATTN_REQUIRE(D % vec == 0, "attn_decode: head_dim must be a multiple of %d for this dtype", vec);
+  const int64_t st[5] = {q_sb, q_sh, kv_sb, kv_sl, kv_sh};
+  for (int i = 0; i < 5; ++i)
+    ATTN_REQUIRE(st[i] >= 0 && st[i] % vec == 0, "attn_decode: strides must be multiples of %d", vec);
+  ATTN_REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(o, 4),
+               "attn_decode: q/k/v must be 16-byte aligned");
+  const size_t need = decode_ws(B, NH, L, D);
+  if (!workspace || workspace_bytes < need) {
+    set_error("attn_decode: workspace of %zu bytes required", need);
+    return ATTN_ERR_WORKSPACE;
+  }
+  return decode(q, k_cache, v_cache, o, lse, B, NH, L, D, q_sb, q_sh, kv_sb, kv_sl, kv_sh, scale,
+                dtype, (float*)workspace, as_stream(stream));
+}
+
+int attn_gemm(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans,
+              int ab_dtype, void* C, int64_t ldc, int c_dtype, const float* bias, int M, int N, int K,
+              int accumulate, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(A && B && C, "attn_gemm: null pointer argument");
+  ATTN_REQUIRE(M > 0 && N > 0 && K > 0, "attn_gemm: M, N, K must be positive");
+  ATTN_REQUIRE(ab_dtype == ATTN_F32 || ab_dtype == ATTN_BF16, "attn_gemm: bad operand dtype");
+  ATTN_REQUIRE(c_dtype == ATTN_F32 || c_dtype == ATTN_BF16, "attn_gemm: bad output dtype");
+  ATTN_REQUIRE(!accumulate || c_dtype == ATTN_F32, "attn_gemm: accumulate requires a float32 C");
+  ATTN_REQUIRE(lda >= (a_trans ? M : K) && ldb >= (b_trans ? K : N) && ldc >= N,
+               "attn_gemm: leading dimensions too small");
+  if (ab_dtype == ATTN_BF16 && tc_gemm_supported(M, N, K, lda, a_trans, ldb, b_trans, A, B))
+    return gemm_tc(A, lda, a_trans, B, ldb, b_trans, C, ldc, c_dtype, bias, M, N, K, accumulate,
+                   as_stream(stream));
+  return gemm_simt(A, lda, a_trans, B, ldb, b_trans, ab_dtype, C, ldc, c_dtype, bias, M, N, K,
+                   accumulate, as_stream(stream));
+}
+
+size_t attn_colsum_workspace_size(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  return colsum_ws(M, N);
+}
+
+int attn_colsum(const void* X, int x_dtype, int64_t ldx, int M, int N, float* out, int accumulate,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(X && out, "attn_colsum: null pointer argument");
+  ATTN_REQUIRE(M > 0 && N > 0 && ldx >= N, "attn_colsum: bad shape");
+  ATTN_REQUIRE(x_dtype == ATTN_F32 || x_dtype == ATTN_BF16, "attn_colsum: bad dtype");
+  if (!workspace || workspace_bytes < colsum_ws(M, N)) {
+    set_error("attn_colsum: workspace of %zu bytes required", colsum_ws(M, N));
+    return ATTN_ERR_WORKSPACE;
+  }
+  return colsum(X, x_dtype, ldx, M, N, out, accumulate, workspace, as_stream(stream));
+}
+
+int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(x && y && n > 0, "attn_cast_f32_to_bf16: bad argument");
+  return cast_f32_bf16(x, y, n, as_stream(stream), sm_count());
+}
+
+int attn_split_heads(const float* qkv, float* q, float* k, float* v, int B, int T, int NH, int HD,
+                     void* stream) {
+  clear_error();
+  ATTN_REQUIRE(qkv && q && k && v, "attn_split_heads: null pointer argument");
+  ATTN_REQUIRE(B > 0 && T > 0 && NH > 0 && HD > 0, "attn_split_heads: sizes must be positive");
+  return split_heads(qkv, q, k, v, B, T, NH, HD, as_stream(stream));
+}
+
+int attn_merge_heads(const float* ctx_heads, float* ctx, int B, int T, int NH, int HD, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(ctx_heads && ctx, "attn_merge_heads: null pointer argument");
+  ATTN_REQUIRE(B > 0 && T > 0 && NH > 0 && HD > 0, "attn_merge_heads: sizes must be positive");
+  return merge_heads(ctx_heads, ctx, B, T, NH, HD, as_stream(stream));
+}
+
+}  // extern "C"

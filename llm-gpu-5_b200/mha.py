@@ -1,0 +1,385 @@
+"""Drop-in ``MultiHeadAttention`` for llm-gpu-5 (model/gpt.py:478-707), running on B200 kernels.
+
+Same constructor, same ``forward(gpu_input, B, T)`` / ``backward(gpu_dOut, B, T, accumulate)`` /
+``free_forward_caches()`` contract, same ``c_attn_w[C,3C]``, ``c_attn_b[3C]``, ``c_proj_w[C,C]``,
+``c_proj_b[C]`` parameters with ``gpu_weights``/``gpu_grads``/``gpu_m``/``gpu_v`` buffers, so
+TransformerBlock (model/gpt.py:742, :779, :825), GPTModel checkpoints (model/gpt.py:1136-1143) and
+the training loops keep working.  What changes is where the work runs:
+
+* forward: QKV projection, causal flash attention (row log-sum-exp instead of the T x T
+  probabilities), output projection: three library calls, no host round trip.  The reference's
+  split_heads/merge_heads copies are folded into the attention kernels' addressing (they read
+  Q/K/V straight out of the fused [B*T, 3C] projection and write the context in [B*T, C]).
+* backward: the whole of model/gpt.py:652-698 on the GPU (projection gradients, softmax VJP,
+  dQ/dK/dV, dX), gradients set or accumulated in place on the device.
+
+Precision: ``"fp32"`` reproduces the reference's float32 arithmetic on CUDA cores (the golden
+tolerance, 1e-5 relative); ``"bf16"`` runs the projections and attention on tcgen05 tensor cores
+with bf16 operands and fp32 accumulation/softmax statistics (2e-2 relative).
+
+Device memory comes from PyTorch's caching allocator; launches go to the current torch stream.
+Buffers returned by ``forward``/``backward`` are ``DeviceBuffer`` objects the caller frees, as in
+the reference (model/gpt.py:780-783, :819, :836-837).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from . import mha_ops as ops
+from .mha_ops import HeadView, ptr
+
+
+class GPTConfig:
+    """The attention-relevant subset of llm-gpu-5's GPTConfig (model/gpt.py:53-87), with the same
+    argument names and validation, plus ``attention_precision`` ("fp32" or "bf16")."""
+
+    def __init__(self, vocab_size: int, max_len: int = 8, embedding_dim: int = 16, num_heads: int = 2,
+                 num_layers: int = 1, dropout_prob: float = 0.1, max_seq_len: int = None,
+                 batch_size: int = None, attention_impl: str = None, use_flash_attention: bool = None,
+                 attention_precision: str = "fp32", **kwargs):
+        self.vocab_size = vocab_size
+        if max_seq_len is not None:
+            max_len = max_seq_len
+        self.max_len = max_len
+        self.embedding_dim = embedding_dim
+        self.num_heads = num_heads
+        self.num_layers = num_layers
+        self.dropout_prob = dropout_prob
+        self.head_dim = embedding_dim // num_heads
+        requested = kwargs.pop("attention_mode", None)
+        flash = kwargs.pop("flash_attention", None)
+        if use_flash_attention is None and flash is not None:
+            use_flash_attention = flash
+        if attention_impl is None:
+            if requested is not None:
+                attention_impl = requested
+            elif use_flash_attention is not None:
+                attention_impl = "strided" if use_flash_attention else "identity"
+            else:
+                attention_impl = "identity"
+        self.attention_impl = str(attention_impl).strip().lower()
+        if self.attention_impl not in {"identity", "strided"}:
+            raise ValueError(f"Unsupported attention_impl: {attention_impl}")
+        self.use_flash_attention = self.attention_impl == "strided"
+        if attention_precision not in ("fp32", "bf16"):
+            raise ValueError(f"attention_precision must be 'fp32' or 'bf16', got {attention_precision!r}")
+        self.attention_precision = attention_precision
+        assert self.embedding_dim % self.num_heads == 0, "embedding_dim must be divisible by num_heads"
+
+
+class DeviceBuffer:
+    """A device allocation handed to the caller: ``int(buf)`` is its address, ``free()`` releases
+    it (the PyCUDA ``DeviceAllocation`` surface the reference's callers use)."""
+
+    __slots__ = ("tensor",)
+
+    def __init__(self, tensor: torch.Tensor):
+        self.tensor = tensor
+
+    def __int__(self):
+        return self.tensor.data_ptr()
+
+    def data_ptr(self):
+        return self.tensor.data_ptr()
+
+    @property
+    def nbytes(self):
+        return self.tensor.numel() * self.tensor.element_size()
+
+    def free(self):
+        self.tensor = None
+
+    def get(self):
+        return self.tensor.detach().cpu().numpy()
+
+
+def _as_tensor(x, numel: int, dtype=torch.float32) -> torch.Tensor:
+    """View any device pointer-like object as a flat CUDA tensor of ``numel`` elements."""
+    if isinstance(x, torch.Tensor):
+        assert x.is_cuda and x.dtype == dtype and x.is_contiguous() and x.numel() >= numel
+        return x.reshape(-1)[:numel]
+    if isinstance(x, DeviceBuffer):
+        return _as_tensor(x.tensor, numel, dtype)
+    addr = int(x)
+
+    class _Iface:  # expose a raw address to torch without copying
+        __cuda_array_interface__ = {
+            "shape": (numel,), "typestr": "<f4" if dtype == torch.float32 else "<u2",
+            "data": (addr, False), "version": 3}
+    return torch.as_tensor(_Iface(), device="cuda")
+
+
+class Parameter:
+    """Weights plus gradient and AdamW moment buffers in device memory (model/gpt.py:101-154).
+
+    Initialised exactly as the reference: ``np.random.normal(0, init_scale, shape)`` from NumPy's
+    global generator, so seeded runs reproduce the reference's weights.  ``grad_storage`` lets a
+    module place the gradient inside one flat buffer (for a single all-reduce).
+    """
+
+    def __init__(self, shape: tuple = None, init_scale: float = 0.02, dtype=None, grad_storage=None):
+        self.shape = tuple(shape)
+        self.dtype = dtype if dtype is not None else np.float32
+        self.total_elements = int(np.prod(shape))
+        self.bytes_size = self.total_elements * 4
+        host_w = np.random.normal(0.0, init_scale, size=shape).astype(np.float32)
+        self.weights = torch.from_numpy(host_w).to("cuda")
+        self.grads = grad_storage if grad_storage is not None else torch.zeros(
+            self.shape, dtype=torch.float32, device="cuda")
+        self.grads.zero_()
+        self.m = torch.zeros(self.shape, dtype=torch.float32, device="cuda")
+        self.v = torch.zeros(self.shape, dtype=torch.float32, device="cuda")
+
+    # PyCUDA-style handles (``int()`` gives the device address)
+    @property
+    def gpu_weights(self):
+        return DeviceBuffer(self.weights)
+
+    @property
+    def gpu_grads(self):
+        return DeviceBuffer(self.grads)
+
+    @property
+    def gpu_m(self):
+        return DeviceBuffer(self.m)
+
+    @property
+    def gpu_v(self):
+        return DeviceBuffer(self.v)
+
+    def free(self):
+        self.weights = self.grads = self.m = self.v = None
+
+    def set_or_accumulate_grads(self, host_grads, accumulate=False):
+        g = torch.from_numpy(np.ascontiguousarray(host_grads, dtype=np.float32)).to("cuda").view(self.shape)
+        if accumulate:
+            self.grads.add_(g)
+        else:
+            self.grads.copy_(g)
+
+    def set_or_accumulate_grads_from_gpu(self, gpu_grads_ptr, accumulate=False):
+        g = _as_tensor(gpu_grads_ptr, self.total_elements).view(self.shape)
+        if accumulate:
+            self.grads.add_(g)
+        else:
+            self.grads.copy_(g)
+
+
+class _NullRange:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NULL = _NullRange()
+
+
+class MultiHeadAttention:
+    """Multi-head causal self-attention with the reference's API (model/gpt.py:478-707)."""
+
+    def __init__(self, config_or_embedding_dim=None, num_heads: int = None, precision: str = None):
+        if isinstance(config_or_embedding_dim, GPTConfig):
+            config = config_or_embedding_dim
+        elif config_or_embedding_dim is not None:
+            config = GPTConfig(vocab_size=50, embedding_dim=config_or_embedding_dim,
+                               num_heads=num_heads or 2, max_len=8)
+        else:
+            raise ValueError("MultiHeadAttention requires either GPTConfig or embedding_dim parameter")
+        self.config = config
+        C = config.embedding_dim
+        self.precision = precision or getattr(config, "attention_precision", "fp32")
+        if self.precision not in ("fp32", "bf16"):
+            raise ValueError(f"precision must be 'fp32' or 'bf16', got {self.precision!r}")
+
+        # one flat fp32 gradient buffer [dWqkv | dbqkv | dWo | dbo] so data-parallel training
+        # all-reduces the four gradients with a single collective
+        sizes = [C * 3 * C, 3 * C, C * C, C]
+        self.flat_grads = torch.zeros(sum(sizes), dtype=torch.float32, device="cuda")
+        views, off = [], 0
+        for n in sizes:
+            views.append(self.flat_grads[off:off + n])
+            off += n
+        # same parameter order and init as model/gpt.py:507-510
+        self.c_attn_w = Parameter((C, C * 3), grad_storage=views[0].view(C, 3 * C))
+        self.c_attn_b = Parameter((C * 3,), init_scale=0.0, grad_storage=views[1])
+        self.c_proj_w = Parameter((C, C), grad_storage=views[2].view(C, C))
+        self.c_proj_b = Parameter((C,), init_scale=0.0, grad_storage=views[3])
+
+        self.profiler = None  # optional: object with .range(name) -> context manager (CUDA events)
+        self.grad_sync_group = None  # a torch.distributed group: backward all-reduces (SUM) into it
+        self._grad_sync_work = None
+        self.training = True
+        self._cache = None
+
+    # ---------------------------------------------------------------- helpers
+    def _rng(self, name):
+        return self.profiler.range(name) if self.profiler is not None else _NULL
+
+    @property
+    def _dt(self):
+        return torch.bfloat16 if self.precision == "bf16" else torch.float32
+
+    def _shape(self):
+        C = self.config.embedding_dim
+        NH = self.config.num_heads
+        return C, NH, C // NH
+
+    # ---------------------------------------------------------------- forward
+    def forward(self, gpu_input, B: int, T: int):
+        """x [B*T, C] float32 (device) -> DeviceBuffer [B*T, C] float32 (caller frees)."""
+        C, NH, D = self._shape()
+        M = B * T
+        dt = self._dt
+        self._cache = None
+        x = _as_tensor(gpu_input, M * C)
+        if dt == torch.bfloat16:
+            with self._rng("cast"):
+                x_op = ops.cast_bf16(x)
+                w_qkv = ops.cast_bf16(self.c_attn_w.weights)
+                w_o = ops.cast_bf16(self.c_proj_w.weights)
+        else:
+            x_op = x.clone()  # the caller may overwrite its input (residual adds are in place)
+            w_qkv, w_o = self.c_attn_w.weights, self.c_proj_w.weights
+        qkv = torch.empty((M, 3 * C), dtype=dt, device="cuda")
+        with self._rng("gemm_qkv"):
+            ops.gemm(x_op.data_ptr(), C, False, w_qkv.data_ptr(), 3 * C, False, dt, qkv.data_ptr(),
+                     3 * C, dt, M, 3 * C, C, bias=self.c_attn_b.weights.data_ptr())
+        ctx = torch.empty((M, C), dtype=dt, device="cuda")
+        lse = torch.empty((B, NH, T), dtype=torch.float32, device="cuda")
+        es = qkv.element_size()
+        base = qkv.data_ptr()
+        qv = HeadView.tokens(base, T, 3 * C, D)
+        kv = HeadView.tokens(base + C * es, T, 3 * C, D)
+        vv = HeadView.tokens(base + 2 * C * es, T, 3 * C, D)
+        ov = HeadView.tokens(ctx.data_ptr(), T, C, D)
+        scale = 1.0 / math.sqrt(D)
+        with self._rng("attn_fwd"):
+            ops.attention_forward(qv, kv, vv, ov, lse, B, NH, T, D, scale, dt)
+        out = torch.empty((M, C), dtype=torch.float32, device="cuda")
+        with self._rng("gemm_out"):
+            ops.gemm(ctx.data_ptr(), C, False, w_o.data_ptr(), C, False, dt, out.data_ptr(), C,
+                     torch.float32, M, C, C, bias=self.c_proj_b.weights.data_ptr())
+        if getattr(self, "training", True):
+            self._cache = dict(B=B, T=T, x=x_op, qkv=qkv, ctx=ctx, lse=lse, w_qkv=w_qkv, w_o=w_o)
+        return DeviceBuffer(out)
+
+    # ---------------------------------------------------------------- backward
+    def backward(self, gpu_dOut, B: int, T: int, accumulate=False):
+        """dY [B*T, C] float32 -> dX DeviceBuffer [B*T, C]; parameter grads set or accumulated."""
+        c = self._cache
+        if c is None or c["B"] != B or c["T"] != T:
+            raise RuntimeError("MultiHeadAttention.backward() called without forward caches")
+        C, NH, D = self._shape()
+        M = B * T
+        dt = self._dt
+        dy = _as_tensor(gpu_dOut, M * C)
+        with self._rng("cast"):
+            dy_op = ops.cast_bf16(dy) if dt == torch.bfloat16 else dy
+        # output projection: dWo = ctx^T dY, dbo = sum(dY), dCtx = dY Wo^T   (gpt.py:666-670)
+        with self._rng("gemm_dwo"):
+            ops.gemm(c["ctx"].data_ptr(), C, True, dy_op.data_ptr(), C, False, dt,
+                     self.c_proj_w.grads.data_ptr(), C, torch.float32, C, C, M, accumulate=accumulate)
+        with self._rng("colsum"):
+            ops.colsum(dy.data_ptr(), torch.float32, C, M, C, self.c_proj_b.grads, accumulate=accumulate)
+        dctx = torch.empty((M, C), dtype=dt, device="cuda")
+        with self._rng("gemm_dctx"):
+            ops.gemm(dy_op.data_ptr(), C, False, c["w_o"].data_ptr(), C, True, dt, dctx.data_ptr(), C,
+                     dt, M, C, C)
+        # attention: softmax VJP + dQ/dK/dV written straight into the [B*T, 3C] layout (gpt.py:672-685)
+        dqkv = torch.empty((M, 3 * C), dtype=dt, device="cuda")
+        es = dqkv.element_size()
+        qb, gb = c["qkv"].data_ptr(), dqkv.data_ptr()
+        tv = lambda base: HeadView.tokens(base, T, 3 * C, D)  # noqa: E731
+        ov = HeadView.tokens(c["ctx"].data_ptr(), T, C, D)
+        dov = HeadView.tokens(dctx.data_ptr(), T, C, D)
+        with self._rng("attn_bwd"):
+            ops.attention_backward(tv(qb), tv(qb + C * es), tv(qb + 2 * C * es), ov, dov, c["lse"],
+                                   tv(gb), tv(gb + C * es), tv(gb + 2 * C * es), B, NH, T, D,
+                                   1.0 / math.sqrt(D), dt)
+        # input projection: dWqkv = x^T dQKV, dbqkv = sum(dQKV), dX = dQKV Wqkv^T  (gpt.py:687-689)
+        with self._rng("gemm_dwqkv"):
+            ops.gemm(c["x"].data_ptr(), C, True, gb, 3 * C, False, dt, self.c_attn_w.grads.data_ptr(),
+                     3 * C, torch.float32, C, 3 * C, M, accumulate=accumulate)
+        with self._rng("colsum"):
+            ops.colsum(gb, dt, 3 * C, M, 3 * C, self.c_attn_b.grads, accumulate=accumulate)
+        if self.grad_sync_group is not None:
+            import torch.distributed as dist
+            # overlaps the dX GEMM below on NCCL's stream
+            self._grad_sync_work = dist.all_reduce(self.flat_grads, op=dist.ReduceOp.SUM,
+                                                   group=self.grad_sync_group, async_op=True)
+        dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
+        with self._rng("gemm_dx"):
+            ops.gemm(gb, 3 * C, False, c["w_qkv"].data_ptr(), 3 * C, True, dt, dx.data_ptr(), C,
+                     torch.float32, M, C, 3 * C)
+        return DeviceBuffer(dx)
+
+    def wait_grad_sync(self):
+        """Wait for the gradient all-reduce launched by the last backward (if any)."""
+        if self._grad_sync_work is not None:
+            self._grad_sync_work.wait()
+            self._grad_sync_work = None
+
+    def free_forward_caches(self):
+        """Release the forward caches (model/gpt.py:700-707)."""
+        self._cache = None
+
+    # ---------------------------------------------------------------- reference cache views
+    # The reference keeps host copies of its caches (model/gpt.py:603-619) and its parity test
+    # reads them (test_mha_integration_parity.py:88-93).  Here the caches stay on the device;
+    # these properties download them in the reference's shapes on demand (debug/test only).
+    def _qkv_heads(self, which):
+        c = self._cache
+        if c is None:
+            return None
+        C, NH, D = self._shape()
+        B, T = c["B"], c["T"]
+        t = c["qkv"].view(B, T, 3, NH, D)[:, :, which].permute(0, 2, 1, 3)
+        return t.float().contiguous().cpu().numpy()
+
+    @property
+    def cache_q(self):
+        return self._qkv_heads(0)
+
+    @property
+    def cache_k(self):
+        return self._qkv_heads(1)
+
+    @property
+    def cache_v(self):
+        return self._qkv_heads(2)
+
+    @property
+    def cache_context(self):
+        c = self._cache
+        return None if c is None else c["ctx"].float().cpu().numpy()
+
+    @property
+    def cache_input(self):
+        c = self._cache
+        return None if c is None else c["x"].float().cpu().numpy()
+
+    @property
+    def cache_lse(self):
+        c = self._cache
+        return None if c is None else c["lse"].cpu().numpy()
+
+    @property
+    def cache_attn_weights(self):
+        """[B, NH, T, T] probabilities rebuilt on the GPU from lse (never stored by forward)."""
+        c = self._cache
+        if c is None:
+            return None
+        C, NH, D = self._shape()
+        B, T = c["B"], c["T"]
+        es = c["qkv"].element_size()
+        base = c["qkv"].data_ptr()
+        p = ops.attention_probs(HeadView.tokens(base, T, 3 * C, D),
+                                HeadView.tokens(base + C * es, T, 3 * C, D), c["lse"], B, NH, T, D,
+                                1.0 / math.sqrt(D), self._dt)
+        return p.cpu().numpy()

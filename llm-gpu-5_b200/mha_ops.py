@@ -1,0 +1,188 @@
+"""Launch wrappers over the C ABI, in the role core/mha_ops.py plays for the reference.
+
+Each wrapper takes torch CUDA tensors (or raw device addresses), checks shapes on the host,
+and launches on the current torch stream.  All compute is in libattn_b200.so.
+
+The reference's launch constants (core/mha_ops.py:22-23) are kept for callers that read them;
+the kernels here choose their own tiling.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._lib import ATTN_BF16, ATTN_F32, call, lib
+
+THREADS_PER_BLOCK = 256
+SOFTMAX_BLOCK_THREADS = 64
+
+_DT = {torch.float32: ATTN_F32, torch.bfloat16: ATTN_BF16}
+
+
+def dtype_code(t: torch.dtype) -> int:
+    try:
+        return _DT[t]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t}; expected float32 or bfloat16") from None
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def ptr(x) -> int:
+    """Device address of a torch tensor, a DeviceBuffer, a pycuda DeviceAllocation or an int."""
+    if isinstance(x, torch.Tensor):
+        if not x.is_cuda:
+            raise TypeError("expected a CUDA tensor")
+        return x.data_ptr()
+    if hasattr(x, "data_ptr"):
+        return int(x.data_ptr())
+    return int(x)
+
+
+class HeadView:
+    """Element strides of an attention operand: element (b, t, h, d) at base[b*sb + t*st + h*sh + d]."""
+
+    __slots__ = ("base", "sb", "st", "sh")
+
+    def __init__(self, base: int, sb: int, st: int, sh: int):
+        self.base, self.sb, self.st, self.sh = int(base), int(sb), int(st), int(sh)
+
+    @staticmethod
+    def tokens(base: int, T: int, ld: int, D: int) -> "HeadView":
+        """Token layout [B*T, ld] with head h at column offset h*D (the fused projection layout)."""
+        return HeadView(base, T * ld, ld, D)
+
+    @staticmethod
+    def heads(base: int, NH: int, T: int, D: int) -> "HeadView":
+        """The reference's split layout [B*NH, T, D] (split_heads_kernel output)."""
+        return HeadView(base, NH * T * D, D, T * D)
+
+
+def attention_forward(q: HeadView, k: HeadView, v: HeadView, o: HeadView, lse: torch.Tensor,
+                      B: int, NH: int, T: int, D: int, scale: float, dtype: torch.dtype):
+    """Causal attention forward; q/k/v share strides.  lse: float32 [B, NH, T]."""
+    assert (k.sb, k.st, k.sh) == (q.sb, q.st, q.sh) == (v.sb, v.st, v.sh)
+    assert lse.dtype == torch.float32 and lse.numel() >= B * NH * T
+    call("attn_fwd", q.base, k.base, v.base, o.base, lse.data_ptr(), B, NH, T, D,
+         q.sb, q.st, q.sh, o.sb, o.st, o.sh, float(scale), dtype_code(dtype), _stream())
+
+
+def attention_backward(q: HeadView, k: HeadView, v: HeadView, o: HeadView, do: HeadView,
+                       lse: torch.Tensor, dq: HeadView, dk: HeadView, dv: HeadView,
+                       B: int, NH: int, T: int, D: int, scale: float, dtype: torch.dtype,
+                       workspace: torch.Tensor | None = None):
+    """Causal attention backward.  dq/dk/dv use q's strides, do uses o's."""
+    assert (dq.sb, dq.st, dq.sh) == (q.sb, q.st, q.sh) == (dk.sb, dk.st, dk.sh) == (dv.sb, dv.st, dv.sh)
+    assert (do.sb, do.st, do.sh) == (o.sb, o.st, o.sh)
+    code = dtype_code(dtype)
+    need = lib.attn_bwd_workspace_size(B, NH, T, D, code)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device="cuda")
+    call("attn_bwd", q.base, k.base, v.base, o.base, do.base, lse.data_ptr(), dq.base, dk.base,
+         dv.base, workspace.data_ptr(), workspace.numel() * workspace.element_size(), B, NH, T, D,
+         q.sb, q.st, q.sh, o.sb, o.st, o.sh, float(scale), code, _stream())
+
+
+def attention_probs(q: HeadView, k: HeadView, lse: torch.Tensor, B, NH, T, D, scale, dtype):
+    """Rebuild the [B, NH, T, T] probabilities from lse (debug/test accessor)."""
+    out = torch.empty((B, NH, T, T), dtype=torch.float32, device="cuda")
+    call("attn_probs", q.base, k.base, lse.data_ptr(), out.data_ptr(), B, NH, T, D, q.sb, q.st, q.sh,
+         float(scale), dtype_code(dtype), _stream())
+    return out
+
+
+def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, scale: float | None = None,
+           out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
+           workspace: torch.Tensor | None = None):
+    """Single-query decode: q [B, NH, D], caches [B, L, NH, D] (token layout) -> out [B, NH, D]."""
+    B, NH, D = q.shape
+    L = k_cache.shape[1]
+    assert k_cache.shape == v_cache.shape == (B, L, NH, D)
+    assert q.dtype == k_cache.dtype == v_cache.dtype
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    need = lib.attn_decode_workspace_size(B, NH, L, D)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    qs = q.stride()
+    ks = k_cache.stride()
+    assert k_cache.stride() == v_cache.stride() and ks[3] == 1 and qs[2] == 1
+    call("attn_decode", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+         lse.data_ptr() if lse is not None else None, B, NH, L, D, qs[0], qs[1], ks[0], ks[1], ks[2],
+         float(scale), dtype_code(q.dtype), workspace.data_ptr(),
+         workspace.numel() * workspace.element_size(), _stream())
+    return out
+
+
+def gemm(A: int, lda: int, a_trans: bool, B: int, ldb: int, b_trans: bool, ab_dtype: torch.dtype,
+         C: int, ldc: int, c_dtype: torch.dtype, M: int, N: int, K: int, bias: int | None = None,
+         accumulate: bool = False):
+    """C[M,N] (=|+=) op(A) op(B) (+bias) on raw device addresses (see include/attn_b200.h)."""
+    call("attn_gemm", A, lda, int(a_trans), B, ldb, int(b_trans), dtype_code(ab_dtype), C, ldc,
+         dtype_code(c_dtype), bias, M, N, K, int(accumulate), _stream())
+
+
+def colsum(X: int, x_dtype: torch.dtype, ldx: int, M: int, N: int, out: torch.Tensor,
+           accumulate: bool = False, workspace: torch.Tensor | None = None):
+    need = lib.attn_colsum_workspace_size(M, N)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device="cuda")
+    call("attn_colsum", X, dtype_code(x_dtype), ldx, M, N, out.data_ptr(), int(accumulate),
+         workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
+
+
+def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    assert x.dtype == torch.float32 and x.is_contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    call("attn_cast_f32_to_bf16", x.data_ptr(), out.data_ptr(), x.numel(), _stream())
+    return out
+
+
+def split_heads(qkv: int, q: int, k: int, v: int, B: int, T: int, NH: int, HD: int):
+    """split_heads_kernel (core/mha_kernels.py:534-558) on float32 device buffers."""
+    call("attn_split_heads", qkv, q, k, v, B, T, NH, HD, _stream())
+
+
+def merge_heads(ctx_heads: int, ctx: int, B: int, T: int, NH: int, HD: int):
+    """merge_heads_kernel (core/mha_kernels.py:567-584) on float32 device buffers."""
+    call("attn_merge_heads", ctx_heads, ctx, B, T, NH, HD, _stream())
+
+
+class _Kernel:
+    """A named kernel handle shaped like the reference's PyCUDA functions (positional args)."""
+
+    def __init__(self, name, fn):
+        self.__name__ = name
+        self._fn = fn
+
+    def __call__(self, *args, block=None, grid=None, shared=None, stream=None):
+        return self._fn(*[ptr(a) if not isinstance(a, (int, float)) else a for a in args])
+
+
+class _SharedModule:
+    """Stand-in for the compiled PyCUDA module of get_shared_mha_module (core/mha_ops.py:39-48):
+    the layout adapters are exposed by the reference's kernel names."""
+
+    def get_function(self, name):
+        if name == "split_heads_kernel":
+            return _Kernel(name, lambda qkv, q, k, v, B, T, NH, HD: split_heads(
+                qkv, q, k, v, int(B), int(T), int(NH), int(HD)))
+        if name == "merge_heads_kernel":
+            return _Kernel(name, lambda ch, c, B, T, NH, HD: merge_heads(
+                ch, c, int(B), int(T), int(NH), int(HD)))
+        raise KeyError(f"{name}: the B200 library replaces this kernel; use MultiHeadAttention or "
+                       "the attention_* wrappers")
+
+
+_SHARED = _SharedModule()
+
+
+def get_shared_mha_module():
+    return _SHARED

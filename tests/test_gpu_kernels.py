@@ -1,0 +1,244 @@
+"""GPU parity of the attention kernels against the oracle, through the C ABI.
+
+Tolerances (max|Δ|/max|ref| per tensor, ``rel_err``): float32 path 1e-5; bf16 tensor-core path
+2e-2, with the oracle evaluated on the same bf16-rounded inputs.  The reference's own
+assert_allclose tolerance (rtol=1e-4, atol=1e-5, test_mha_golden_model.py:45) is also applied to
+the float32 path on its golden fixture.
+"""
+import math
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from oracle import mha_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-5
+BF16_TOL = 2e-2
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dev(a, dtype=None):
+    torch = _torch()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.to(dtype) if dtype is not None else t
+
+
+def _bf16_round(a):
+    torch = _torch()
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def _run_attention(pkg, q, k, v, do, dtype, layout):
+    """q/k/v/do: float arrays [B, NH, T, D].  Returns (o, lse, dq, dk, dv) as float64 arrays."""
+    torch = _torch()
+    ops = pkg.mha_ops
+    B, NH, T, D = q.shape
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    if layout == "heads":
+        def put(a):
+            return _dev(a.astype(np.float32), tdt).contiguous()
+
+        def view(t):
+            return ops.HeadView.heads(t.data_ptr(), NH, T, D)
+
+        def get(t):
+            return t.float().cpu().numpy().reshape(B, NH, T, D)
+        tq, tk, tv, tdo = put(q), put(k), put(v), put(do)
+        to, tdq, tdk, tdv = (torch.empty_like(tq) for _ in range(4))
+        qv, kv, vv, ov, dov = view(tq), view(tk), view(tv), view(to), view(tdo)
+        dqv, dkv, dvv = view(tdq), view(tdk), view(tdv)
+    else:  # token layout of the fused projection: one [B*T, 3C] buffer, context [B*T, C]
+        C = NH * D
+        qkv = np.concatenate([a.transpose(0, 2, 1, 3).reshape(B * T, C) for a in (q, k, v)], axis=1)
+        tqkv = _dev(qkv.astype(np.float32), tdt).contiguous()
+        tdo = _dev(do.transpose(0, 2, 1, 3).reshape(B * T, C).astype(np.float32), tdt).contiguous()
+        to = torch.empty((B * T, C), dtype=tdt, device="cuda")
+        tg = torch.empty((B * T, 3 * C), dtype=tdt, device="cuda")
+        es = tqkv.element_size()
+        tokv = lambda base: ops.HeadView.tokens(base, T, 3 * C, D)  # noqa: E731
+        qv, kv, vv = (tokv(tqkv.data_ptr() + i * C * es) for i in range(3))
+        dqv, dkv, dvv = (tokv(tg.data_ptr() + i * C * es) for i in range(3))
+        ov = ops.HeadView.tokens(to.data_ptr(), T, C, D)
+        dov = ops.HeadView.tokens(tdo.data_ptr(), T, C, D)
+
+        def get_g(i):
+            return tg[:, i * C:(i + 1) * C].float().cpu().numpy().reshape(B, T, NH, D).transpose(0, 2, 1, 3)
+    lse = torch.empty((B, NH, T), dtype=torch.float32, device="cuda")
+    scale = 1.0 / math.sqrt(D)
+    ops.attention_forward(qv, kv, vv, ov, lse, B, NH, T, D, scale, tdt)
+    ops.attention_backward(qv, kv, vv, ov, dov, lse, dqv, dkv, dvv, B, NH, T, D, scale, tdt)
+    torch.cuda.synchronize()
+    if layout == "heads":
+        res = (get(to), lse.cpu().numpy(), get(tdq), get(tdk), get(tdv))
+    else:
+        o = to.float().cpu().numpy().reshape(B, T, NH, D).transpose(0, 2, 1, 3)
+        res = (o, lse.cpu().numpy(), get_g(0), get_g(1), get_g(2))
+    return [np.asarray(r, dtype=np.float64) for r in res]
+
+
+def _oracle(q, k, v, do):
+    D = q.shape[-1]
+    scale = 1.0 / math.sqrt(D)
+    o, lse, p = O.causal_attention_forward(q, k, v, scale)
+    dq, dk, dv, _ = O.causal_attention_backward(p, q, k, v, do, scale, apply_scale=True)
+    return o, lse, dq, dk, dv
+
+
+def _inputs(B, NH, T, D, seed):
+    rng = np.random.default_rng(seed)
+    return [rng.standard_normal((B, NH, T, D)).astype(np.float32) for _ in range(4)]
+
+
+@pytest.mark.parametrize("B,NH,T,D", [(1, 3, 17, 8), (2, 2, 5, 4), (2, 4, 128, 16), (1, 2, 130, 32),
+                                      (1, 2, 200, 64), (1, 1, 97, 128), (2, 8, 128, 32)])
+@pytest.mark.parametrize("layout", ["heads", "tokens"])
+def test_attention_f32_matches_oracle(pkg, cuda_dev, B, NH, T, D, layout):
+    q, k, v, do = _inputs(B, NH, T, D, seed=B * 1000 + T * 10 + D)
+    got = _run_attention(pkg, q, k, v, do, "f32", layout)
+    ref = _oracle(q, k, v, do)
+    for name, g, r in zip(("o", "lse", "dq", "dk", "dv"), got, ref):
+        assert O.rel_err(g, r) < F32_TOL, (name, O.rel_err(g, r))
+
+
+@pytest.mark.parametrize("B,NH,T,D", [(1, 2, 256, 64), (2, 2, 200, 64), (1, 2, 384, 64), (1, 2, 77, 32),
+                                      (2, 3, 130, 16), (1, 2, 1024, 64), (1, 1, 129, 128)])
+@pytest.mark.parametrize("layout", ["heads", "tokens"])
+def test_attention_bf16_matches_oracle(pkg, cuda_dev, B, NH, T, D, layout):
+    q, k, v, do = (_bf16_round(a) for a in _inputs(B, NH, T, D, seed=7 + T + D))
+    got = _run_attention(pkg, q, k, v, do, "bf16", layout)
+    ref = _oracle(q, k, v, do)
+    for name, g, r in zip(("o", "lse", "dq", "dk", "dv"), got, ref):
+        assert O.rel_err(g, r) < BF16_TOL, (name, O.rel_err(g, r))
+
+
+def test_kernel_golden_fixture(pkg, cuda_dev):
+    """The reference's Layer-1 golden case (seed 1337, H=3, M=17, D=8) through the fp32 kernels."""
+    torch = _torch()
+    g = np.load(os.path.join(GOLDEN, "kernel_h3_m17_d8.npz"))
+    H, M, D = int(g["H"]), int(g["M"]), int(g["D"])
+    scale = float(g["scale"])
+    q, k, v, do = (g[n][None] for n in ("Q", "K", "V", "dOut"))
+    o, lse, dq, dk, dv = _run_attention(pkg, q, k, v, do, "f32", "heads")
+    tol = dict(rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(o[0], g["out"], **tol)
+    # golden dQ/dK leave the scale out of dS (test_mha_golden_model.py:75-91); the kernels apply it
+    np.testing.assert_allclose(dq[0] / scale, g["dQ"], **tol)
+    np.testing.assert_allclose(dk[0] / scale, g["dK"], **tol)
+    np.testing.assert_allclose(dv[0], g["dV"], **tol)
+    # probabilities rebuilt from lse match the reference's cache_attn_weights semantics
+    ops = pkg.mha_ops
+    tq = _dev(g["Q"]).contiguous()
+    tk = _dev(g["K"]).contiguous()
+    tl = _dev(lse.astype(np.float32)).contiguous()
+    p = ops.attention_probs(ops.HeadView.heads(tq.data_ptr(), H, M, D),
+                            ops.HeadView.heads(tk.data_ptr(), H, M, D), tl, 1, H, M, D, scale,
+                            torch.float32)
+    np.testing.assert_allclose(p.cpu().numpy()[0], g["probs"], **tol)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("B,NH,L,D", [(2, 3, 37, 16), (4, 8, 2048, 64), (1, 2, 300, 128), (3, 2, 1, 32)])
+def test_decode_matches_oracle(pkg, cuda_dev, dtype, B, NH, L, D):
+    torch = _torch()
+    if dtype == "bf16" and D < 8:
+        pytest.skip("bf16 decode needs head_dim % 8 == 0")
+    rng = np.random.default_rng(L + D)
+    q = rng.standard_normal((B, NH, D)).astype(np.float32)
+    kc = rng.standard_normal((B, L, NH, D)).astype(np.float32)
+    vc = rng.standard_normal((B, L, NH, D)).astype(np.float32)
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    if dtype == "bf16":
+        q, kc, vc = _bf16_round(q), _bf16_round(kc), _bf16_round(vc)
+    tq, tk, tv = _dev(q, tdt), _dev(kc, tdt), _dev(vc, tdt)
+    lse = torch.empty((B, NH), dtype=torch.float32, device="cuda")
+    out = pkg.mha_ops.decode(tq, tk, tv, lse=lse)
+    torch.cuda.synchronize()
+    ref_o, ref_l = O.decode_attention(q, kc.transpose(0, 2, 1, 3), vc.transpose(0, 2, 1, 3), 1.0 / math.sqrt(D))
+    tol = F32_TOL if dtype == "f32" else BF16_TOL
+    assert O.rel_err(out.float().cpu().numpy(), ref_o) < tol
+    assert O.rel_err(lse.cpu().numpy(), ref_l) < tol
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("M,N,K,at,bt", [(100, 72, 40, 0, 0), (256, 768, 256, 0, 0), (64, 96, 300, 1, 0),
+                                         (130, 64, 96, 0, 1), (384, 256, 128, 1, 1), (1024, 2304, 768, 0, 0),
+                                         (768, 2304, 4096, 1, 0), (4096, 768, 2304, 0, 1), (512, 512, 8192, 1, 0)])
+def test_gemm_matches_numpy(pkg, cuda_dev, dtype, M, N, K, at, bt):
+    torch = _torch()
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((K, M) if at else (M, K)).astype(np.float32)
+    Bm = rng.standard_normal((N, K) if bt else (K, N)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    if dtype == "bf16":
+        A, Bm = _bf16_round(A), _bf16_round(Bm)
+    tA, tB, tbias = _dev(A, tdt), _dev(Bm, tdt), _dev(bias)
+    ref = (A.T if at else A).astype(np.float64) @ (Bm.T if bt else Bm).astype(np.float64)
+    for acc in (False, True):
+        tC = _dev(C0.copy())
+        pkg.mha_ops.gemm(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, tdt,
+                         tC.data_ptr(), N, torch.float32, M, N, K, bias=tbias.data_ptr(), accumulate=acc)
+        torch.cuda.synchronize()
+        want = ref + bias + (C0 if acc else 0)
+        tol = F32_TOL if dtype == "f32" else 1e-3  # bf16 operands are exact; fp32 accumulation
+        assert O.rel_err(tC.cpu().numpy(), want) < tol, (acc, O.rel_err(tC.cpu().numpy(), want))
+    # bf16 output
+    tCb = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    pkg.mha_ops.gemm(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, tdt, tCb.data_ptr(), N,
+                     torch.bfloat16, M, N, K)
+    torch.cuda.synchronize()
+    assert O.rel_err(tCb.float().cpu().numpy(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N", [(1, 5), (1000, 33), (262144, 96), (4097, 2304)])
+def test_colsum_and_cast(pkg, cuda_dev, M, N):
+    torch = _torch()
+    rng = np.random.default_rng(M + N)
+    X = rng.standard_normal((M, N)).astype(np.float32)
+    tX = _dev(X)
+    out = torch.full((N,), 3.0, dtype=torch.float32, device="cuda")
+    pkg.mha_ops.colsum(tX.data_ptr(), torch.float32, N, M, N, out, accumulate=True)
+    torch.cuda.synchronize()
+    assert O.rel_err(out.cpu().numpy(), X.astype(np.float64).sum(0) + 3.0) < 1e-5
+    xb = pkg.mha_ops.cast_bf16(tX)
+    torch.cuda.synchronize()
+    assert torch.equal(xb, tX.to(torch.bfloat16))
+    pkg.mha_ops.colsum(xb.data_ptr(), torch.bfloat16, N, M, N, out, accumulate=False)
+    torch.cuda.synchronize()
+    ref = _bf16_round(X).astype(np.float64).sum(0)
+    assert O.rel_err(out.cpu().numpy(), ref) < 1e-5
+
+
+def test_split_merge_heads_reference_semantics(pkg, cuda_dev):
+    torch = _torch()
+    B, T, NH, HD = 2, 7, 3, 4
+    C = NH * HD
+    qkv = np.random.default_rng(0).standard_normal((B * T, 3 * C)).astype(np.float32)
+    tq = _dev(qkv)
+    q, k, v = (torch.empty(B * NH * T * HD, device="cuda") for _ in range(3))
+    pkg.mha_ops.split_heads(tq.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), B, T, NH, HD)
+    rq, rk, rv = O.split_heads(qkv, B, T, NH, HD)
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), rq.reshape(-1))
+    assert np.array_equal(k.cpu().numpy(), rk.reshape(-1))
+    assert np.array_equal(v.cpu().numpy(), rv.reshape(-1))
+    ctx = torch.empty(B * T * C, device="cuda")
+    pkg.mha_ops.merge_heads(q.data_ptr(), ctx.data_ptr(), B, T, NH, HD)
+    torch.cuda.synchronize()
+    assert np.array_equal(ctx.cpu().numpy(), O.merge_heads(rq, B, T, NH, HD).reshape(-1))
+    # the same adapters by the reference's kernel names (get_shared_mha_module().get_function)
+    mod = pkg.get_shared_mha_module()
+    ctx2 = torch.empty_like(ctx)
+    mod.get_function("merge_heads_kernel")(q, ctx2, np.int32(B), np.int32(T), np.int32(NH), np.int32(HD),
+                                           block=(256, 1, 1), grid=(1, 1))
+    torch.cuda.synchronize()
+    assert torch.equal(ctx, ctx2)

@@ -1,0 +1,146 @@
+"""API-level parity of the drop-in MultiHeadAttention (model/gpt.py:478-707).
+
+Mirrors test_mha_integration_parity.py: same seeds, same shapes, same checked quantities (forward
+output, the forward caches, dIn and the four parameter gradients), against fixtures produced by
+the reference's own MultiHeadAttention, with its tolerance rtol=1e-4, atol=1e-5 for the float32
+path, plus max-relative 1e-5.  The bf16 tensor-core path is checked against the oracle at 2e-2.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from oracle import mha_oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = dict(rtol=1e-4, atol=1e-5)
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _load_weights(attn, g):
+    torch = _torch()
+    for p, key in ((attn.c_attn_w, "w_qkv"), (attn.c_attn_b, "b_qkv"), (attn.c_proj_w, "w_o"),
+                   (attn.c_proj_b, "b_o")):
+        p.weights.copy_(torch.from_numpy(g[key]))
+
+
+def _run(attn, x, dy, B, T, accumulate=False):
+    torch = _torch()
+    gx = torch.from_numpy(x).cuda()
+    out = attn.forward(gx, B, T)
+    gdy = torch.from_numpy(dy).cuda()
+    din = attn.backward(gdy, B, T, accumulate=accumulate)
+    torch.cuda.synchronize()
+    res = dict(out=out.get(), din=din.get(), d_attn_w=attn.c_attn_w.grads.cpu().numpy(),
+               d_attn_b=attn.c_attn_b.grads.cpu().numpy(), d_proj_w=attn.c_proj_w.grads.cpu().numpy(),
+               d_proj_b=attn.c_proj_b.grads.cpu().numpy())
+    out.free()
+    din.free()
+    return res
+
+
+def test_integration_oracle_scenario(pkg, cuda_dev):
+    """capture_mha_oracle.py / test_mha_integration_parity.py: seed 4242, B=2 T=5 C=8 NH=2.
+    Construction from the seeded global NumPy generator reproduces the reference's weights."""
+    g = np.load(os.path.join(GOLDEN, "mha_b2_t5_c8_nh2.npz"))
+    B, T, C, NH = (int(g[k]) for k in ("B", "T", "C", "NH"))
+    np.random.seed(4242)
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T))
+    np.testing.assert_array_equal(attn.c_attn_w.weights.cpu().numpy(), g["w_qkv"])
+    np.testing.assert_array_equal(attn.c_proj_w.weights.cpu().numpy(), g["w_o"])
+    rng = np.random.RandomState(4243)
+    x = rng.normal(0.0, 1.0, size=(B * T, C)).astype(np.float32)
+    dy = rng.normal(0.0, 1.0, size=(B * T, C)).astype(np.float32)
+    np.testing.assert_array_equal(x, g["x"])
+    torch = _torch()
+    out = attn.forward(torch.from_numpy(x).cuda(), B, T)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.get(), g["out"], **TOL)
+    for name in ("cache_q", "cache_k", "cache_v", "cache_attn_weights", "cache_context"):
+        np.testing.assert_allclose(getattr(attn, name), g[name], **TOL, err_msg=name)
+    din = attn.backward(torch.from_numpy(dy).cuda(), B, T)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(din.get(), g["din"], **TOL)
+    np.testing.assert_allclose(attn.c_attn_w.grads.cpu().numpy(), g["d_attn_w"], **TOL)
+    np.testing.assert_allclose(attn.c_attn_b.grads.cpu().numpy(), g["d_attn_b"], **TOL)
+    np.testing.assert_allclose(attn.c_proj_w.grads.cpu().numpy(), g["d_proj_w"], **TOL)
+    np.testing.assert_allclose(attn.c_proj_b.grads.cpu().numpy(), g["d_proj_b"], **TOL)
+
+
+FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "mha_*.npz")))
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=[os.path.basename(p) for p in FIXTURES])
+def test_mha_fp32_matches_reference_fixture(pkg, cuda_dev, path):
+    g = np.load(path)
+    B, T, C, NH = (int(g[k]) for k in ("B", "T", "C", "NH"))
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T))
+    _load_weights(attn, g)
+    res = _run(attn, g["x"], g["dy"], B, T)
+    for k, v in res.items():
+        ref = g["out"] if k == "out" else g["din"] if k == "din" else g[k]
+        np.testing.assert_allclose(v, ref, **TOL, err_msg=k)
+        assert O.rel_err(v, ref) < 1e-5, (k, O.rel_err(v, ref))
+
+
+@pytest.mark.parametrize("cfg,B,T,C,NH,prec,tol", [
+    (1, 8, 128, 64, 4, "fp32", 1e-5),      # the 'small' preset, full size
+    (2, 16, 128, 256, 8, "fp32", 1e-5),    # training-batch shape, batch slice
+    (3, 2, 1024, 512, 8, "bf16", 2e-2),    # long context, batch slice
+    (5, 2, 512, 768, 12, "bf16", 2e-2),    # data-parallel step shape, batch slice
+    (1, 4, 100, 128, 2, "bf16", 2e-2),     # ragged T on the tensor-core path
+])
+def test_mha_config_against_oracle(pkg, cuda_dev, cfg, B, T, C, NH, prec, tol):
+    inp = O.make_config_inputs(cfg, B, T, C, NH)
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
+                                                attention_precision=prec))
+    _load_weights(attn, inp)
+    res = _run(attn, inp["x"], inp["dy"], B, T)
+    out, cache = O.mha_forward(inp["x"], inp["w_qkv"], inp["b_qkv"], inp["w_o"], inp["b_o"], B, T, NH)
+    din, daw, dab, dpw, dpb = O.mha_backward(cache, inp["dy"], inp["w_qkv"], inp["w_o"], B, T, NH)
+    ref = dict(out=out, din=din, d_attn_w=daw, d_attn_b=dab, d_proj_w=dpw, d_proj_b=dpb)
+    for k in ref:
+        assert O.rel_err(res[k], ref[k]) < tol, (k, O.rel_err(res[k], ref[k]))
+
+
+@pytest.mark.parametrize("prec", ["fp32", "bf16"])
+def test_accumulate_adds_to_existing_grads(pkg, cuda_dev, prec):
+    B, T, C, NH = 2, 64, 128, 2
+    inp = O.make_config_inputs(9, B, T, C, NH)
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
+                                                attention_precision=prec))
+    _load_weights(attn, inp)
+    first = _run(attn, inp["x"], inp["dy"], B, T, accumulate=False)
+    second = _run(attn, inp["x"], inp["dy"], B, T, accumulate=True)
+    for k in ("d_attn_w", "d_attn_b", "d_proj_w", "d_proj_b"):
+        np.testing.assert_allclose(second[k], 2 * first[k], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(second["din"], first["din"], rtol=0, atol=0)
+
+
+def test_backward_without_forward_raises(pkg, cuda_dev):
+    torch = _torch()
+    attn = pkg.MultiHeadAttention(16, 2)
+    with pytest.raises(RuntimeError, match="without forward caches"):
+        attn.backward(torch.zeros(4 * 16, device="cuda"), 1, 4)
+    attn.forward(torch.zeros(4 * 16, device="cuda"), 1, 4)
+    attn.free_forward_caches()
+    with pytest.raises(RuntimeError, match="without forward caches"):
+        attn.backward(torch.zeros(4 * 16, device="cuda"), 1, 4)
+
+
+def test_native_library_is_what_runs(pkg, cuda_dev):
+    """Every op of a forward+backward is a launch of libattn_b200.so kernels."""
+    torch = _torch()
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=64, num_heads=4, max_len=32))
+    before = pkg.launch_count()
+    out = attn.forward(torch.randn(2 * 32 * 64, device="cuda"), 2, 32)
+    attn.backward(torch.randn(2 * 32 * 64, device="cuda"), 2, 32)
+    torch.cuda.synchronize()
+    assert pkg.launch_count() - before >= 8
+    out.free()
