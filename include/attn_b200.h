@@ -50,6 +50,13 @@ const char* attn_last_error_string(void);
 uint64_t attn_launch_count(void);
 
 /*
+ * Status word of the tensor-core kernels on the current device: 0, or the code of a bounded
+ * wait inside a kernel that gave up (the kernel then skipped its remaining work and returned
+ * instead of hanging).  Synchronises with the device.  clear != 0 resets it to 0.
+ */
+int attn_device_error(int clear);
+
+/*
  * Causal attention forward: O = softmax(scale * Q K^T + causal mask) V, plus lse.
  * Replaces fused_attention_forward_kernel (core/mha_kernels.py:404-521); instead of writing the
  * normalised probabilities Scores[B*NH,T,T] it writes lse[B,NH,T].

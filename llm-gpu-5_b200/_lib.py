@@ -31,6 +31,7 @@ SIGNATURES = {
     "attn_version": (_i, []),
     "attn_last_error_string": (ctypes.c_char_p, []),
     "attn_launch_count": (ctypes.c_uint64, []),
+    "attn_device_error": (_i, [_i]),
     "attn_fwd": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i, _p]),
     "attn_bwd_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "attn_bwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _i, _i, _i, _i,

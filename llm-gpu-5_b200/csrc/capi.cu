@@ -5,7 +5,7 @@
 // sets the per-thread error string; no kernel runs.  This mirrors the reference's failure
 // behaviour at the API level (MultiHeadAttention raises before touching the GPU when its caches
 // are missing, model/gpt.py:649-650) while keeping the ABI free of exceptions.
-#include "common.cuh"
+#include "tc_common.cuh"
 
 #include <atomic>
 #include <cstdarg>
@@ -35,6 +35,72 @@ int check_launch(const char* what) {
     return ATTN_ERR_CUDA;
   }
   return ATTN_OK;
+}
+
+// ---- device error word of the tensor-core kernels' bounded waits ---------------------------
+static __device__ int g_dev_error;
+static int* g_dev_error_ptr[64];
+
+int* dev_error_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("cudaGetDevice failed");
+    return nullptr;
+  }
+  if (!g_dev_error_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_dev_error);
+    if (e != cudaSuccess) {
+      set_error("cudaGetSymbolAddress(error word) failed: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_dev_error_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_dev_error_ptr[dev];
+}
+
+// ---- TMA tensor maps through the driver entry point (no libcuda link dependency) ----------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+bool make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable");
+    return false;
+  }
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i < rank - 1) st[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx,
+                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d): rank %d dims %llu x %llu", (int)r, rank,
+              (unsigned long long)dims[0], (unsigned long long)dims[1]);
+    return false;
+  }
+  return true;
 }
 
 static int sm_count() {
@@ -101,6 +167,18 @@ int attn_version(void) { return 100; }
 const char* attn_last_error_string(void) { return g_last_error.c_str(); }
 
 uint64_t attn_launch_count(void) { return g_launches.load(); }
+
+int attn_device_error(int clear) {
+  int* p = dev_error_ptr();
+  if (!p) return ATTN_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return ATTN_ERR_CUDA;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpy(p, &z, sizeof(int), cudaMemcpyHostToDevice);
+  }
+  return v;
+}
 
 int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int NH, int T,
              int D, int64_t in_sb, int64_t in_st, int64_t in_sh, int64_t out_sb, int64_t out_st,

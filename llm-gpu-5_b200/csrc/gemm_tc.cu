@@ -1,10 +1,342 @@
-// tcgen05 tensor-core GEMM (placeholder until the sm_100a kernel lands).
-#include "common.cuh"
+// tcgen05 tensor-core GEMM for the attention projections (bf16 operands, fp32 accumulation).
+//
+// C[M,N] (=|+=) op(A)[M,K] . op(B)[K,N] (+ bias[N]), C float32 or bf16.  Serves the QKV and
+// output projections of MultiHeadAttention.forward (model/gpt.py:558, :629; matmul_2d_kernel,
+// core/kernels.py:119-140) and the projection gradients of its backward (model/gpt.py:666-689).
+//
+// Persistent, warp-specialised kernel, one CTA per SM:
+//   warp 0      TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 4-stage ring
+//   warp 1      TMEM allocation and the single MMA-issuing thread: 4 x tcgen05.mma (128x256x16)
+//               per 64-deep K block, accumulating in TMEM
+//   warps 2-5   epilogue: tcgen05.ld of the 128x256 fp32 accumulator (one row per thread), bias,
+//               conversion, global stores
+// The accumulator is double-buffered in TMEM (2 x 256 columns) so the epilogue of one tile
+// overlaps the main loop of the next.  Either operand may be K-major or MN-major (the transposed
+// operands of the weight gradients); TMA writes both in the canonical 128B-swizzled layouts.
+// Weight-gradient shapes (M, N = d_model, K = tokens) are split along K; the splits add their
+// partial tiles into C with fp32 atomics (C is zeroed first unless accumulating).
+#include "tc_common.cuh"
+
 namespace attn {
-bool tc_gemm_supported(int, int, int, int64_t, int, int64_t, int, const void*, const void*) { return false; }
-int gemm_tc(const void*, int64_t, int, const void*, int64_t, int, void*, int64_t, int, const float*,
-            int, int, int, int, cudaStream_t) {
-  set_error("tensor-core GEMM not built");
-  return ATTN_ERR_UNSUPPORTED;
+
+constexpr int GT_BM = 128, GT_BN = 256, GT_BK = 64, GT_STAGES = 4;
+constexpr int GT_THREADS = 192;
+constexpr int GT_A_BYTES = GT_BM * GT_BK * 2;  // 16 KB
+constexpr int GT_B_BYTES = GT_BN * GT_BK * 2;  // 32 KB
+constexpr int GT_STAGE_BYTES = GT_A_BYTES + GT_B_BYTES;
+constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + 1024 + 256;
+constexpr uint32_t GT_TMEM_COLS = 512;
+
+struct GemmParams {
+  int M, N, K;
+  int a_mn, b_mn;
+  int tiles_m, tiles_n, kb_total, kb_per_split, units;
+  void* C;
+  int64_t ldc;
+  int c_bf16, vec_ok, accumulate, atomic;
+  const float* bias;
+  int* err;
+};
+
+__device__ __forceinline__ void unit_coords(const GemmParams& p, int unit, int& tm, int& tn, int& kb0,
+                                            int& kb1) {
+  tn = unit % p.tiles_n;
+  tm = (unit / p.tiles_n) % p.tiles_m;
+  const int split = unit / (p.tiles_n * p.tiles_m);
+  kb0 = split * p.kb_per_split;
+  kb1 = min(p.kb_total, kb0 + p.kb_per_split);
 }
+
+__device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int n0, const uint32_t (&r)[32],
+                                                 bool add_bias) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  if (add_bias && p.bias) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (n0 + i < p.N) v[i] += __ldg(p.bias + n0 + i);
+  }
+  const bool full = n0 + 32 <= p.N;
+  if (p.c_bf16) {
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)m * p.ldc + n0;
+    if (full && p.vec_ok) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 u;
+        u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+        u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+        u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+        u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+        reinterpret_cast<uint4*>(c)[i] = u;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (n0 + i < p.N) c[i] = __float2bfloat16_rn(v[i]);
+    }
+    return;
+  }
+  float* c = reinterpret_cast<float*>(p.C) + (int64_t)m * p.ldc + n0;
+  if (p.atomic) {
+    for (int i = 0; i < 32; ++i)
+      if (n0 + i < p.N) atomicAdd(c + i, v[i]);
+    return;
+  }
+  if (full && p.vec_ok) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      if (p.accumulate) {
+        const float4 e = reinterpret_cast<const float4*>(c)[i];
+        o.x += e.x; o.y += e.y; o.z += e.z; o.w += e.w;
+      }
+      reinterpret_cast<float4*>(c)[i] = o;
+    }
+  } else {
+    for (int i = 0; i < 32; ++i)
+      if (n0 + i < p.N) c[i] = p.accumulate ? c[i] + v[i] : v[i];
+  }
+}
+
+__global__ void __launch_bounds__(GT_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GT_STAGES * GT_STAGE_BYTES);
+  uint64_t* empty = full + GT_STAGES;
+  uint64_t* tfull = empty + GT_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GT_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, GT_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.units && ok; unit += gridDim.x) {
+        int tm, tn, kb0, kb1;
+        unit_coords(p, unit, tm, tn, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, p.err, 101)) { ok = false; break; }
+          uint8_t* sa = smem + s * GT_STAGE_BYTES;
+          uint8_t* sb = sa + GT_A_BYTES;
+          mbar_arrive_expect_tx(&full[s], GT_STAGE_BYTES);
+          const int k0 = kb * GT_BK;
+          if (!p.a_mn) {
+            tma_load_2d(sa, &tmA, &full[s], k0, tm * GT_BM);
+          } else {
+            tma_load_2d(sa, &tmA, &full[s], tm * GT_BM, k0);
+            tma_load_2d(sa + 8192, &tmA, &full[s], tm * GT_BM + 64, k0);
+          }
+          if (!p.b_mn) {
+            tma_load_2d(sb, &tmB, &full[s], k0, tn * GT_BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < GT_BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full[s], tn * GT_BN + 64 * j, k0);
+          }
+          if (++s == GT_STAGES) { s = 0; ph ^= 1; }
+        }
+      }
+      // tail: wait until the MMA thread has released every stage, so no asynchronous arrive is
+      // still in flight to this CTA's shared memory when it exits
+      for (int i = 0; i < GT_STAGES && ok; ++i) {
+        ok = mbar_wait(&empty[s], ph ^ 1, p.err, 105);
+        if (++s == GT_STAGES) { s = 0; ph ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(GT_BM, GT_BN, p.a_mn, p.b_mn);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int local = 0;
+      for (int unit = blockIdx.x; unit < p.units && ok; unit += gridDim.x, ++local) {
+        int tm, tn, kb0, kb1;
+        unit_coords(p, unit, tm, tn, kb0, kb1);
+        const int acc = local & 1;
+        const uint32_t acc_ph = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1, p.err, 102)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * GT_BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[s], ph, p.err, 103)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * GT_STAGE_BYTES);
+          const uint32_t sb = sa + GT_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < GT_BK / 16; ++k) {
+            const uint64_t ad = p.a_mn ? smem_desc_sw128(sa + k * 2048, 8192, 1024)
+                                       : smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = p.b_mn ? smem_desc_sw128(sb + k * 2048, 8192, 1024)
+                                       : smem_desc_sw128(sb + k * 32, 16, 1024);
+            umma_ss(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+          if (++s == GT_STAGES) { s = 0; ph ^= 1; }
+        }
+        if (ok) umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+      }
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    int local = 0;
+    for (int unit = blockIdx.x; unit < p.units; unit += gridDim.x, ++local) {
+      int tm, tn, kb0, kb1;
+      unit_coords(p, unit, tm, tn, kb0, kb1);
+      const int acc = local & 1;
+      const uint32_t acc_ph = (local >> 1) & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, p.err, 104));
+      if (!ok) break;
+      tc_fence_after();
+      const int m = tm * GT_BM + row;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * GT_BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < GT_BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c0, r);
+        tmem_wait_ld();
+        const int n0 = tn * GT_BN + c0;
+        if (m < p.M && n0 < p.N) epilogue_store32(p, m, n0, r, kb0 == 0);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, GT_TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------
+static int g_sms = 0;
+
+static int num_sms() {
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_sms <= 0) g_sms = 148;
+  }
+  return g_sms;
+}
+
+bool tc_gemm_supported(int M, int N, int K, int64_t lda, int a_trans, int64_t ldb, int b_trans,
+                       const void* A, const void* B) {
+  (void)a_trans;
+  (void)b_trans;
+  return aligned(A, 16) && aligned(B, 16) && lda % 8 == 0 && ldb % 8 == 0 && K >= 16 &&
+         (int64_t)M * N * K >= (int64_t)1 << 21;
+}
+
+// Pick the number of K splits so that the work units fill the SMs in near-whole waves.
+static int choose_splits(int tiles, int kb_total, int sms) {
+  if (tiles >= sms || kb_total < 16) return 1;
+  int best = 1;
+  double best_eff = (double)tiles / (double)(((tiles + sms - 1) / sms) * sms);
+  for (int s = 2; s <= 64 && kb_total / s >= 4; ++s) {
+    const int units = tiles * s;
+    const double eff = (double)units / (double)(((units + sms - 1) / sms) * sms);
+    if (eff > best_eff + 0.02) {
+      best = s;
+      best_eff = eff;
+    }
+    if (best_eff > 0.95) break;
+  }
+  return best;
+}
+
+int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans, void* C,
+            int64_t ldc, int c_dtype, const float* bias, int M, int N, int K, int accumulate,
+            cudaStream_t s) {
+  CUtensorMap tmA, tmB;
+  {
+    uint64_t dims[2], strides[1];
+    uint32_t box[2];
+    if (!a_trans) {  // A stored [M][lda], K contiguous
+      dims[0] = K; dims[1] = M; box[0] = 64; box[1] = GT_BM;
+    } else {         // A stored [K][lda], M contiguous
+      dims[0] = M; dims[1] = K; box[0] = 64; box[1] = 64;
+    }
+    strides[0] = (uint64_t)lda * 2;
+    if (!make_tmap_bf16(&tmA, A, 2, dims, strides, box)) return ATTN_ERR_CUDA;
+  }
+  {
+    uint64_t dims[2], strides[1];
+    uint32_t box[2];
+    if (b_trans) {   // B stored [N][ldb], K contiguous
+      dims[0] = K; dims[1] = N; box[0] = 64; box[1] = GT_BN;
+    } else {         // B stored [K][ldb], N contiguous
+      dims[0] = N; dims[1] = K; box[0] = 64; box[1] = 64;
+    }
+    strides[0] = (uint64_t)ldb * 2;
+    if (!make_tmap_bf16(&tmB, B, 2, dims, strides, box)) return ATTN_ERR_CUDA;
+  }
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.a_mn = a_trans ? 1 : 0;
+  p.b_mn = b_trans ? 0 : 1;
+  p.tiles_m = (M + GT_BM - 1) / GT_BM;
+  p.tiles_n = (N + GT_BN - 1) / GT_BN;
+  p.kb_total = (K + GT_BK - 1) / GT_BK;
+  const int sms = num_sms();
+  const int tiles = p.tiles_m * p.tiles_n;
+  int splits = c_dtype == ATTN_F32 ? choose_splits(tiles, p.kb_total, sms) : 1;
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
+  p.units = tiles * splits;
+  p.C = C;
+  p.ldc = ldc;
+  p.c_bf16 = c_dtype == ATTN_BF16;
+  p.accumulate = accumulate;
+  p.atomic = splits > 1;
+  p.bias = bias;
+  p.vec_ok = aligned(C, 16) && (ldc % (p.c_bf16 ? 8 : 4) == 0);
+  p.err = dev_error_ptr();
+  if (!p.err) return ATTN_ERR_CUDA;
+  if (p.atomic && !accumulate)
+    ATTN_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s));
+  static bool attr_set = false;
+  if (!attr_set) {
+    ATTN_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GT_SMEM));
+    attr_set = true;
+  }
+  const int grid = p.units < sms ? p.units : sms;
+  gemm_tc_kernel<<<grid, GT_THREADS, GT_SMEM, s>>>(tmA, tmB, p);
+  count_launch();
+  return check_launch("gemm_tc_kernel");
+}
+
 }  // namespace attn

@@ -170,7 +170,8 @@ def test_decode_matches_oracle(pkg, cuda_dev, dtype, B, NH, L, D):
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("M,N,K,at,bt", [(100, 72, 40, 0, 0), (256, 768, 256, 0, 0), (64, 96, 300, 1, 0),
                                          (130, 64, 96, 0, 1), (384, 256, 128, 1, 1), (1024, 2304, 768, 0, 0),
-                                         (768, 2304, 4096, 1, 0), (4096, 768, 2304, 0, 1), (512, 512, 8192, 1, 0)])
+                                         (768, 2304, 4096, 1, 0), (4096, 768, 2304, 0, 1), (512, 512, 8192, 1, 0),
+                                         (300, 520, 200, 0, 0), (1000, 300, 136, 1, 1), (777, 2304, 768, 0, 1)])
 def test_gemm_matches_numpy(pkg, cuda_dev, dtype, M, N, K, at, bt):
     torch = _torch()
     rng = np.random.default_rng(M + N + K)
@@ -197,6 +198,7 @@ def test_gemm_matches_numpy(pkg, cuda_dev, dtype, M, N, K, at, bt):
                      torch.bfloat16, M, N, K)
     torch.cuda.synchronize()
     assert O.rel_err(tCb.float().cpu().numpy(), ref) < 1e-2
+    assert pkg.lib.attn_device_error(1) == 0  # no bounded wait inside a kernel gave up
 
 
 @pytest.mark.parametrize("M,N", [(1, 5), (1000, 33), (262144, 96), (4097, 2304)])
