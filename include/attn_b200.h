@@ -117,6 +117,28 @@ int attn_decode(const void* q, const void* k_cache, const void* v_cache, void* o
                 float scale, int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * attn_decode without a workspace argument: it allocates nothing.  No counterpart in the
+ * reference (which has no decode kernel at all); it exists for callers that cannot allocate a
+ * per-call device workspace: callers whose device memory is owned by another allocator (a pool
+ * that reserved the free HBM up front, as a serving process sizing its KV cache does) and thin
+ * FFI callers that hold only the q/K/V/o pointers.
+ * The split partial states go to one fixed file-scope device array of 4 MiB (1,048,576 floats),
+ * held on every GPU that loads the library until the process exits.  Problems needing more,
+ * B*NH*ceil(L/256)*(D+2) > 1,048,576 (e.g. B=64, NH=8, L=2048, D=64 needs 270,336), are rejected
+ * with ATTN_ERR_UNSUPPORTED and a message; nothing is launched.
+ * The first call on each device resolves the array's device address (cudaGetSymbolAddress, with
+ * that device current); make that first call before any stream capture.  Every call shares the
+ * array and it keeps the last call's contents (each call writes every partial state before reading
+ * it, so nothing needs zeroing); calls that overlap on the GPU (concurrent streams or threads)
+ * race on the array and must be serialised by the caller.  Arguments otherwise as attn_decode.
+ */
+int attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
+                        int B, int NH, int L, int D,
+                        int64_t q_sb, int64_t q_sh,
+                        int64_t kv_sb, int64_t kv_sl, int64_t kv_sh,
+                        float scale, int dtype, void* stream);
+
+/*
  * Projection GEMM: C[M,N] = op(A)[M,K] . op(B)[K,N] (+ bias[N]) ; with accumulate, C += ...
  * Replaces matmul_2d_kernel (core/kernels.py:119-140) and the projection-gradient GEMMs of
  * model/gpt.py:666-689 (dWo = ctx^T dY, dCtx = dY Wo^T, dWqkv = x^T dQKV, dX = dQKV Wqkv^T).

@@ -39,6 +39,8 @@ SIGNATURES = {
     "attn_decode_workspace_size": (_sz, [_i, _i, _i, _i]),
     "attn_decode": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _f, _i,
                          _p, _sz, _p]),
+    "attn_decode_noalloc": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _f,
+                                 _i, _p]),
     "attn_probs": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _f, _i, _p]),
     "attn_gemm": (_i, [_p, _i64, _i, _p, _i64, _i, _i, _p, _i64, _i, _p, _i, _i, _i, _i, _p]),
     "attn_colsum_workspace_size": (_sz, [_i, _i]),

@@ -190,3 +190,78 @@ int decode(const void* q, const void* k, const void* v, void* o, float* lse, int
 }
 
 }  // namespace attn
+
+// ------------------------------------------------------------------------------------------
+// attn_decode_noalloc: the same decode with its scratch in a fixed device array
+// ------------------------------------------------------------------------------------------
+// Some callers cannot hand this library a workspace: their device memory belongs to another
+// allocator (a pool that reserved the free HBM up front, as the reference's monkey-patched
+// pycuda mem_alloc pool or a serving process that pre-sizes its KV cache does), or they are thin
+// FFI callers that hold only the q/K/V/o pointers.  For them the per-split partial softmax
+// states live in this file-scope array, sized once at load time; every GPU that loads the
+// library holds it until the process exits.
+#include <mutex>
+
+namespace attn {
+
+constexpr size_t kNoAllocDecodeFloats = size_t(1) << 20;  // 4 MiB
+static __device__ __align__(256) float g_decode_scratch[kNoAllocDecodeFloats];
+
+static std::mutex g_decode_scratch_mu;
+static float* g_decode_scratch_dev[64];  // device address of the array, per device
+
+// Resolve the array's device address on the current device (first call per device only).
+// In host code `g_decode_scratch` names a host-side stand-in, not device memory, so the address
+// must come from cudaGetSymbolAddress with the device current.
+static float* decode_scratch_address() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("attn_decode_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_decode_scratch_mu);
+  if (!g_decode_scratch_dev[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("attn_decode_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_decode_scratch_dev[dev] = static_cast<float*>(p);
+  }
+  return g_decode_scratch_dev[dev];
+}
+
+}  // namespace attn
+
+extern "C" int attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o,
+                                   float* lse, int B, int NH, int L, int D, int64_t q_sb,
+                                   int64_t q_sh, int64_t kv_sb, int64_t kv_sl, int64_t kv_sh,
+                                   float scale, int dtype, void* stream) {
+  using namespace attn;
+  clear_error();
+  ATTN_REQUIRE(q && k_cache && v_cache && o, "attn_decode_noalloc: null pointer argument");
+  ATTN_REQUIRE(dtype == ATTN_F32 || dtype == ATTN_BF16, "attn_decode_noalloc: bad dtype");
+  ATTN_REQUIRE(B > 0 && NH > 0 && L > 0 && D > 0, "attn_decode_noalloc: sizes must be positive");
+  const int vec = dtype == ATTN_F32 ? 4 : 8;
+  ATTN_REQUIRE(D % vec == 0, "attn_decode_noalloc: head_dim must be a multiple of %d for this dtype", vec);
+  const int64_t st[5] = {q_sb, q_sh, kv_sb, kv_sl, kv_sh};
+  for (int i = 0; i < 5; ++i)
+    ATTN_REQUIRE(st[i] >= 0 && st[i] % vec == 0, "attn_decode_noalloc: strides must be multiples of %d", vec);
+  ATTN_REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(o, 4),
+               "attn_decode_noalloc: q/k/v must be 16-byte aligned");
+  const size_t need = decode_ws(B, NH, L, D);
+  if (need > sizeof(float) * kNoAllocDecodeFloats) {
+    set_error("attn_decode_noalloc: this problem needs %zu bytes of scratch but the fixed array holds "
+              "%zu (B*NH*ceil(L/256)*(D+2) must be <= %zu floats); use attn_decode with a workspace",
+              need, sizeof(float) * kNoAllocDecodeFloats, kNoAllocDecodeFloats);
+    return ATTN_ERR_UNSUPPORTED;
+  }
+  float* ws = decode_scratch_address();
+  if (!ws) return ATTN_ERR_CUDA;
+  // every partial state is written before it is read: nothing in the array needs zeroing
+  return decode(q, k_cache, v_cache, o, lse, B, NH, L, D, q_sb, q_sh, kv_sb, kv_sl, kv_sh, scale,
+                dtype, ws, as_stream(stream));
+}
