@@ -248,7 +248,10 @@ def run_ours(args, cfg):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     pkg = importlib.import_module("llm-gpu-5_b200")
-    w = WORKLOADS[cfg]
+    w = dict(WORKLOADS[cfg])
+    if args.batch:
+        w["global_batch"] = args.batch
+        w["name"] += f" [batch overridden to {args.batch}]"
     GB, T, C, NH = w["global_batch"], w["T"], w["C"], w["NH"]
     assert GB % world == 0, f"global batch {GB} is not divisible by {world} GPUs"
     B = GB // world
@@ -398,6 +401,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=5, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the global batch (small cases for profiler captures only)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args, args.config)
