@@ -164,6 +164,15 @@ size_t attn_colsum_workspace_size(int M, int N);
 int attn_colsum(const void* X, int x_dtype, int64_t ldx, int M, int N, float* out,
                 int accumulate, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Y = bf16(X) and out[n] (+)= sum_m X[m, n] in one pass over X (float32 [M][ldx]; Y bf16 [M][ldy]).
+ * The upstream-gradient cast of the bf16 path fused with the output-projection bias gradient
+ * (model/gpt.py:667).  Workspace: attn_colsum_workspace_size(M, N).
+ */
+int attn_cast_colsum_f32(const float* X, int64_t ldx, int M, int N, void* Y, int64_t ldy,
+                         float* out, int accumulate, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
 /* y[i] = bf16(x[i]) (round to nearest even), n elements. */
 int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream);
 

@@ -132,6 +132,7 @@ int merge_heads(const float*, float*, int, int, int, int, cudaStream_t);
 int cast_f32_bf16(const float*, void*, int64_t, cudaStream_t, int);
 size_t colsum_ws(int, int);
 int colsum(const void*, int, int64_t, int, int, float*, int, void*, cudaStream_t);
+int cast_colsum(const float*, int64_t, int, int, void*, int64_t, float*, int, void*, cudaStream_t);
 int attn_probs_launch(const void*, const void*, const float*, float*, int, int, int, int, int64_t,
                       int64_t, int64_t, float, int, cudaStream_t);
 size_t decode_ws(int, int, int, int);
@@ -314,6 +315,18 @@ int attn_colsum(const void* X, int x_dtype, int64_t ldx, int M, int N, float* ou
     return ATTN_ERR_WORKSPACE;
   }
   return colsum(X, x_dtype, ldx, M, N, out, accumulate, workspace, as_stream(stream));
+}
+
+int attn_cast_colsum_f32(const float* X, int64_t ldx, int M, int N, void* Y, int64_t ldy, float* out,
+                         int accumulate, void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(X && Y && out, "attn_cast_colsum_f32: null pointer argument");
+  ATTN_REQUIRE(M > 0 && N > 0 && ldx >= N && ldy >= N, "attn_cast_colsum_f32: bad shape");
+  if (!workspace || workspace_bytes < colsum_ws(M, N)) {
+    set_error("attn_cast_colsum_f32: workspace of %zu bytes required", colsum_ws(M, N));
+    return ATTN_ERR_WORKSPACE;
+  }
+  return cast_colsum(X, ldx, M, N, Y, ldy, out, accumulate, workspace, as_stream(stream));
 }
 
 int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream) {

@@ -180,36 +180,86 @@ int cast_f32_bf16(const float* x, void* y, int64_t n, cudaStream_t s, int sm_cou
 }
 
 // Column sums: pass 1 writes one partial row per split of M; pass 2 adds the partials in a fixed
-// order (deterministic), optionally onto the existing output.
+// order (deterministic), optionally onto the existing output.  Pass 1 reads 16-byte vectors: a
+// CTA covers 256 columns with 256/V threads per row (V = 4 fp32 or 8 bf16 elements per thread) and
+// 4 or 8 rows in flight.  The fp32 variant can also write the bf16 copy of X in the same pass
+// (the dY cast and the output-projection bias gradient of model/gpt.py:667 read dY once).
+constexpr int CS_COLS = 256;
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 static int colsum_splits(int M, int N) {
-  const int col_blocks = (N + 31) / 32;
-  int s = (600 + col_blocks - 1) / col_blocks;
+  const int col_blocks = (N + CS_COLS - 1) / CS_COLS;
+  int s = (4 * 148 + col_blocks - 1) / col_blocks;
   const int max_s = (M + 63) / 64;
   if (s > max_s) s = max_s;
-  if (s > 256) s = 256;
+  if (s > 1024) s = 1024;
   return s < 1 ? 1 : s;
 }
 
 size_t colsum_ws(int M, int N) { return (size_t)colsum_splits(M, N) * N * sizeof(float); }
 
-template <typename T>
+template <typename T, bool CAST>
 __global__ void __launch_bounds__(256)
 colsum_partial_kernel(const T* __restrict__ X, int64_t ldx, int M, int N, int rows_per_split,
-                      float* __restrict__ part) {
-  __shared__ float red[8][33];
-  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
-  const int n = blockIdx.x * 32 + tx;
+                      float* __restrict__ part, __nv_bfloat16* __restrict__ Y, int64_t ldy, int vec) {
+  constexpr int V = 16 / sizeof(T);
+  constexpr int TX = CS_COLS / V;  // threads along the columns
+  constexpr int TY = 256 / TX;     // rows in flight
+  __shared__ float red[TY][CS_COLS + 4];
+  const int tx = threadIdx.x % TX, ty = threadIdx.x / TX;
+  const int c0 = blockIdx.x * CS_COLS + tx * V;
   const int r0 = blockIdx.y * rows_per_split;
   const int r1 = min(M, r0 + rows_per_split);
-  float acc = 0.f;
-  if (n < N)
-    for (int r = r0 + ty; r < r1; r += 8) acc += Elem<T>::load(X + (int64_t)r * ldx + n);
-  red[ty][tx] = acc;
+  float acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = 0.f;
+  const bool full = vec && (c0 + V <= N);
+  for (int r = r0 + ty; r < r1; r += TY) {
+    const T* row = X + (int64_t)r * ldx + c0;
+    float v[V];
+    if (full) {
+      if constexpr (sizeof(T) == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(row);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      } else {
+        const uint4 u = *reinterpret_cast<const uint4*>(row);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+          v[2 * i] = f.x;
+          v[2 * i + 1] = f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) v[i] = (c0 + i < N) ? Elem<T>::load(row + i) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] += v[i];
+    if constexpr (CAST) {
+      __nv_bfloat16* y = Y + (int64_t)r * ldy + c0;
+      if (full) {
+        *reinterpret_cast<uint2*>(y) = make_uint2(bf16x2_bits(v[0], v[1]), bf16x2_bits(v[2], v[3]));
+      } else {
+        for (int i = 0; i < V; ++i)
+          if (c0 + i < N) y[i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) red[ty][tx * V + i] = acc[i];
   __syncthreads();
-  if (ty == 0 && n < N) {
+  for (int c = threadIdx.x; c < CS_COLS; c += 256) {
+    const int n = blockIdx.x * CS_COLS + c;
+    if (n >= N) continue;
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s += red[i][tx];
+    for (int i = 0; i < TY; ++i) s += red[i][c];
     part[(int64_t)blockIdx.y * N + n] = s;
   }
 }
@@ -223,23 +273,40 @@ __global__ void colsum_combine_kernel(const float* __restrict__ part, int splits
   out[n] = accumulate ? out[n] + s : s;
 }
 
-int colsum(const void* X, int x_dtype, int64_t ldx, int M, int N, float* out, int accumulate,
-           void* ws, cudaStream_t s) {
+static int colsum_launch(const void* X, int x_dtype, int64_t ldx, int M, int N, float* out,
+                         int accumulate, void* ws, __nv_bfloat16* Y, int64_t ldy, cudaStream_t s) {
   const int splits = colsum_splits(M, N);
   const int rps = (M + splits - 1) / splits;
-  dim3 g1((N + 31) / 32, splits);
+  dim3 g1((N + CS_COLS - 1) / CS_COLS, splits);
   float* part = (float*)ws;
-  if (x_dtype == ATTN_F32)
-    colsum_partial_kernel<float><<<g1, 256, 0, s>>>((const float*)X, ldx, M, N, rps, part);
-  else
-    colsum_partial_kernel<__nv_bfloat16><<<g1, 256, 0, s>>>((const __nv_bfloat16*)X, ldx, M, N, rps,
-                                                            part);
+  const size_t es = x_dtype == ATTN_F32 ? 4 : 2;
+  int vec = aligned(X, 16) && ((ldx * es) % 16 == 0);
+  if (Y) vec = vec && aligned(Y, 8) && ((ldy * 2) % 8 == 0);
+  if (x_dtype == ATTN_F32) {
+    if (Y)
+      colsum_partial_kernel<float, true><<<g1, 256, 0, s>>>((const float*)X, ldx, M, N, rps, part, Y, ldy, vec);
+    else
+      colsum_partial_kernel<float, false><<<g1, 256, 0, s>>>((const float*)X, ldx, M, N, rps, part, nullptr, 0, vec);
+  } else {
+    colsum_partial_kernel<__nv_bfloat16, false><<<g1, 256, 0, s>>>((const __nv_bfloat16*)X, ldx, M, N, rps,
+                                                                   part, nullptr, 0, vec);
+  }
   count_launch();
   int rc = check_launch("colsum_partial_kernel");
   if (rc) return rc;
   colsum_combine_kernel<<<(N + 255) / 256, 256, 0, s>>>(part, splits, N, out, accumulate);
   count_launch();
   return check_launch("colsum_combine_kernel");
+}
+
+int colsum(const void* X, int x_dtype, int64_t ldx, int M, int N, float* out, int accumulate,
+           void* ws, cudaStream_t s) {
+  return colsum_launch(X, x_dtype, ldx, M, N, out, accumulate, ws, nullptr, 0, s);
+}
+
+int cast_colsum(const float* X, int64_t ldx, int M, int N, void* Y, int64_t ldy, float* out,
+                int accumulate, void* ws, cudaStream_t s) {
+  return colsum_launch(X, ATTN_F32, ldx, M, N, out, accumulate, ws, (__nv_bfloat16*)Y, ldy, s);
 }
 
 }  // namespace attn

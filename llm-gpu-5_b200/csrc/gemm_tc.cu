@@ -5,26 +5,31 @@
 // core/kernels.py:119-140) and the projection gradients of its backward (model/gpt.py:666-689).
 //
 // Persistent, warp-specialised kernel, one CTA per SM:
-//   warp 0      TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 4-stage ring
+//   warp 0      TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 3-stage ring
 //   warp 1      TMEM allocation and the single MMA-issuing thread: 4 x tcgen05.mma (128x256x16)
 //               per 64-deep K block, accumulating in TMEM
 //   warps 2-5   epilogue: tcgen05.ld of the 128x256 fp32 accumulator (one row per thread), bias,
-//               conversion, global stores
+//               conversion, then 128-byte-wide column chunks staged in swizzled shared memory and
+//               written by TMA stores (or TMA reduce-adds when accumulating into C)
 // The accumulator is double-buffered in TMEM (2 x 256 columns) so the epilogue of one tile
 // overlaps the main loop of the next.  Either operand may be K-major or MN-major (the transposed
 // operands of the weight gradients); TMA writes both in the canonical 128B-swizzled layouts.
 // Weight-gradient shapes (M, N = d_model, K = tokens) are split along K; the splits add their
-// partial tiles into C with fp32 atomics (C is zeroed first unless accumulating).
+// partial tiles into C with TMA reduce-adds (C is zeroed first unless accumulating).  Outputs
+// without a 16-byte row pitch fall back to direct per-row stores (fp32 atomics for K splits).
 #include "tc_common.cuh"
+
+#include <string.h>
 
 namespace attn {
 
-constexpr int GT_BM = 128, GT_BN = 256, GT_BK = 64, GT_STAGES = 4;
+constexpr int GT_BM = 128, GT_BN = 256, GT_BK = 64, GT_STAGES = 3;
 constexpr int GT_THREADS = 192;
 constexpr int GT_A_BYTES = GT_BM * GT_BK * 2;  // 16 KB
 constexpr int GT_B_BYTES = GT_BN * GT_BK * 2;  // 32 KB
 constexpr int GT_STAGE_BYTES = GT_A_BYTES + GT_B_BYTES;
-constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + 1024 + 256;
+constexpr int GT_EPI_BYTES = GT_BM * 128;      // one 128-row x 128-byte output chunk (16 KB)
+constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + 2 * GT_EPI_BYTES + 1024 + 256;
 constexpr uint32_t GT_TMEM_COLS = 512;
 
 struct GemmParams {
@@ -34,6 +39,8 @@ struct GemmParams {
   void* C;
   int64_t ldc;
   int c_bf16, vec_ok, accumulate, atomic;
+  int tma_epi;  // 1: stage output chunks in swizzled smem and write them with TMA
+  int reduce;   // with tma_epi: add into C (accumulate or K splits) instead of storing
   const float* bias;
   int* err;
 };
@@ -100,10 +107,11 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
 
 __global__ void __launch_bounds__(GT_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const GemmParams p) {
+               const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GT_STAGES * GT_STAGE_BYTES);
+  uint8_t* epi = smem + GT_STAGES * GT_STAGE_BYTES;  // [2] output staging chunks
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + 2 * GT_EPI_BYTES);
   uint64_t* empty = full + GT_STAGES;
   uint64_t* tfull = empty + GT_STAGES;
   uint64_t* tempty = tfull + 2;
@@ -204,6 +212,74 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (ok) umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
       }
     }
+  } else if (p.tma_epi) {
+    // Epilogue through shared memory: each thread owns one accumulator row; a chunk of 128 bytes
+    // per row (32 fp32 or 64 bf16 columns) goes to a 128B-swizzled staging buffer (conflict-free
+    // 16-byte stores) and one thread writes the 128-row chunk with a TMA store, or a TMA
+    // reduce-add when accumulating or splitting K.  Two staging buffers alternate.
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool leader = (warp == 2 && lane == 0);
+    const int cols = p.c_bf16 ? 64 : 32;  // columns per 128-byte chunk
+    int buf = 0;
+    int local = 0;
+    for (int unit = blockIdx.x; unit < p.units; unit += gridDim.x, ++local) {
+      int tm, tn, kb0, kb1;
+      unit_coords(p, unit, tm, tn, kb0, kb1);
+      const int acc = local & 1;
+      const uint32_t acc_ph = (local >> 1) & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, p.err, 104));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * GT_BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < GT_BN; c0 += cols) {
+        uint32_t r[64];
+        tmem_ld32(taddr + c0, *reinterpret_cast<uint32_t(*)[32]>(r));
+        if (p.c_bf16) tmem_ld32(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+        tmem_wait_ld();
+        if (c0 + cols >= GT_BN) {  // accumulator fully read: hand it back to the MMA thread
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
+        const int n0 = tn * GT_BN + c0;
+        if (n0 >= p.N) continue;  // uniform across the CTA
+        float v[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+        if (p.bias && kb0 == 0) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i < cols && n0 + i < p.N) v[i] += __ldg(p.bias + n0 + i);
+        }
+        uint32_t w[32];
+        if (p.c_bf16) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+        }
+        if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
+        named_bar_sync(1, 128);
+        uint8_t* rowp = epi + buf * GT_EPI_BYTES + row * 128;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) =
+              make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (leader) {
+          if (p.reduce)
+            tma_reduce_add_2d(&tmC, epi + buf * GT_EPI_BYTES, n0, tm * GT_BM);
+          else
+            tma_store_2d(&tmC, epi + buf * GT_EPI_BYTES, n0, tm * GT_BM);
+          bulk_commit();
+        }
+        buf ^= 1;
+      }
+    }
+    if (leader) bulk_wait0();
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
@@ -326,6 +402,19 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   p.vec_ok = aligned(C, 16) && (ldc % (p.c_bf16 ? 8 : 4) == 0);
   p.err = dev_error_ptr();
   if (!p.err) return ATTN_ERR_CUDA;
+  // TMA epilogue whenever C is 16-byte aligned with 16-byte row pitch
+  CUtensorMap tmC;
+  memset(&tmC, 0, sizeof(tmC));
+  p.tma_epi = p.vec_ok ? 1 : 0;
+  p.reduce = (accumulate || p.atomic) ? 1 : 0;
+  if (p.tma_epi) {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)ldc * (p.c_bf16 ? 2 : 4)};
+    const uint32_t box[2] = {(uint32_t)(p.c_bf16 ? 64 : 32), (uint32_t)GT_BM};
+    const bool ok = p.c_bf16 ? make_tmap_bf16(&tmC, C, 2, dims, strides, box)
+                             : make_tmap_f32(&tmC, C, 2, dims, strides, box);
+    if (!ok) return ATTN_ERR_CUDA;
+  }
   if (p.atomic && !accumulate)
     ATTN_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s));
   static bool attr_set = false;
@@ -334,7 +423,7 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
     attr_set = true;
   }
   const int grid = p.units < sms ? p.units : sms;
-  gemm_tc_kernel<<<grid, GT_THREADS, GT_SMEM, s>>>(tmA, tmB, p);
+  gemm_tc_kernel<<<grid, GT_THREADS, GT_SMEM, s>>>(tmA, tmB, tmC, p);
   count_launch();
   return check_launch("gemm_tc_kernel");
 }

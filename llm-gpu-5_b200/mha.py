@@ -279,14 +279,17 @@ class MultiHeadAttention:
         M = B * T
         dt = self._dt
         dy = _as_tensor(gpu_dOut, M * C)
-        with self._rng("cast"):
-            dy_op = ops.cast_bf16(dy) if dt == torch.bfloat16 else dy
-        # output projection: dWo = ctx^T dY, dbo = sum(dY), dCtx = dY Wo^T   (gpt.py:666-670)
+        # output projection: dbo = sum(dY), dWo = ctx^T dY, dCtx = dY Wo^T   (gpt.py:666-670)
+        if dt == torch.bfloat16:
+            with self._rng("cast_colsum"):  # one pass over dY: bf16 copy + bias gradient
+                dy_op = ops.cast_colsum(dy.view(M, C), self.c_proj_b.grads, accumulate=accumulate)
+        else:
+            dy_op = dy
+            with self._rng("colsum"):
+                ops.colsum(dy.data_ptr(), torch.float32, C, M, C, self.c_proj_b.grads, accumulate=accumulate)
         with self._rng("gemm_dwo"):
             ops.gemm(c["ctx"].data_ptr(), C, True, dy_op.data_ptr(), C, False, dt,
                      self.c_proj_w.grads.data_ptr(), C, torch.float32, C, C, M, accumulate=accumulate)
-        with self._rng("colsum"):
-            ops.colsum(dy.data_ptr(), torch.float32, C, M, C, self.c_proj_b.grads, accumulate=accumulate)
         dctx = torch.empty((M, C), dtype=dt, device="cuda")
         with self._rng("gemm_dctx"):
             ops.gemm(dy_op.data_ptr(), C, False, c["w_o"].data_ptr(), C, True, dt, dctx.data_ptr(), C,

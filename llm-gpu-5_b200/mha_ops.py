@@ -137,6 +137,21 @@ def colsum(X: int, x_dtype: torch.dtype, ldx: int, M: int, N: int, out: torch.Te
          workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
 
 
+def cast_colsum(x: torch.Tensor, colsum_out: torch.Tensor, accumulate: bool = False,
+                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 copy of a float32 [M, N] matrix plus its column sums (into/onto colsum_out), one pass."""
+    assert x.dtype == torch.float32 and x.is_contiguous() and x.dim() == 2
+    M, N = x.shape
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    need = lib.attn_colsum_workspace_size(M, N)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    call("attn_cast_colsum_f32", x.data_ptr(), N, M, N, out.data_ptr(), N, colsum_out.data_ptr(),
+         int(accumulate), workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
+    return out
+
+
 def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     assert x.dtype == torch.float32 and x.is_contiguous()
     if out is None:

@@ -244,3 +244,39 @@ def test_split_merge_heads_reference_semantics(pkg, cuda_dev):
                                            block=(256, 1, 1), grid=(1, 1))
     torch.cuda.synchronize()
     assert torch.equal(ctx, ctx2)
+
+
+@pytest.mark.parametrize("M,N", [(4096, 768), (1000, 33), (262144, 64)])
+def test_cast_colsum_fused(pkg, cuda_dev, M, N):
+    """bf16 copy plus column sums of a float32 matrix in one pass (the dY cast fused with dbo)."""
+    torch = _torch()
+    rng = np.random.default_rng(M + N + 1)
+    X = rng.standard_normal((M, N)).astype(np.float32)
+    tX = _dev(X)
+    sums = torch.full((N,), 2.0, dtype=torch.float32, device="cuda")
+    y = pkg.mha_ops.cast_colsum(tX, sums, accumulate=True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, tX.to(torch.bfloat16))
+    assert O.rel_err(sums.cpu().numpy(), X.astype(np.float64).sum(0) + 2.0) < 1e-5
+
+
+@pytest.mark.parametrize("M,N,K,at,bt,pad", [(512, 256, 128, 0, 0, 1), (256, 256, 8192, 1, 0, 3),
+                                             (384, 520, 256, 0, 1, 5)])
+def test_gemm_tc_unaligned_output_pitch(pkg, cuda_dev, M, N, K, at, bt, pad):
+    """Tensor-core GEMM whose output rows are not 16-byte aligned: the per-row store epilogue."""
+    torch = _torch()
+    rng = np.random.default_rng(M * 7 + K)
+    A = _bf16_round(rng.standard_normal((K, M) if at else (M, K)).astype(np.float32))
+    Bm = _bf16_round(rng.standard_normal((N, K) if bt else (K, N)).astype(np.float32))
+    C0 = rng.standard_normal((M, N + pad)).astype(np.float32)
+    tA, tB = _dev(A, torch.bfloat16), _dev(Bm, torch.bfloat16)
+    ref = (A.T if at else A).astype(np.float64) @ (Bm.T if bt else Bm).astype(np.float64)
+    for acc in (False, True):
+        tC = _dev(C0.copy())
+        pkg.mha_ops.gemm(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, torch.bfloat16,
+                         tC.data_ptr(), N + pad, torch.float32, M, N, K, accumulate=acc)
+        torch.cuda.synchronize()
+        got = tC.cpu().numpy()
+        assert O.rel_err(got[:, :N], ref + (C0[:, :N] if acc else 0)) < 1e-3
+        np.testing.assert_array_equal(got[:, N:], C0[:, N:])  # padding columns untouched
+    assert pkg.lib.attn_device_error(1) == 0
