@@ -1,0 +1,58 @@
+// Shared pieces of the tcgen05 attention kernels (head_dim 64, bf16): tile constants, the 4D TMA
+// maps that read a [B, T, NH, 64] or [B, NH, T, 64] operand through its element strides, and the
+// host-side checks of those strides.
+#pragma once
+
+#include "tc_common.cuh"
+
+namespace attn {
+
+constexpr int AT_TILE = 128;                       // query / key rows per tile
+constexpr int AT_D = 64;                           // head_dim handled by the tensor-core kernels
+constexpr int AT_TILE_BYTES = AT_TILE * AT_D * 2;  // 16 KB bf16 tile, 128 B per row
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+struct TileMap {
+  CUtensorMap map;
+  int h_first;  // 1: dims {D, NH, T, B}; 0: dims {D, T, NH, B}
+};
+
+// 128 rows (t0 .. t0+127) of head h of batch b; rows past T read as zeros.
+__device__ __forceinline__ void load_tile(void* dst, const TileMap& tm, uint64_t* bar, int b, int h,
+                                          int t0) {
+  if (tm.h_first)
+    tma_load_4d(dst, &tm.map, bar, 0, h, t0, b);
+  else
+    tma_load_4d(dst, &tm.map, bar, 0, t0, h, b);
+}
+
+// Element strides usable by TMA: 16-byte multiples and a row pitch of at least one head.
+inline bool head_strides_ok(int64_t sb, int64_t st, int64_t sh) {
+  return sb % 8 == 0 && st % 8 == 0 && sh % 8 == 0 && st >= AT_D;
+}
+
+// 4D map over a bf16 tensor with element (b, t, h, d) at base[b*sb + t*st + h*sh + d]; the two
+// middle dimensions are ordered by stride so the map's strides increase.
+inline bool make_head_map(TileMap* tm, const void* base, int B, int NH, int T, int64_t sb, int64_t st,
+                          int64_t sh) {
+  uint64_t dims[4], strides[3];
+  uint32_t box[4];
+  tm->h_first = sh <= st ? 1 : 0;
+  dims[0] = AT_D;
+  box[0] = AT_D;
+  if (tm->h_first) {
+    dims[1] = NH; dims[2] = T; dims[3] = B;
+    strides[0] = sh * 2; strides[1] = st * 2; strides[2] = sb * 2;
+    box[1] = 1; box[2] = AT_TILE; box[3] = 1;
+  } else {
+    dims[1] = T; dims[2] = NH; dims[3] = B;
+    strides[0] = st * 2; strides[1] = sh * 2; strides[2] = sb * 2;
+    box[1] = AT_TILE; box[2] = 1; box[3] = 1;
+  }
+  return make_tmap_bf16(&tm->map, base, 4, dims, strides, box);
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace attn

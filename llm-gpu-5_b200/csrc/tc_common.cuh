@@ -74,18 +74,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait until the phase with the given parity has completed.  Gives up after `limit_ns`
 // (default 2 s, far above any legitimate wait in these kernels), records `site` in g_tc_error
 // and returns false; callers then skip their remaining work and fall through to teardown.
+// The poll loop only reads the %globaltimer register; the error word in global memory (another
+// wait having given up) is looked at once per millisecond of waiting, so a wait that completes
+// normally is noticed within one try_wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site,
                                           uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  uint64_t next_check = t0 + 1000000ull;
   while (true) {
-    for (int i = 0; i < 64; ++i)
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) {
+    const uint64_t now = globaltimer_ns();
+    if (now - t0 > limit_ns) {
       atomicCAS(err, 0, site);
       return false;
     }
-    if (*(volatile int*)err != 0) return false;  // another wait gave up: stop early
+    if (now > next_check) {
+      if (*(volatile int*)err != 0) return false;  // another wait gave up: stop early
+      next_check = now + 1000000ull;
+    }
   }
 }
 
