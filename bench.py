@@ -313,36 +313,66 @@ def run_ours(args, cfg):
     value = GB * T / (ms * 1e-3)
 
     # ---------------- end to end through the public API with host buffers
+    # Every step copies its x and dY in from pinned host memory and its dX and gradients out.
+    # The copies run on their own streams with double-buffered device slots, so step k's
+    # host->device copies overlap step k-1's compute and step k-1's device->host copies (what a
+    # training loop with a prefetching data loader does); each step still moves all its bytes.
     x_h = torch.empty((M, C), dtype=torch.float32, pin_memory=True)
     dy_h = torch.empty((M, C), dtype=torch.float32, pin_memory=True)
     x_h.copy_(x)
     dy_h.copy_(dy)
-    dx_h = torch.empty((M, C), dtype=torch.float32, pin_memory=True)
-    g_h = torch.empty(attn.flat_grads.numel(), dtype=torch.float32, pin_memory=True)
-    x_d = torch.empty_like(x)
-    dy_d = torch.empty_like(dy)
+    comp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    slots = []
+    for _ in range(2):
+        slots.append(dict(
+            x=torch.empty_like(x), dy=torch.empty_like(dy),
+            g=torch.empty_like(attn.flat_grads),
+            dx_h=torch.empty((M, C), dtype=torch.float32, pin_memory=True),
+            g_h=torch.empty(attn.flat_grads.numel(), dtype=torch.float32, pin_memory=True),
+            ev_x=torch.cuda.Event(), ev_dy=torch.cuda.Event(), ev_done=torch.cuda.Event(),
+            ev_out=torch.cuda.Event(), used=False))
 
-    def e2e_step():
-        x_d.copy_(x_h, non_blocking=True)
-        out = attn.forward(x_d, B, T)
-        dy_d.copy_(dy_h, non_blocking=True)
-        din = attn.backward(dy_d, B, T)
+    def e2e_step(k):
+        sl = slots[k % 2]
+        with torch.cuda.stream(s_in):
+            if sl["used"]:
+                s_in.wait_event(sl["ev_done"])  # the slot's previous step has read its inputs
+            sl["x"].copy_(x_h, non_blocking=True)
+            sl["ev_x"].record(s_in)
+            sl["dy"].copy_(dy_h, non_blocking=True)
+            sl["ev_dy"].record(s_in)
+        if sl["used"]:
+            comp.wait_event(sl["ev_out"])  # the slot's previous gradient snapshot has been copied out
+        comp.wait_event(sl["ev_x"])
+        out = attn.forward(sl["x"], B, T)
+        comp.wait_event(sl["ev_dy"])
+        din = attn.backward(sl["dy"], B, T)
         attn.wait_grad_sync()
-        dx_h.copy_(din.tensor, non_blocking=True)
-        g_h.copy_(attn.flat_grads, non_blocking=True)
+        sl["g"].copy_(attn.flat_grads)
+        sl["ev_done"].record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(sl["ev_done"])
+            sl["dx_h"].copy_(din.tensor, non_blocking=True)
+            sl["g_h"].copy_(sl["g"], non_blocking=True)
+            sl["ev_out"].record(s_out)
+        din.tensor.record_stream(s_out)
+        sl["used"] = True
         out.free()
         din.free()
 
-    e2e_steps = max(1, min(steps, 5))
-    for _ in range(2):
-        e2e_step()
+    e2e_steps = max(2, min(steps, 6))
+    for k in range(2):
+        e2e_step(k)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
+    e0.record(comp)
+    s_in.wait_stream(comp)
+    for k in range(e2e_steps):
+        e2e_step(k)
+    comp.wait_stream(s_out)
+    e1.record(comp)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
     h2d = 2 * M * C * 4

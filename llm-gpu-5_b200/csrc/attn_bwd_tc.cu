@@ -4,25 +4,31 @@
 // softmax_fused_backward / matmul_grad_{q,k,v}, core/mha_kernels.py:195-236, 592-680):
 //   dV = P^T dO,  dP = dO V^T,  dS = P (dP - rowsum(dP P)) * scale,  dQ = dS K,  dK = dS^T Q
 // with rowsum(dP P) = rowsum(dO O) = delta (model/gpt.py:675-677), and P recomputed from the
-// forward's log-sum-exp instead of being stored.
+// forward's log-sum-exp instead of being stored.  The softmax scale is applied when dQ and dK are
+// written out (both are linear in dS).
 //
 // 1. attn_bwd_prep_kernel: delta = rowsum(dO * O) and lse in log2 units, both padded to whole
 //    128-row tiles (padding rows get lse = +inf so their probabilities are exactly 0).
-// 2. attn_bwd_tc_kernel: one CTA per (b, h, 128-key tile).  K, V and the dK/dV accumulators stay
-//    resident; the query tiles that can see these keys stream through a 2-stage TMA ring.  Each
-//    query tile is processed as two halves of 64 queries, double-buffered in TMEM so that the
-//    tensor core works on one half while the dS warpgroup works on the other:
-//      MMA thread     S^T = K Q_h^T and dP^T = V dO_h^T (128x64 each) into TMEM buffer h,
-//                     then dV += P^T dO_h and dK += dS^T Q_h with P^T, dS^T read from TMEM,
-//                     and per query tile dQ = dS K (128x64) with dS read from shared memory
-//      dS warps       one key row per thread: P^T = 2^(S^T*scale*log2e - lse2), dS^T =
-//                     P^T (dP^T - delta) scale; bf16 P^T and dS^T back to TMEM (over the S^T /
-//                     dP^T columns already read) and dS^T to shared memory for the dQ MMA
-//      dQ warps       drain each dQ tile from TMEM to swizzled shared memory and add it into an
-//                     fp32 accumulator in the workspace with TMA reduce-adds (done in L2)
-//    TMEM: half-buffers [0,128) and [128,256) (S^T | dP^T, 64 columns each), dV [256,320),
-//    dK [320,384), dQ [384,448).
-// 3. attn_dq_convert_kernel: fp32 dQ accumulator -> bf16 dQ in the caller's layout.
+// 2. attn_bwd_tc_kernel, persistent: one CTA per SM walks the heads (b, h) assigned to it; for
+//    each head it visits the 128-key tiles jt = nq-1 .. 0, keeps K_jt, V_jt and the dK/dV
+//    accumulators resident and streams the query tiles i = jt .. nq-1 that can see those keys:
+//      MMA thread     S^T = K Q_i^T and dP^T = V dO_i^T (128 x 128 each) into TMEM;
+//                     dV += P^T dO_i and dK += dS^T Q_i with P^T, dS^T read from TMEM;
+//                     dQ_i(partial) = dS K with dS read from shared memory
+//      8 P/dS warps   one key row per thread and 64 of the 128 queries per warpgroup:
+//                     P^T = 2^(S^T*scale*log2e - lse2) into its own TMEM columns (so S^T of the
+//                     next tile can be computed while dS is formed), dS^T = P^T (dP^T - delta)
+//                     to TMEM over the dP^T columns already read and to shared memory for dQ
+//      4 drain warps  per tile: the dQ partial from TMEM to a per-CTA fp32 accumulator (a TMA
+//                     store from the diagonal key tile, which reaches a query tile first, TMA
+//                     reduce-adds after it, all into L2-resident memory); for key tile 0 (each
+//                     query tile's last contribution) the accumulator row is read back, the
+//                     partial added, and scale * dQ written as bf16.  Per key tile: dK (times
+//                     scale) and dV out.
+//    Because one CTA owns a head, the dQ accumulator needs no zeroing and no atomics between
+//    CTAs, and no separate conversion pass.
+//    TMEM: S^T [0,128), dP^T / dS^T [128,256), P^T [256,320), dV [320,384), dK [384,448),
+//    dQ [448,512).
 //
 // Every mbarrier wait is bounded (tc_common.cuh): a wait that gives up sets the library's device
 // error word and the kernel skips its remaining work instead of hanging.
@@ -32,25 +38,27 @@
 
 namespace attn {
 
-constexpr int BA_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 dS, warps 6-9 dQ drain
+constexpr int BA_THREADS = 448;  // warp 0 TMA, warp 1 MMA, warps 2-9 P/dS, warps 10-13 drain
 constexpr uint32_t BA_TMEM_COLS = 512;
-constexpr int BA_QSTAGE = 2 * AT_TILE_BYTES + 2 * AT_TILE * 4;  // Q, dO, lse2, delta
-constexpr int BA_DS_BYTES = 2 * AT_TILE_BYTES;                   // dS^T of one query tile
-constexpr int BA_SMEM = 2 * AT_TILE_BYTES /*K,V*/ + 2 * BA_QSTAGE + 2 * BA_DS_BYTES +
-                        AT_TILE * AT_D * 4 /*dQ staging*/ + 1024 + 256;
+constexpr uint32_t BA_TM_S = 0, BA_TM_DP = 128, BA_TM_P = 256, BA_TM_DV = 320, BA_TM_DK = 384, BA_TM_DQ = 448;
+constexpr int BA_MAX_CTAS = 160;  // the dQ accumulator workspace is sized for this many CTAs
+constexpr int BA_SMEM = 1024 + 4 * AT_TILE_BYTES /*K,V x2*/ + 4 * AT_TILE_BYTES /*Q,dO x2*/ +
+                        2 * AT_TILE_BYTES /*dS^T*/ + AT_TILE * AT_D * 4 /*dQ staging*/ +
+                        4 * AT_TILE * 4 /*lse2, delta x2*/ + 256;
 
 struct BwdMaps {
   TileMap q, k, v, dout;
-  CUtensorMap dq_acc;  // fp32 [BH*Tp rows][64], box 32 x 128, 128B swizzle
+  CUtensorMap dq_acc;  // fp32 [grid * Tp rows][64], box 32 x 128, 128B swizzle
 };
 
 struct BwdParams {
-  int NH, T, nq, Tp;
+  int NH, T, nq, Tp, BH;
   float scale, scale_log2;
   const float* lse2;    // [BH][Tp] lse * log2 e (+inf on padding rows)
   const float* delta;   // [BH][Tp]
-  __nv_bfloat16 *dk, *dv;
-  int64_t sb, st, sh;   // strides of dk/dv (same as q/k/v)
+  float* dq_acc;        // [gridDim.x][Tp][64]
+  __nv_bfloat16 *dq, *dk, *dv;
+  int64_t sb, st, sh;   // strides of dq/dk/dv (same as q/k/v)
   int* err;
 };
 
@@ -89,49 +97,94 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o,
   lse2[idx] = lse[bh * T + t] * LOG2E;
 }
 
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Wait until at most n of this thread's most recent bulk groups are pending (n clamped to 7).
+__device__ __forceinline__ void bulk_wait_upto(int n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.bulk.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.bulk.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.bulk.wait_group 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.bulk.wait_group 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.bulk.wait_group 5;" ::: "memory"); break;
+    case 6: asm volatile("cp.async.bulk.wait_group 6;" ::: "memory"); break;
+    default: asm volatile("cp.async.bulk.wait_group 7;" ::: "memory"); break;
+  }
+}
+
+// 64 fp32 values (two TMEM loads of 32 columns) times `mul` -> 32 packed bf16 pairs.
+__device__ __forceinline__ void pack_row_bf16(uint32_t (&out)[32], const uint32_t (&a0)[32],
+                                              const uint32_t (&a1)[32], float mul) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    out[j] = pack_bf16x2(__uint_as_float(a0[2 * j]) * mul, __uint_as_float(a0[2 * j + 1]) * mul);
+    out[16 + j] = pack_bf16x2(__uint_as_float(a1[2 * j]) * mul, __uint_as_float(a1[2 * j + 1]) * mul);
+  }
+}
+
+// 32 packed bf16 pairs -> 8 x 16 B at dst (one 64-element row).
+__device__ __forceinline__ void store_packed_row(__nv_bfloat16* dst, const uint32_t (&w)[32]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    reinterpret_cast<uint4*>(dst)[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+
 __global__ void __launch_bounds__(BA_THREADS, 1)
 attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = smem;
-  uint8_t* sV = sK + AT_TILE_BYTES;
-  uint8_t* sStage = sV + AT_TILE_BYTES;         // [2] x {Q, dO, lse2[128], delta[128]}
-  uint8_t* sDS = sStage + 2 * BA_QSTAGE;         // [2] x dS^T: two 64-query blocks of [128 keys][64]
-  uint8_t* sDQ = sDS + 2 * BA_DS_BYTES;          // dQ staging: two [128 q][32 fp32] swizzled halves
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDQ + AT_TILE * AT_D * 4);
-  uint64_t* kv_full = bars;
-  uint64_t* q_full = bars + 1;       // [2] per query-tile stage
-  uint64_t* q_empty = q_full + 2;    // [2]
-  uint64_t* sdp_full = q_empty + 2;  // [2] per TMEM half-buffer
-  uint64_t* ds_ready = sdp_full + 2; // [2]
-  uint64_t* buf_free = ds_ready + 2; // [2]
-  uint64_t* ds_free = buf_free + 2;  // [2] per dS^T shared-memory buffer
-  uint64_t* dq_full = ds_free + 2;
-  uint64_t* dq_free = dq_full + 1;
-  uint64_t* kv_done = dq_free + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kv_done + 1);
+  uint8_t* sK = smem;                          // [2]
+  uint8_t* sV = sK + 2 * AT_TILE_BYTES;        // [2]
+  uint8_t* sQ = sV + 2 * AT_TILE_BYTES;        // [2]
+  uint8_t* sDO = sQ + 2 * AT_TILE_BYTES;       // [2]
+  uint8_t* sDS = sDO + 2 * AT_TILE_BYTES;      // dS^T: two 64-query blocks of [128 keys][64]
+  uint8_t* sDQ = sDS + 2 * AT_TILE_BYTES;      // dQ staging: two [128 q][32 fp32] swizzled halves
+  float* sLse = reinterpret_cast<float*>(sDQ + AT_TILE * AT_D * 4);  // [2][128]
+  float* sDelta = sLse + 2 * AT_TILE;                                // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + 2 * AT_TILE);
+  uint64_t* kv_full = bars;           // [2] per key tile (unit)
+  uint64_t* kv_empty = kv_full + 2;   // [2]
+  uint64_t* q_full = kv_empty + 2;    // [2] per query tile
+  uint64_t* q_empty = q_full + 2;     // [2]
+  uint64_t* s_full = q_empty + 2;     // S^T in TMEM
+  uint64_t* dp_full = s_full + 1;     // dP^T in TMEM
+  uint64_t* p_ready = dp_full + 1;    // S^T read, P^T written (256 arrivals)
+  uint64_t* dv_done = p_ready + 1;    // the dV MMA reading P^T has completed
+  uint64_t* ds_ready = dv_done + 1;   // dP^T read, dS^T written to TMEM and smem (256 arrivals)
+  uint64_t* dk_done = ds_ready + 1;   // the dK MMA reading dS^T from TMEM has completed
+  uint64_t* ds_free = dk_done + 1;    // the dQ MMA reading dS^T from smem has completed
+  uint64_t* dq_full = ds_free + 1;
+  uint64_t* dq_free = dq_full + 1;    // 128 arrivals
+  uint64_t* dkdv_full = dq_free + 1;
+  uint64_t* dkdv_free = dkdv_full + 1;  // 128 arrivals
+  uint64_t* drain_bar = dkdv_free + 1;  // 128 arrivals: sync of the drain warpgroup
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int nkv = p.nq;
-  const int bh = blockIdx.x / nkv;
-  const int jt = (int)(blockIdx.x % nkv);  // key tile; tile 0 sees the most query tiles
-  const int b = bh / p.NH, h = bh % p.NH;
-  const int n_it = p.nq - jt;              // query tiles jt .. nq-1
-  const int n_half = 2 * n_it;
+  const int nq = p.nq;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
-      mbar_init(&sdp_full[s], 1);
-      mbar_init(&ds_ready[s], 128);
-      mbar_init(&buf_free[s], 1);
-      mbar_init(&ds_free[s], 1);
     }
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(p_ready, 256);
+    mbar_init(dv_done, 1);
+    mbar_init(ds_ready, 256);
+    mbar_init(dk_done, 1);
+    mbar_init(ds_free, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 128);
-    mbar_init(kv_done, 1);
+    mbar_init(dkdv_full, 1);
+    mbar_init(dkdv_free, 128);
+    mbar_init(drain_bar, 128);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -142,12 +195,6 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tdV = tmem + 256, tdK = tmem + 320, tdQ = tmem + 384;
-
-  auto stage_q = [&](int s) { return sStage + s * BA_QSTAGE; };
-  auto stage_do = [&](int s) { return sStage + s * BA_QSTAGE + AT_TILE_BYTES; };
-  auto stage_lse = [&](int s) { return reinterpret_cast<float*>(sStage + s * BA_QSTAGE + 2 * AT_TILE_BYTES); };
-  auto stage_delta = [&](int s) { return stage_lse(s) + AT_TILE; };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -156,203 +203,323 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
       tma_prefetch_desc(&maps.k.map);
       tma_prefetch_desc(&maps.v.map);
       tma_prefetch_desc(&maps.dout.map);
-      mbar_arrive_expect_tx(kv_full, 2 * AT_TILE_BYTES);
-      load_tile(sK, maps.k, kv_full, b, h, jt * AT_TILE);
-      load_tile(sV, maps.v, kv_full, b, h, jt * AT_TILE);
+      int u = 0, n = 0;
       bool ok = true;
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int s = it & 1;
-        const uint32_t ph = (it >> 1) & 1;
-        if (!mbar_wait(&q_empty[s], ph ^ 1, p.err, 301)) { ok = false; break; }
-        const int q0 = (jt + it) * AT_TILE;
-        mbar_arrive_expect_tx(&q_full[s], 2 * AT_TILE_BYTES + 2 * AT_TILE * 4);
-        load_tile(stage_q(s), maps.q, &q_full[s], b, h, q0);
-        load_tile(stage_do(s), maps.dout, &q_full[s], b, h, q0);
-        bulk_load(stage_lse(s), p.lse2 + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
-        bulk_load(stage_delta(s), p.delta + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
-      }
-      for (int it = n_it; it < n_it + 2 && ok; ++it)
-        ok = mbar_wait(&q_empty[it & 1], ((it >> 1) & 1) ^ 1, p.err, 302);
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc_sdp = idesc_bf16_f32(128, 64, 0, 0);  // K/V and Q/dO all K-major
-      const uint32_t idesc_kv = idesc_bf16_f32(128, 64, 0, 1);   // A from TMEM, B MN-major
-      const uint32_t idesc_q = idesc_bf16_f32(128, 64, 1, 1);    // A = dS (MN-major), B = K MN-major
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      bool ok = mbar_wait(kv_full, 0, p.err, 303);
-
-      // S^T and dP^T of half n (query tile n/2, queries 64*(n%2) .. +63) into TMEM buffer n%2
-      auto issue_sdp = [&](int n) -> bool {
-        const int it = n >> 1, hf = n & 1, s = it & 1;
-        if (hf == 0 && !mbar_wait(&q_full[s], (it >> 1) & 1, p.err, 304)) return false;
-        tc_fence_after();
-        const uint32_t tS = tmem + (n & 1) * 128, tdP = tS + 64;
-        const uint32_t q_addr = smem_u32(stage_q(s)) + hf * 8192, do_addr = smem_u32(stage_do(s)) + hf * 8192;
-#pragma unroll
-        for (int k = 0; k < AT_D / 16; ++k)
-          umma_ss(tS, smem_desc_sw128(k_addr + k * 32, 16, 1024), smem_desc_sw128(q_addr + k * 32, 16, 1024),
-                  idesc_sdp, k > 0 ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < AT_D / 16; ++k)
-          umma_ss(tdP, smem_desc_sw128(v_addr + k * 32, 16, 1024), smem_desc_sw128(do_addr + k * 32, 16, 1024),
-                  idesc_sdp, k > 0 ? 1u : 0u);
-        umma_commit(&sdp_full[n & 1]);
-        return true;
-      };
-
-      for (int n = 0; n < 2 && n < n_half && ok; ++n) ok = issue_sdp(n);
-      for (int n = 0; n < n_half && ok; ++n) {
-        const int it = n >> 1, hf = n & 1, s = it & 1, bb = n & 1;
-        if (!mbar_wait(&ds_ready[bb], (n >> 1) & 1, p.err, 305)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t tP = tmem + bb * 128, tdS = tP + 64;
-        const uint32_t q_addr = smem_u32(stage_q(s)) + hf * 8192, do_addr = smem_u32(stage_do(s)) + hf * 8192;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)  // dV += P^T dO_h   (k over the 64 queries of the half)
-          umma_ts(tdV, tP + k * 8, smem_desc_sw128(do_addr + k * 2048, 8192, 1024), idesc_kv,
-                  (n > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)  // dK += dS^T Q_h
-          umma_ts(tdK, tdS + k * 8, smem_desc_sw128(q_addr + k * 2048, 8192, 1024), idesc_kv,
-                  (n > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&buf_free[bb]);
-        if (hf == 1) {  // both halves of query tile `it` done: dQ = dS K
-          if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, p.err, 306)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t ds_addr = smem_u32(sDS + (it & 1) * BA_DS_BYTES);
-#pragma unroll
-          for (int k = 0; k < AT_TILE / 16; ++k)
-            umma_ss(tdQ, smem_desc_sw128(ds_addr + k * 2048, 16384, 1024),
-                    smem_desc_sw128(k_addr + k * 2048, 8192, 1024), idesc_q, k > 0 ? 1u : 0u);
-          umma_commit(dq_full);
-          umma_commit(&ds_free[it & 1]);
-          umma_commit(&q_empty[s]);
-        }
-        if (n + 2 < n_half) {
-          // the half-buffer is rewritten only once dV/dK above have read P^T and dS^T from it
-          if (!mbar_wait(&buf_free[bb], (n >> 1) & 1, p.err, 307)) { ok = false; break; }
-          ok = issue_sdp(n + 2);
-        }
-      }
-      if (ok) umma_commit(kv_done);
-    }
-  } else if (warp < 6) {
-    // ---------------- dS warpgroup: one key row per thread ----------------
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // key row within the tile
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    bool ok = true;
-    for (int n = 0; n < n_half; ++n) {
-      const int it = n >> 1, hf = n & 1, s = it & 1, bb = n & 1;
-      bool w = mbar_wait(&sdp_full[bb], (n >> 1) & 1, p.err, 308) &&
-               mbar_wait(&q_full[s], (it >> 1) & 1, p.err, 309);
-      if (w && hf == 0 && it >= 2) w = mbar_wait(&ds_free[it & 1], ((it >> 1) & 1) ^ 1, p.err, 310);
-      ok = __all_sync(0xffffffffu, w);
-      if (!ok) break;
-      tc_fence_after();
-      const bool diag = (it == 0);  // query tile jt: key r is visible to query q iff r <= q
-      const float* lse2 = stage_lse(s) + hf * 64;
-      const float* dl = stage_delta(s) + hf * 64;
-      const uint32_t tS = tmem + bb * 128 + lane_off, tdP = tS + 64;
-      uint8_t* dsrow = sDS + (it & 1) * BA_DS_BYTES + hf * AT_TILE_BYTES + r * 128;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tS + c * 32, sr);
-        tmem_ld32(tdP + c * 32, dr);
-        tmem_wait_ld();
-        uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int ql = c * 32 + i;          // query within the half
-          const int qt = hf * 64 + ql;        // query within the tile
-          float p0 = ex2_approx(fmaf(__uint_as_float(sr[i]), p.scale_log2, -lse2[ql]));
-          float p1 = ex2_approx(fmaf(__uint_as_float(sr[i + 1]), p.scale_log2, -lse2[ql + 1]));
-          if (diag && qt < r) p0 = 0.f;
-          if (diag && qt + 1 < r) p1 = 0.f;
-          const float d0 = p0 * (__uint_as_float(dr[i]) - dl[ql]) * p.scale;
-          const float d1 = p1 * (__uint_as_float(dr[i + 1]) - dl[ql + 1]) * p.scale;
-          pk[i / 2] = pack_bf16x2(p0, p1);
-          dk[i / 2] = pack_bf16x2(d0, d1);
-        }
-        tmem_st16(tS + c * 16, pk);   // P^T over S^T columns already read
-        tmem_st16(tdP + c * 16, dk);  // dS^T over dP^T columns already read
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {  // dS^T -> 128B-swizzled [key row][64 queries] block
-          const int chunk = c * 4 + u;
-          *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
-        }
-      }
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&ds_ready[bb]);
-    }
-    // dK, dV epilogue
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(kv_done, 0, p.err, 311));
-    if (ok) {
-      tc_fence_after();
-      const int key = jt * AT_TILE + r;
-#pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t src_col = which == 0 ? tdV : tdK;
-        uint32_t a0[32], a1[32];
-        tmem_ld32(src_col + lane_off, a0);
-        tmem_ld32(src_col + lane_off + 32, a1);
-        tmem_wait_ld();
-        if (key < p.T) {
-          __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + (int64_t)b * p.sb + (int64_t)key * p.st +
-                               (int64_t)h * p.sh;
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            const uint32_t* src = cc < 4 ? a0 + 8 * cc : a1 + 8 * (cc - 4);
-            uint4 u;
-            u.x = pack_bf16x2(__uint_as_float(src[0]), __uint_as_float(src[1]));
-            u.y = pack_bf16x2(__uint_as_float(src[2]), __uint_as_float(src[3]));
-            u.z = pack_bf16x2(__uint_as_float(src[4]), __uint_as_float(src[5]));
-            u.w = pack_bf16x2(__uint_as_float(src[6]), __uint_as_float(src[7]));
-            reinterpret_cast<uint4*>(dst)[cc] = u;
+      for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
+        const int b = bh / p.NH, h = bh % p.NH;
+        for (int jt = nq - 1; jt >= 0 && ok; --jt, ++u) {
+          const int ks = u & 1;
+          if (!mbar_wait(&kv_empty[ks], ((u >> 1) & 1) ^ 1, p.err, 301)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[ks], 2 * AT_TILE_BYTES);
+          load_tile(sK + ks * AT_TILE_BYTES, maps.k, &kv_full[ks], b, h, jt * AT_TILE);
+          load_tile(sV + ks * AT_TILE_BYTES, maps.v, &kv_full[ks], b, h, jt * AT_TILE);
+          for (int i = jt; i < nq; ++i, ++n) {
+            const int s = n & 1;
+            if (!mbar_wait(&q_empty[s], ((n >> 1) & 1) ^ 1, p.err, 302)) { ok = false; break; }
+            const int q0 = i * AT_TILE;
+            mbar_arrive_expect_tx(&q_full[s], 2 * AT_TILE_BYTES + 2 * AT_TILE * 4);
+            load_tile(sQ + s * AT_TILE_BYTES, maps.q, &q_full[s], b, h, q0);
+            load_tile(sDO + s * AT_TILE_BYTES, maps.dout, &q_full[s], b, h, q0);
+            bulk_load(sLse + s * AT_TILE, p.lse2 + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
+            bulk_load(sDelta + s * AT_TILE, p.delta + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
           }
         }
       }
     }
-  } else {
-    // ---------------- dQ drain warpgroup: one query row per thread ----------------
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const bool leader = (warp == 6 && lane == 0);
-    for (int it = 0; it < n_it; ++it) {
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, 312));
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t a0[32], a1[32];
-      tmem_ld32(tdQ + lane_off, a0);
-      tmem_ld32(tdQ + lane_off + 32, a1);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(dq_free);
-      if (leader) bulk_wait_read0();  // the previous reduce has finished reading the staging buffer
-      named_bar_sync(1, 128);
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_sdp = idesc_bf16_f32(128, 128, 0, 0);  // K/V and Q/dO all K-major
+      const uint32_t idesc_kv = idesc_bf16_f32(128, 64, 0, 1);    // A from TMEM, B MN-major
+      const uint32_t idesc_q = idesc_bf16_f32(128, 64, 1, 1);     // A = dS (MN-major), B = K MN-major
+      const uint32_t tS = tmem + BA_TM_S, tdP = tmem + BA_TM_DP, tP = tmem + BA_TM_P;
+      const uint32_t tdV = tmem + BA_TM_DV, tdK = tmem + BA_TM_DK, tdQ = tmem + BA_TM_DQ;
+      const uint32_t ds_addr = smem_u32(sDS);
+      // the previous tile's dK and dQ are issued after this tile's S^T
+      int pn = -1, ps = 0, pks = 0;
+      bool pfirst = false, plast = false;
+      uint32_t pk_addr = 0;
+      auto finish_prev = [&]() -> bool {
+        if (!mbar_wait(ds_ready, pn & 1, p.err, 303)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + ps * AT_TILE_BYTES);
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint8_t* rowp = sDQ + hf * (AT_TILE * 128) + row * 128;
+        for (int k = 0; k < AT_TILE / 16; ++k)  // dK += dS^T Q   (k over the 128 queries)
+          umma_ts(tdK, tdP + (k >> 2) * 64 + (k & 3) * 8, smem_desc_sw128(q_addr + k * 2048, 8192, 1024),
+                  idesc_kv, (pfirst && k == 0) ? 0u : 1u);
+        umma_commit(dk_done);
+        if (!mbar_wait(dq_free, (pn & 1) ^ 1, p.err, 304)) return false;
+        tc_fence_after();
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const uint32_t* src = (hf == 0 ? a0 : a1) + 4 * ch;
-          *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) = make_uint4(src[0], src[1], src[2], src[3]);
+        for (int k = 0; k < AT_TILE / 16; ++k)  // dQ = dS K   (k over the 128 keys)
+          umma_ss(tdQ, smem_desc_sw128(ds_addr + k * 2048, 16384, 1024),
+                  smem_desc_sw128(pk_addr + k * 2048, 8192, 1024), idesc_q, k > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(ds_free);
+        umma_commit(&q_empty[ps]);
+        if (plast) {
+          umma_commit(dkdv_full);
+          umma_commit(&kv_empty[pks]);
+        }
+        return true;
+      };
+      int u = 0, n = 0;
+      bool ok = true;
+      for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
+        for (int jt = nq - 1; jt >= 0 && ok; --jt, ++u) {
+          const int ks = u & 1;
+          if (!mbar_wait(&kv_full[ks], (u >> 1) & 1, p.err, 305)) { ok = false; break; }
+          const uint32_t k_addr = smem_u32(sK + ks * AT_TILE_BYTES), v_addr = smem_u32(sV + ks * AT_TILE_BYTES);
+          for (int i = jt; i < nq; ++i, ++n) {
+            const int s = n & 1;
+            if (!mbar_wait(&q_full[s], (n >> 1) & 1, p.err, 306)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(sQ + s * AT_TILE_BYTES), do_addr = smem_u32(sDO + s * AT_TILE_BYTES);
+            // S^T = K Q^T: the P/dS warps finished reading the previous S^T (p_ready waited below)
+#pragma unroll
+            for (int k = 0; k < AT_D / 16; ++k)
+              umma_ss(tS, smem_desc_sw128(k_addr + k * 32, 16, 1024), smem_desc_sw128(q_addr + k * 32, 16, 1024),
+                      idesc_sdp, k > 0 ? 1u : 0u);
+            umma_commit(s_full);
+            if (pn >= 0 && !finish_prev()) { ok = false; break; }
+            // dP^T = V dO^T over the previous dS^T: wait for the dK MMA that reads it
+            if (!mbar_wait(dk_done, (n & 1) ^ 1, p.err, 307)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < AT_D / 16; ++k)
+              umma_ss(tdP, smem_desc_sw128(v_addr + k * 32, 16, 1024), smem_desc_sw128(do_addr + k * 32, 16, 1024),
+                      idesc_sdp, k > 0 ? 1u : 0u);
+            umma_commit(dp_full);
+            // dV += P^T dO (the first tile of a key tile starts dV/dK afresh once drained)
+            if (i == jt && !mbar_wait(dkdv_free, (u & 1) ^ 1, p.err, 308)) { ok = false; break; }
+            if (!mbar_wait(p_ready, n & 1, p.err, 309)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < AT_TILE / 16; ++k)
+              umma_ts(tdV, tP + k * 8, smem_desc_sw128(do_addr + k * 2048, 8192, 1024), idesc_kv,
+                      (i == jt && k == 0) ? 0u : 1u);
+            umma_commit(dv_done);
+            pn = n;
+            ps = s;
+            pks = ks;
+            pfirst = (i == jt);
+            plast = (i == nq - 1);
+            pk_addr = k_addr;
+          }
         }
       }
-      fence_proxy_async_smem();
-      named_bar_sync(1, 128);
-      if (leader) {
-        const int grow = bh * p.Tp + (jt + it) * AT_TILE;
-        tma_reduce_add_2d(&maps.dq_acc, sDQ, 0, grow);
-        tma_reduce_add_2d(&maps.dq_acc, sDQ + AT_TILE * 128, 32, grow);
-        bulk_commit();
+      if (ok && pn >= 0) finish_prev();
+    }
+  } else if (warp < 10) {
+    // ---------------- P/dS warps: one key row per thread, 64 queries per warpgroup ----------------
+    const int g = (warp - 2) >> 2;      // query half of the tile
+    const int quarter = warp & 3;       // TMEM lane quarter
+    const int r = quarter * 32 + lane;  // key row within the tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + BA_TM_S + lane_off + g * 64;
+    const uint32_t tdP = tmem + BA_TM_DP + lane_off + g * 64;
+    const uint32_t tP = tmem + BA_TM_P + lane_off + g * 32;
+    uint8_t* dsrow = sDS + g * AT_TILE_BYTES + r * 128;
+    const float sl2 = p.scale_log2;
+    int n = 0;
+    bool ok = true;
+    for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
+      for (int jt = nq - 1; jt >= 0 && ok; --jt) {
+        for (int i = jt; i < nq; ++i, ++n) {
+          const int s = n & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(s_full, n & 1, p.err, 310) &&
+                                           mbar_wait(&q_full[s], (n >> 1) & 1, p.err, 311));
+          if (!ok) break;
+          tc_fence_after();
+          const bool diag = (i == jt);  // key r is visible to query q iff r <= q
+          // ---- P^T = 2^(S^T * scale * log2 e - lse2)
+          // the P^T columns are rewritten once the previous tile's dV MMA has read them
+          ok = __all_sync(0xffffffffu, mbar_wait(dv_done, (n & 1) ^ 1, p.err, 312));
+          if (!ok) break;
+          tc_fence_after();
+          uint32_t pw[32];  // P^T as packed bf16 pairs: what the dV MMA reads, reused for dS
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t a[32];
+            tmem_ld32(tS + c * 32, a);
+            tmem_wait_ld();
+            const float4* l4 = reinterpret_cast<const float4*>(sLse + s * AT_TILE + g * 64 + c * 32);
+            float pr[32];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 lv = l4[j];
+              pr[4 * j + 0] = ex2_approx(fmaf(__uint_as_float(a[4 * j + 0]), sl2, -lv.x));
+              pr[4 * j + 1] = ex2_approx(fmaf(__uint_as_float(a[4 * j + 1]), sl2, -lv.y));
+              pr[4 * j + 2] = ex2_approx(fmaf(__uint_as_float(a[4 * j + 2]), sl2, -lv.z));
+              pr[4 * j + 3] = ex2_approx(fmaf(__uint_as_float(a[4 * j + 3]), sl2, -lv.w));
+            }
+            if (diag) {
+#pragma unroll
+              for (int q = 0; q < 32; ++q)
+                if (g * 64 + c * 32 + q < r) pr[q] = 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pw[c * 16 + j] = pack_bf16x2(pr[2 * j], pr[2 * j + 1]);
+            tmem_st16(tP + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(pw + c * 16));
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(p_ready);
+          // ---- dS^T = P^T (dP^T - delta)
+          ok = __all_sync(0xffffffffu, mbar_wait(dp_full, n & 1, p.err, 313) &&
+                                           mbar_wait(ds_free, (n & 1) ^ 1, p.err, 314));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t a[32];
+            tmem_ld32(tdP + c * 32, a);
+            tmem_wait_ld();
+            const float4* d4 = reinterpret_cast<const float4*>(sDelta + s * AT_TILE + g * 64 + c * 32);
+            uint32_t dk[16];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 dv = d4[j];
+              const uint32_t w0 = pw[c * 16 + 2 * j], w1 = pw[c * 16 + 2 * j + 1];
+              const float d0 = __uint_as_float(w0 << 16) * (__uint_as_float(a[4 * j + 0]) - dv.x);
+              const float d1 = __uint_as_float(w0 & 0xffff0000u) * (__uint_as_float(a[4 * j + 1]) - dv.y);
+              const float d2 = __uint_as_float(w1 << 16) * (__uint_as_float(a[4 * j + 2]) - dv.z);
+              const float d3 = __uint_as_float(w1 & 0xffff0000u) * (__uint_as_float(a[4 * j + 3]) - dv.w);
+              dk[2 * j] = pack_bf16x2(d0, d1);
+              dk[2 * j + 1] = pack_bf16x2(d2, d3);
+            }
+            tmem_st16(tdP + c * 16, dk);  // dS^T over dP^T columns already read
+#pragma unroll
+            for (int u4 = 0; u4 < 4; ++u4) {  // dS^T -> 128B-swizzled [key row][64 queries] block
+              const int ch = c * 4 + u4;
+              *reinterpret_cast<uint4*>(dsrow + ((ch ^ (r & 7)) << 4)) =
+                  make_uint4(dk[4 * u4], dk[4 * u4 + 1], dk[4 * u4 + 2], dk[4 * u4 + 3]);
+            }
+          }
+          tmem_wait_st();
+          fence_proxy_async_smem();
+          tc_fence_before();
+          mbar_arrive(ds_ready);
+        }
+      }
+    }
+  } else {
+    // ---------------- drain warps: dQ per tile, dK/dV per key tile ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // TMEM lane: query row of dQ, key row of dK/dV
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const bool leader = (warp == 10 && lane == 0);
+    float* acc = p.dq_acc + (size_t)blockIdx.x * p.Tp * AT_D;
+    uint32_t sync_phase = 0;
+    auto drain_sync = [&]() -> bool {
+      mbar_arrive(drain_bar);
+      const bool w = mbar_wait(drain_bar, sync_phase & 1, p.err, 315);
+      ++sync_phase;
+      return __all_sync(0xffffffffu, w);
+    };
+    int u = 0, n = 0;
+    bool ok = true;
+    for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
+      const int b = bh / p.NH, h = bh % p.NH;
+      for (int jt = nq - 1; jt >= 0 && ok; --jt, ++u) {
+        for (int i = jt; i < nq; ++i, ++n) {
+          ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, p.err, 316));
+          if (!ok) break;
+          tc_fence_after();
+          uint32_t a0[32], a1[32];
+          tmem_ld32(tmem + BA_TM_DQ + lane_off, a0);
+          tmem_ld32(tmem + BA_TM_DQ + lane_off + 32, a1);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(dq_free);
+          const int qrow = i * AT_TILE + row;
+          if (jt == 0) {
+            // key tile 0 is this query tile's last contribution: finish dQ
+            if (i > 0) {
+              // the accumulator's last reduce-add for tile i came from key tile 1, whose later
+              // tiles i+1 .. nq-1 may still be in flight
+              if (leader) {
+                bulk_wait_upto(nq - 1 - i);
+                fence_proxy_async_global();
+              }
+              if (!(ok = drain_sync())) break;
+              const float4* src = reinterpret_cast<const float4*>(acc + (size_t)qrow * AT_D);
+#pragma unroll
+              for (int c = 0; c < 16; ++c) {
+                const float4 v = src[c];
+                uint32_t* d = c < 8 ? a0 + 4 * c : a1 + 4 * (c - 8);
+                d[0] = __float_as_uint(__uint_as_float(d[0]) + v.x);
+                d[1] = __float_as_uint(__uint_as_float(d[1]) + v.y);
+                d[2] = __float_as_uint(__uint_as_float(d[2]) + v.z);
+                d[3] = __float_as_uint(__uint_as_float(d[3]) + v.w);
+              }
+            }
+            if (qrow < p.T) {
+              uint32_t w[32];
+              pack_row_bf16(w, a0, a1, p.scale);
+              store_packed_row(p.dq + (int64_t)b * p.sb + (int64_t)qrow * p.st + (int64_t)h * p.sh, w);
+            }
+          } else {
+            // an earlier contribution: into the accumulator in L2 (a TMA store from the diagonal
+            // key tile, which reaches query tile i first, reduce-adds after it)
+            if (leader) bulk_wait_read0();  // the previous bulk op has finished reading sDQ
+            if (!(ok = drain_sync())) break;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              uint8_t* rowp = sDQ + hf * (AT_TILE * 128) + row * 128;
+#pragma unroll
+              for (int ch = 0; ch < 8; ++ch) {
+                const uint32_t* src = (hf == 0 ? a0 : a1) + 4 * ch;
+                *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) = make_uint4(src[0], src[1], src[2], src[3]);
+              }
+            }
+            fence_proxy_async_smem();
+            if (!(ok = drain_sync())) break;
+            if (leader) {
+              fence_proxy_async_global();  // earlier generic reads of these rows come first
+              const int grow = blockIdx.x * p.Tp + i * AT_TILE;
+              if (i == jt) {
+                tma_store_2d(&maps.dq_acc, sDQ, 0, grow);
+                tma_store_2d(&maps.dq_acc, sDQ + AT_TILE * 128, 32, grow);
+              } else {
+                tma_reduce_add_2d(&maps.dq_acc, sDQ, 0, grow);
+                tma_reduce_add_2d(&maps.dq_acc, sDQ + AT_TILE * 128, 32, grow);
+              }
+              bulk_commit();
+            }
+          }
+          if (i == nq - 1) {
+            // key tile jt done: dV and scale * dK out
+            ok = __all_sync(0xffffffffu, mbar_wait(dkdv_full, u & 1, p.err, 317));
+            if (!ok) break;
+            tc_fence_after();
+            // dV packed to bf16 first, then dK, so at most 64 fp32 values are live
+            uint32_t pv[32];
+            {
+              uint32_t a0[32], a1[32];
+              tmem_ld32(tmem + BA_TM_DV + lane_off, a0);
+              tmem_ld32(tmem + BA_TM_DV + lane_off + 32, a1);
+              tmem_wait_ld();
+              pack_row_bf16(pv, a0, a1, 1.f);
+            }
+            uint32_t pkk[32];
+            {
+              uint32_t a0[32], a1[32];
+              tmem_ld32(tmem + BA_TM_DK + lane_off, a0);
+              tmem_ld32(tmem + BA_TM_DK + lane_off + 32, a1);
+              tmem_wait_ld();
+              tc_fence_before();
+              mbar_arrive(dkdv_free);
+              pack_row_bf16(pkk, a0, a1, p.scale);
+            }
+            const int key = jt * AT_TILE + row;
+            if (key < p.T) {
+              const int64_t off = (int64_t)b * p.sb + (int64_t)key * p.st + (int64_t)h * p.sh;
+              store_packed_row(p.dv + off, pv);
+              store_packed_row(p.dk + off, pkk);
+            }
+          }
+        }
       }
     }
     if (leader) bulk_wait0();
@@ -365,35 +532,17 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   }
 }
 
-__global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dq,
-                                       int NH, int T, int Tp, int64_t sb, int64_t st, int64_t sh,
-                                       int64_t n8) {
-  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // one thread per 8 elements
-  if (idx >= n8) return;
-  const int c8 = (int)(idx % (AT_D / 8));
-  const int64_t rowi = idx / (AT_D / 8);
-  const int t = (int)(rowi % T);
-  const int64_t bh = rowi / T;
-  const int b = (int)(bh / NH), h = (int)(bh % NH);
-  const float4* src = reinterpret_cast<const float4*>(dq_acc + ((bh * Tp + t) * AT_D + c8 * 8));
-  const float4 a = src[0], c = src[1];
-  uint4 u;
-  u.x = pack_bf16x2(a.x, a.y);
-  u.y = pack_bf16x2(a.z, a.w);
-  u.z = pack_bf16x2(c.x, c.y);
-  u.w = pack_bf16x2(c.z, c.w);
-  *reinterpret_cast<uint4*>(dq + b * sb + (int64_t)t * st + (int64_t)h * sh + c8 * 8) = u;
-}
-
 // ==========================================================================================
 // host side
 // ==========================================================================================
 bool tc_bwd_supported(int D, int dtype) { return D == AT_D && dtype == ATTN_BF16; }
 
+static int bwd_grid(int BH) { return BH < BA_MAX_CTAS ? BH : BA_MAX_CTAS; }
+
 size_t attn_bwd_tc_ws(int B, int NH, int T, int D) {
   const size_t Tp = (size_t)((T + AT_TILE - 1) / AT_TILE) * AT_TILE;
   const size_t BH = (size_t)B * NH;
-  return 2 * align256(BH * Tp * 4) + align256(BH * Tp * D * 4);
+  return 2 * align256(BH * Tp * 4) + align256((size_t)bwd_grid((int)BH) * Tp * D * 4);
 }
 
 int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, const void* dout,
@@ -409,12 +558,14 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   }
   const int nq = (T + AT_TILE - 1) / AT_TILE;
   const int Tp = nq * AT_TILE;
-  const size_t BH = (size_t)B * NH;
+  const int BH = B * NH;
+  const int sms = current_device_sms();
+  int grid = bwd_grid(BH);
+  if (grid > sms) grid = sms;
   uint8_t* w = reinterpret_cast<uint8_t*>(ws);
   float* lse2 = reinterpret_cast<float*>(w);
-  float* delta = reinterpret_cast<float*>(w + align256(BH * Tp * 4));
-  float* dq_acc = reinterpret_cast<float*>(w + 2 * align256(BH * Tp * 4));
-  ATTN_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, BH * Tp * AT_D * 4, stream));
+  float* delta = reinterpret_cast<float*>(w + align256((size_t)BH * Tp * 4));
+  float* dq_acc = reinterpret_cast<float*>(w + 2 * align256((size_t)BH * Tp * 4));
   const int64_t rows = (int64_t)BH * Tp;
   attn_bwd_prep_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
       (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, lse2, delta, NH, T, Tp, s[3], s[4], s[5], rows);
@@ -428,7 +579,7 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
       !make_head_map(&maps.dout, dout, B, NH, T, s[3], s[4], s[5]))
     return ATTN_ERR_CUDA;
   {
-    const uint64_t dims[2] = {(uint64_t)AT_D, (uint64_t)BH * Tp};
+    const uint64_t dims[2] = {(uint64_t)AT_D, (uint64_t)grid * Tp};
     const uint64_t strides[1] = {AT_D * 4};
     const uint32_t box[2] = {32, AT_TILE};
     if (!make_tmap_f32(&maps.dq_acc, dq_acc, 2, dims, strides, box)) return ATTN_ERR_CUDA;
@@ -438,10 +589,13 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   p.T = T;
   p.nq = nq;
   p.Tp = Tp;
+  p.BH = BH;
   p.scale = scale;
   p.scale_log2 = scale * LOG2E;
   p.lse2 = lse2;
   p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.dq = reinterpret_cast<__nv_bfloat16*>(dq);
   p.dk = reinterpret_cast<__nv_bfloat16*>(dk);
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
   p.sb = s[0];
@@ -449,19 +603,11 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   p.sh = s[2];
   p.err = dev_error_ptr();
   if (!p.err) return ATTN_ERR_CUDA;
-  static bool attr = false;
-  if (!attr) {
-    ATTN_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BA_SMEM));
-    attr = true;
-  }
-  attn_bwd_tc_kernel<<<(unsigned)(BH * nq), BA_THREADS, BA_SMEM, stream>>>(maps, p);
+  static uint64_t attr_done = 0;
+  if (!set_smem_limit_once(attn_bwd_tc_kernel, BA_SMEM, attr_done)) return ATTN_ERR_CUDA;
+  attn_bwd_tc_kernel<<<grid, BA_THREADS, BA_SMEM, stream>>>(maps, p);
   count_launch();
-  if (int rc = check_launch("attn_bwd_tc_kernel")) return rc;
-  const int64_t n8 = (int64_t)BH * T * (AT_D / 8);
-  attn_dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, stream>>>(dq_acc, (__nv_bfloat16*)dq, NH, T,
-                                                                          Tp, s[0], s[1], s[2], n8);
-  count_launch();
-  return check_launch("attn_dq_convert_kernel");
+  return check_launch("attn_bwd_tc_kernel");
 }
 
 }  // namespace attn

@@ -1,16 +1,24 @@
 // tcgen05 tensor-core causal attention forward for head_dim 64, bf16 operands, fp32 accumulation.
 //
-// Replaces fused_attention_forward_kernel (core/mha_kernels.py:404-521): one CTA per
-// (b, h, 128-row query tile), two CTAs per SM.  Per 128-key K/V block:
-//   S = Q K^T           tcgen05.mma, A = Q and B = K from shared memory (TMA, 128B swizzle),
-//                       fp32 accumulator in TMEM columns [0,128)
-//   softmax             4 warps, one query row per thread (tcgen05.ld of its TMEM lane): causal
-//                       mask on the diagonal block, row max, 2^(s*scale*log2e - m), row sum; P is
-//                       packed to bf16 and written back over S in TMEM columns [0,64)
-//   O += P V            tcgen05.mma with A = P read from TMEM, B = V (MN-major) from shared
-//                       memory, fp32 accumulator in TMEM columns [128,192)
-// The running max is only moved (and O rescaled in TMEM) when it grows by more than 2^8, so
-// rescaling is rare.  The row's log-sum-exp is written instead of the T x T probabilities.
+// Replaces fused_attention_forward_kernel (core/mha_kernels.py:404-521).  A persistent kernel:
+// one CTA per SM walks a static list of items.  An item is two consecutive 128-row query tiles
+// (A = 2m, B = 2m+1) of one (batch, head); they share one stream of 128-key K/V blocks.  Items
+// are walked in pairs (m, nI-1-m) so that every pair costs the same number of blocks.
+//
+//   MMA thread     per block j: S_X = Q_X K_j^T (X = A, B; tcgen05.mma, A and B operands from
+//                  shared memory, fp32 accumulator in TMEM), then O_X += P_X V_{j-1} for the
+//                  previous block (A = P_X read from TMEM, B = V MN-major from shared memory)
+//   softmax A, B   two warpgroups, one per query tile, one query row per thread: the row of S
+//                  is read from TMEM once (128 columns), causal mask on the diagonal block only,
+//                  row max, 2^(s*scale*log2e - m), row sum; P packed to bf16 into the tile's own
+//                  TMEM P columns, so the next S can be computed while P V runs
+// While one warpgroup computes its softmax the tensor core works for the other, and the two
+// warpgroups give each SM sub-partition two softmax warps.  The running max is only moved (and O
+// rescaled in TMEM) when it grows by more than 2^8, so rescaling is rare.  The row's log-sum-exp
+// is written instead of the T x T probabilities.
+//
+// TMEM columns: S_A [0,128), S_B [128,256), P_A [256,320), P_B [320,384), O_A [384,448),
+// O_B [448,512).
 //
 // Every mbarrier wait is bounded (tc_common.cuh): a wait that gives up sets the library's device
 // error word and the kernel skips its remaining work instead of hanging.
@@ -20,20 +28,18 @@
 
 namespace attn {
 
-// ==========================================================================================
-// forward
-// ==========================================================================================
-constexpr int FA_THREADS = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 softmax/epilogue
-constexpr int FA_STAGES = 2;
-constexpr uint32_t FA_TMEM_COLS = 256;  // S/P [0,128), O [128,192)
-constexpr int FA_SMEM = AT_TILE_BYTES * (1 + 2 * FA_STAGES) + 1024 + 256;
+constexpr int FA_THREADS = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 softmax A, 6-9 softmax B
+constexpr int FA_KV = 3;         // K/V ring stages
+constexpr uint32_t FA_TMEM_COLS = 512;
+constexpr uint32_t FA_TM_S = 0, FA_TM_P = 256, FA_TM_O = 384;
+constexpr int FA_SMEM = 1024 + AT_TILE_BYTES * (4 + 2 * FA_KV) + 256;
 
 struct FwdMaps {
   TileMap q, k, v;
 };
 
 struct FwdParams {
-  int NH, T, nq;
+  int NH, T, nq, n_items, n_units, BH;  // n_items = ceil(nq/2) per head, n_units = ceil(n_items/2)
   float scale_log2;
   __nv_bfloat16* o;
   int64_t o_sb, o_st, o_sh;
@@ -41,39 +47,57 @@ struct FwdParams {
   int* err;
 };
 
-__global__ void __launch_bounds__(FA_THREADS, 2)
+// The item list every role of a CTA walks in the same order: units w = blockIdx.x, +gridDim.x,
+// ...; unit w is head bh = w / n_units with items m = u and n_items-1-u (u = w % n_units; one
+// item when they coincide).  Item m covers query tiles 2m and 2m+1 (tB = -1 past the end).
+// fn(bh, tA, tB) returns false to stop the walk.
+template <typename Fn>
+__device__ __forceinline__ void for_each_item(const FwdParams& p, Fn&& fn) {
+  for (int w = blockIdx.x; w < p.BH * p.n_units; w += gridDim.x) {
+    const int bh = w / p.n_units, u = w % p.n_units;
+    const int m0 = p.n_items - 1 - u, m1 = u;  // the longer item first
+    int tB = 2 * m0 + 1 < p.nq ? 2 * m0 + 1 : -1;
+    if (!fn(bh, 2 * m0, tB)) return;
+    if (m1 != m0) {
+      tB = 2 * m1 + 1 < p.nq ? 2 * m1 + 1 : -1;
+      if (!fn(bh, 2 * m1, tB)) return;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(FA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + AT_TILE_BYTES;                      // [FA_STAGES]
-  uint8_t* sV = sK + FA_STAGES * AT_TILE_BYTES;            // [FA_STAGES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + FA_STAGES * AT_TILE_BYTES);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + FA_STAGES;
-  uint64_t* kv_empty = v_full + FA_STAGES;
-  uint64_t* s_full = kv_empty + FA_STAGES;
-  uint64_t* p_ready = s_full + 1;
-  uint64_t* pv_done = p_ready + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+  uint8_t* sQ = smem;                               // [2 slots][A, B]
+  uint8_t* sK = sQ + 4 * AT_TILE_BYTES;             // [FA_KV]
+  uint8_t* sV = sK + FA_KV * AT_TILE_BYTES;         // [FA_KV]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + FA_KV * AT_TILE_BYTES);
+  uint64_t* q_full = bars;              // [2] per Q slot (both tiles of an item)
+  uint64_t* q_empty = q_full + 2;       // [2]
+  uint64_t* k_full = q_empty + 2;       // [FA_KV]
+  uint64_t* v_full = k_full + FA_KV;    // [FA_KV]
+  uint64_t* kv_empty = v_full + FA_KV;  // [FA_KV]
+  uint64_t* s_full = kv_empty + FA_KV;  // [2] per query tile X: S_X is in TMEM
+  uint64_t* p_ready = s_full + 2;       // [2] S_X read and P_X written (128 arrivals)
+  uint64_t* pv_done = p_ready + 2;      // [2] the P_X V MMA has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int bh = blockIdx.x / p.nq;
-  const int qt = p.nq - 1 - (int)(blockIdx.x % p.nq);  // longest causal rows first within a head
-  const int b = bh / p.NH, h = bh % p.NH;
-  const int n_kv = qt + 1;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < FA_STAGES; ++s) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_ready[s], 128);
+      mbar_init(&pv_done[s], 1);
+    }
+    for (int s = 0; s < FA_KV; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_ready, 128);
-    mbar_init(pv_done, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -84,161 +108,198 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tP = tmem, tO = tmem + 128;
 
   if (warp == 0) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_desc(&maps.q.map);
       tma_prefetch_desc(&maps.k.map);
       tma_prefetch_desc(&maps.v.map);
-      mbar_arrive_expect_tx(q_full, AT_TILE_BYTES);
-      load_tile(sQ, maps.q, q_full, b, h, qt * AT_TILE);
-      bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % FA_STAGES;
-        const uint32_t ph = (j / FA_STAGES) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, p.err, 201)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[st], AT_TILE_BYTES);
-        load_tile(sK + st * AT_TILE_BYTES, maps.k, &k_full[st], b, h, j * AT_TILE);
-        mbar_arrive_expect_tx(&v_full[st], AT_TILE_BYTES);
-        load_tile(sV + st * AT_TILE_BYTES, maps.v, &v_full[st], b, h, j * AT_TILE);
-      }
-      // tail: every stage released by the MMA thread before the CTA may exit
-      for (int j = n_kv; j < n_kv + FA_STAGES && ok; ++j)
-        ok = mbar_wait(&kv_empty[j % FA_STAGES], ((j / FA_STAGES) & 1) ^ 1, p.err, 202);
+      int it = 0, g = 0;
+      for_each_item(p, [&](int bh, int tA, int tB) -> bool {
+        const int b = bh / p.NH, h = bh % p.NH;
+        const int qs = it & 1;
+        if (!mbar_wait(&q_empty[qs], ((it >> 1) & 1) ^ 1, p.err, 201)) return false;
+        mbar_arrive_expect_tx(&q_full[qs], (tB >= 0 ? 2 : 1) * AT_TILE_BYTES);
+        load_tile(sQ + (2 * qs) * AT_TILE_BYTES, maps.q, &q_full[qs], b, h, tA * AT_TILE);
+        if (tB >= 0) load_tile(sQ + (2 * qs + 1) * AT_TILE_BYTES, maps.q, &q_full[qs], b, h, tB * AT_TILE);
+        const int jmax = tB >= 0 ? tB : tA;
+        for (int j = 0; j <= jmax; ++j, ++g) {
+          const int st = g % FA_KV;
+          if (!mbar_wait(&kv_empty[st], ((g / FA_KV) & 1) ^ 1, p.err, 202)) return false;
+          mbar_arrive_expect_tx(&k_full[st], AT_TILE_BYTES);
+          load_tile(sK + st * AT_TILE_BYTES, maps.k, &k_full[st], b, h, j * AT_TILE);
+          mbar_arrive_expect_tx(&v_full[st], AT_TILE_BYTES);
+          load_tile(sV + st * AT_TILE_BYTES, maps.v, &v_full[st], b, h, j * AT_TILE);
+        }
+        ++it;
+        return true;
+      });
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);  // Q K-major, K K-major
       const uint32_t idesc_o = idesc_bf16_f32(128, 64, 0, 1);   // P from TMEM, V MN-major
-      bool ok = mbar_wait(q_full, 0, p.err, 203);
-      const uint32_t q_addr = smem_u32(sQ);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % FA_STAGES;
-        const uint32_t ph = (j / FA_STAGES) & 1;
-        if (!mbar_wait(&k_full[st], ph, p.err, 204)) break;
-        if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, p.err, 205)) break;  // P_{j-1} consumed
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + st * AT_TILE_BYTES);
+      int cnt[2] = {0, 0};  // S MMAs issued per query tile X (= softmax steps of X)
+      int it = 0, g = 0;
+      bool ok = true;
+      for_each_item(p, [&](int bh, int tA, int tB) -> bool {
+        (void)bh;
+        const int qs = it & 1;
+        const int tX[2] = {tA, tB};
+        if (!mbar_wait(&q_full[qs], (it >> 1) & 1, p.err, 203)) return ok = false;
+        const int jmax = tB >= 0 ? tB : tA;
+        // block j: S_X(j) for the tiles that see it, then P_X V_{j-1}; a last pass (j = jmax+1)
+        // issues only the final P V products
+        for (int j = 0; j <= jmax + 1; ++j) {
+          const int st = (g + j) % FA_KV, pst = (g + j - 1) % FA_KV;
+          if (j <= jmax && !mbar_wait(&k_full[st], ((g + j) / FA_KV) & 1, p.err, 204)) return ok = false;
+          if (j > 0 && !mbar_wait(&v_full[pst], ((g + j - 1) / FA_KV) & 1, p.err, 205)) return ok = false;
+          for (int x = 0; x < 2; ++x) {
+            const bool now = j <= tX[x], prev = j >= 1 && j - 1 <= tX[x];
+            if (!now && !prev) continue;
+            // S_X is rewritten (and P_X read by the MMA) once softmax X has finished its step
+            if (cnt[x] > 0 && !mbar_wait(&p_ready[x], (cnt[x] - 1) & 1, p.err, 206)) return ok = false;
+            tc_fence_after();
+            if (now) {
+              const uint32_t q_addr = smem_u32(sQ + (2 * qs + x) * AT_TILE_BYTES);
+              const uint32_t k_addr = smem_u32(sK + st * AT_TILE_BYTES);
+              const uint32_t tS = tmem + FA_TM_S + x * 128;
 #pragma unroll
-        for (int k = 0; k < AT_D / 16; ++k)
-          umma_ss(tS, smem_desc_sw128(q_addr + k * 32, 16, 1024), smem_desc_sw128(k_addr + k * 32, 16, 1024),
-                  idesc_s, k > 0 ? 1u : 0u);
-        umma_commit(s_full);
-        if (!mbar_wait(p_ready, j & 1, p.err, 206)) break;
-        if (!mbar_wait(&v_full[st], ph, p.err, 207)) break;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + st * AT_TILE_BYTES);
+              for (int k = 0; k < AT_D / 16; ++k)
+                umma_ss(tS, smem_desc_sw128(q_addr + k * 32, 16, 1024), smem_desc_sw128(k_addr + k * 32, 16, 1024),
+                        idesc_s, k > 0 ? 1u : 0u);
+              umma_commit(&s_full[x]);
+              ++cnt[x];
+            }
+            if (prev) {
+              const uint32_t v_addr = smem_u32(sV + pst * AT_TILE_BYTES);
+              const uint32_t tP = tmem + FA_TM_P + x * 64, tO = tmem + FA_TM_O + x * 64;
 #pragma unroll
-        for (int k = 0; k < AT_TILE / 16; ++k)
-          umma_ts(tO, tP + k * 8, smem_desc_sw128(v_addr + k * 2048, 8192, 1024), idesc_o,
-                  (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[st]);
-      }
+              for (int k = 0; k < AT_TILE / 16; ++k)
+                umma_ts(tO, tP + k * 8, smem_desc_sw128(v_addr + k * 2048, 8192, 1024), idesc_o,
+                        (j == 1 && k == 0) ? 0u : 1u);
+              umma_commit(&pv_done[x]);
+            }
+          }
+          if (j == jmax) umma_commit(&q_empty[qs]);  // the item's last S MMAs read Q
+          if (j > 0) umma_commit(&kv_empty[pst]);
+        }
+        g += jmax + 1;
+        ++it;
+        return true;
+      });
     }
   } else {
-    // ---------------- softmax warpgroup: one query row per thread ----------------
+    // ---------------- softmax warpgroups: X = 0 (tile A) warps 2-5, X = 1 (tile B) warps 6-9 ----------------
+    const int x = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int grow = qt * AT_TILE + row;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + FA_TM_S + x * 128 + lane_off;
+    const uint32_t tP = tmem + FA_TM_P + x * 64 + lane_off;
+    const uint32_t tO = tmem + FA_TM_O + x * 64 + lane_off;
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, p.err, 208));
-      if (!ok) break;
-      tc_fence_after();
-      const bool diag = (j == qt);
-      // pass 1: row max of the scaled scores (log2 domain)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + lane_off + c * 32, r);
+    int c = 0;  // softmax steps done by this warpgroup
+    for_each_item(p, [&](int bh, int tA, int tB) -> bool {
+      const int t = x == 0 ? tA : tB;
+      if (t < 0) return true;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j <= t; ++j, ++c) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], c & 1, p.err, 207))) return false;
+        tc_fence_after();
+        uint32_t sr[128];
+        tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(sr));
+        tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+        tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+        tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
         tmem_wait_ld();
+        const bool diag = (j == t);
+        if (diag) {  // key column k is visible to query row r iff k <= r
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float s = __uint_as_float(r[i]);
-          const bool masked = diag && (c * 32 + i > row);
-          mx = masked ? mx : fmaxf(mx, s);
+          for (int i = 0; i < 128; ++i)
+            if (i > row) sr[i] = __float_as_uint(-INFINITY);
         }
-      }
-      const float m_cand = mx * sl2;
-      // move the max (and rescale O) only when it grows by more than 8 in log2 units
-      const bool grow_m = (j == 0) || (m_cand > m + 8.0f);
-      if (j > 0 && __any_sync(0xffffffffu, grow_m)) {
-        const float alpha = grow_m ? ex2_approx(m - m_cand) : 1.f;
-        // O holds exactly PV_0..PV_{j-1}: S_j was issued only after PV_{j-1} completed
-        uint32_t o0[32], o1[32];
-        tmem_ld32(tO + lane_off, o0);
-        tmem_ld32(tO + lane_off + 32, o1);
-        tmem_wait_ld();
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
-          o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
+        for (int i = 0; i < 128; i += 8) {
+          mx0 = fmax3(mx0, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
+          mx2 = fmax3(mx2, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
+          mx3 = fmax3(mx3, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
         }
-        uint32_t w[16];
+        const float m_cand = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+        // move the max (and rescale O) only when it grows by more than 8 in log2 units
+        const bool grow_m = (j == 0) || (m_cand > m + 8.0f);
+        const bool rescale = j > 0 && __any_sync(0xffffffffu, grow_m);
+        const float alpha = (j > 0 && grow_m) ? ex2_approx(m - m_cand) : 1.f;
+        if (grow_m) m = m_cand;
+        // P_X and O_X are touched once the previous step's P V has completed
+        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[x], (c - 1) & 1, p.err, 208))) return false;
+        tc_fence_after();
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const uint32_t* src = q4 < 2 ? o0 + 16 * q4 : o1 + 16 * (q4 - 2);
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = src[i];
-          tmem_st16(tO + lane_off + 16 * q4, w);
+          for (int i = 0; i < 32; i += 4) {
+            const float a0 = ex2_approx(fmaf(__uint_as_float(sr[cc * 32 + i]), sl2, -m));
+            const float a1 = ex2_approx(fmaf(__uint_as_float(sr[cc * 32 + i + 1]), sl2, -m));
+            const float a2 = ex2_approx(fmaf(__uint_as_float(sr[cc * 32 + i + 2]), sl2, -m));
+            const float a3 = ex2_approx(fmaf(__uint_as_float(sr[cc * 32 + i + 3]), sl2, -m));
+            s0 += a0;
+            s1 += a1;
+            s2 += a2;
+            s3 += a3;
+            pk[i / 2] = pack_bf16x2(a0, a1);
+            pk[i / 2 + 1] = pack_bf16x2(a2, a3);
+          }
+          tmem_st16(tP + cc * 16, pk);
+        }
+        if (rescale) {  // O *= 2^(m_old - m_new) on the rows whose max moved (before this P V)
+          uint32_t o[64];
+          tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
+          tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 64; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) tmem_st16(tO + 16 * q4, *reinterpret_cast<const uint32_t(*)[16]>(o + 16 * q4));
         }
         l *= alpha;
+        l += (s0 + s1) + (s2 + s3);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[x]);
       }
-      if (grow_m) m = m_cand;
-      // pass 2: probabilities, row sum, P (bf16) over the first 64 columns of S
-      float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + lane_off + c * 32, r);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const bool m0 = diag && (c * 32 + i > row);
-          const bool m1 = diag && (c * 32 + i + 1 > row);
-          const float p0 = m0 ? 0.f : ex2_approx(fmaf(__uint_as_float(r[i]), sl2, -m));
-          const float p1 = m1 ? 0.f : ex2_approx(fmaf(__uint_as_float(r[i + 1]), sl2, -m));
-          sum += p0 + p1;
-          pk[i / 2] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(tP + lane_off + c * 16, pk);
-      }
-      tmem_wait_st();
-      l += sum;
-      tc_fence_before();
-      mbar_arrive(p_ready);
-    }
-    // epilogue: O / l -> bf16 rows, lse = (m + log2 l) * ln 2
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (n_kv - 1) & 1, p.err, 209));
-    if (ok) {
+      // epilogue: O / l -> bf16 rows, lse = (m + log2 l) * ln 2
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[x], (c - 1) & 1, p.err, 209))) return false;
       tc_fence_after();
-      uint32_t o0[32], o1[32];
-      tmem_ld32(tO + lane_off, o0);
-      tmem_ld32(tO + lane_off + 32, o1);
+      uint32_t o[64];
+      tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
+      tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
       tmem_wait_ld();
+      tc_fence_before();
+      const int grow = t * AT_TILE + row;
       if (grow < p.T) {
+        const int b = bh / p.NH, h = bh % p.NH;
         const float inv = 1.f / l;
         __nv_bfloat16* dst = p.o + (int64_t)b * p.o_sb + (int64_t)grow * p.o_st + (int64_t)h * p.o_sh;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t* src = c < 4 ? o0 + 8 * c : o1 + 8 * (c - 4);
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t* src = o + 8 * k;
           uint4 u;
           u.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
           u.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
           u.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
           u.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-          reinterpret_cast<uint4*>(dst)[c] = u;
+          reinterpret_cast<uint4*>(dst)[k] = u;
         }
         p.lse[(int64_t)bh * p.T + grow] = (m + __log2f(l)) * LN2;
       }
-    }
+      return true;
+    });
   }
   tc_fence_before();
   __syncthreads();
@@ -271,6 +332,9 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   p.NH = NH;
   p.T = T;
   p.nq = (T + AT_TILE - 1) / AT_TILE;
+  p.n_items = (p.nq + 1) / 2;
+  p.n_units = (p.n_items + 1) / 2;
+  p.BH = B * NH;
   p.scale_log2 = scale * LOG2E;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.o_sb = s[3];
@@ -279,13 +343,12 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   p.lse = lse;
   p.err = dev_error_ptr();
   if (!p.err) return ATTN_ERR_CUDA;
-  static bool attr = false;
-  if (!attr) {
-    ATTN_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM));
-    attr = true;
-  }
-  const int64_t grid = (int64_t)B * NH * p.nq;
-  attn_fwd_tc_kernel<<<(unsigned)grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);
+  static uint64_t attr_done = 0;
+  if (!set_smem_limit_once(attn_fwd_tc_kernel, FA_SMEM, attr_done)) return ATTN_ERR_CUDA;
+  const int64_t units = (int64_t)p.BH * p.n_units;
+  const int sms = current_device_sms();
+  const int grid = (int)(units < sms ? units : sms);
+  attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);
   count_launch();
   return check_launch("attn_fwd_tc_kernel");
 }

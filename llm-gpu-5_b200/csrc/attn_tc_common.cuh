@@ -55,4 +55,32 @@ inline bool make_head_map(TileMap* tm, const void* base, int B, int NH, int T, i
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Streaming multiprocessors of the current device (cached per device).
+inline int current_device_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+// Raise a kernel's dynamic shared-memory limit once per device; `done` holds one bit per device.
+template <typename Kernel>
+inline bool set_smem_limit_once(Kernel kernel, int bytes, uint64_t& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done & bit) return true;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(MaxDynamicSharedMemorySize=%d) failed: %s", bytes, cudaGetErrorString(e));
+    return false;
+  }
+  done |= bit;
+  return true;
+}
+
 }  // namespace attn

@@ -71,30 +71,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the warp sleeps (issuing nothing) until the phase completes
+// or about `hint_ns` nanoseconds pass, instead of spinning and taking issue slots from the warps
+// that share its scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed.  Gives up after `limit_ns`
 // (default 2 s, far above any legitimate wait in these kernels), records `site` in g_tc_error
 // and returns false; callers then skip their remaining work and fall through to teardown.
-// The poll loop only reads the %globaltimer register; the error word in global memory (another
-// wait having given up) is looked at once per millisecond of waiting, so a wait that completes
-// normally is noticed within one try_wait.
+// Between checks of %globaltimer the warp is suspended in try_wait (at most 0.2 ms per try);
+// the error word in global memory (another wait having given up) is read once per try.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site,
                                           uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  uint64_t next_check = t0 + 1000000ull;
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t now = globaltimer_ns();
-    if (now - t0 > limit_ns) {
+    if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) {
       atomicCAS(err, 0, site);
       return false;
     }
-    if (now > next_check) {
-      if (*(volatile int*)err != 0) return false;  // another wait gave up: stop early
-      next_check = now + 1000000ull;
-    }
+    if (*(volatile int*)err != 0) return false;  // another wait gave up: stop early
   }
 }
 
@@ -176,6 +183,13 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
   return y;
 }
 

@@ -109,7 +109,9 @@ def test_attention_f32_matches_oracle(pkg, cuda_dev, B, NH, T, D, layout):
 
 
 @pytest.mark.parametrize("B,NH,T,D", [(1, 2, 256, 64), (2, 2, 200, 64), (1, 2, 384, 64), (1, 2, 77, 32),
-                                      (2, 3, 130, 16), (1, 2, 1024, 64), (1, 1, 129, 128)])
+                                      (2, 3, 130, 16), (1, 2, 1024, 64), (1, 1, 129, 128),
+                                      # more heads than SMs: the persistent kernels loop over items
+                                      (40, 4, 200, 64), (100, 4, 130, 64)])
 @pytest.mark.parametrize("layout", ["heads", "tokens"])
 def test_attention_bf16_matches_oracle(pkg, cuda_dev, B, NH, T, D, layout):
     q, k, v, do = (_bf16_round(a) for a in _inputs(B, NH, T, D, seed=7 + T + D))
