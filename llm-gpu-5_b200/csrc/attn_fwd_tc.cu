@@ -32,10 +32,10 @@ constexpr int FA_THREADS = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 sof
 constexpr int FA_KV = 3;         // K/V ring stages
 constexpr uint32_t FA_TMEM_COLS = 512;
 constexpr uint32_t FA_TM_S = 0, FA_TM_P = 256, FA_TM_O = 384;
-constexpr int FA_SMEM = 1024 + AT_TILE_BYTES * (4 + 2 * FA_KV) + 256;
+constexpr int FA_SMEM = 1024 + AT_TILE_BYTES * (4 + 2 * FA_KV + 2) + 256;
 
 struct FwdMaps {
-  TileMap q, k, v;
+  TileMap q, k, v, o;
 };
 
 struct FwdParams {
@@ -65,6 +65,36 @@ __device__ __forceinline__ void for_each_item(const FwdParams& p, Fn&& fn) {
   }
 }
 
+// The same walk as an explicit cursor, for the producer, which loads the next item's Q while
+// streaming the current item's K/V blocks.
+struct ItemCursor {
+  int w, second;  // unit index and which item of the unit
+  int bh, tA, tB;
+  __device__ __forceinline__ void set(const FwdParams& p) {
+    const int u = w % p.n_units;
+    const int m = second ? u : p.n_items - 1 - u;
+    bh = w / p.n_units;
+    tA = 2 * m;
+    tB = 2 * m + 1 < p.nq ? 2 * m + 1 : -1;
+  }
+  __device__ __forceinline__ bool valid(const FwdParams& p) const { return w < p.BH * p.n_units; }
+  __device__ __forceinline__ void start(const FwdParams& p) {
+    w = blockIdx.x;
+    second = 0;
+    if (valid(p)) set(p);
+  }
+  __device__ __forceinline__ void next(const FwdParams& p) {
+    const int u = w % p.n_units;
+    if (!second && u != p.n_items - 1 - u) {
+      second = 1;
+    } else {
+      second = 0;
+      w += gridDim.x;
+    }
+    if (valid(p)) set(p);
+  }
+};
+
 __global__ void __launch_bounds__(FA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -72,7 +102,8 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   uint8_t* sQ = smem;                               // [2 slots][A, B]
   uint8_t* sK = sQ + 4 * AT_TILE_BYTES;             // [FA_KV]
   uint8_t* sV = sK + FA_KV * AT_TILE_BYTES;         // [FA_KV]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + FA_KV * AT_TILE_BYTES);
+  uint8_t* sO = sV + FA_KV * AT_TILE_BYTES;         // [2] epilogue staging per softmax warpgroup
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sO + 2 * AT_TILE_BYTES);
   uint64_t* q_full = bars;              // [2] per Q slot (both tiles of an item)
   uint64_t* q_empty = q_full + 2;       // [2]
   uint64_t* k_full = q_empty + 2;       // [FA_KV]
@@ -81,7 +112,8 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   uint64_t* s_full = kv_empty + FA_KV;  // [2] per query tile X: S_X is in TMEM
   uint64_t* p_ready = s_full + 2;       // [2] S_X read and P_X written (128 arrivals)
   uint64_t* pv_done = p_ready + 2;      // [2] the P_X V MMA has completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* wg_bar = pv_done + 2;       // [2] sync of softmax warpgroup X (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wg_bar + 2);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -92,6 +124,7 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       mbar_init(&s_full[s], 1);
       mbar_init(&p_ready[s], 128);
       mbar_init(&pv_done[s], 1);
+      mbar_init(&wg_bar[s], 128);
     }
     for (int s = 0; s < FA_KV; ++s) {
       mbar_init(&k_full[s], 1);
@@ -115,26 +148,37 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       tma_prefetch_desc(&maps.q.map);
       tma_prefetch_desc(&maps.k.map);
       tma_prefetch_desc(&maps.v.map);
-      int it = 0, g = 0;
-      for_each_item(p, [&](int bh, int tA, int tB) -> bool {
-        const int b = bh / p.NH, h = bh % p.NH;
+      auto load_q = [&](const ItemCursor& c, int it) -> bool {
         const int qs = it & 1;
         if (!mbar_wait(&q_empty[qs], ((it >> 1) & 1) ^ 1, p.err, 201)) return false;
-        mbar_arrive_expect_tx(&q_full[qs], (tB >= 0 ? 2 : 1) * AT_TILE_BYTES);
-        load_tile(sQ + (2 * qs) * AT_TILE_BYTES, maps.q, &q_full[qs], b, h, tA * AT_TILE);
-        if (tB >= 0) load_tile(sQ + (2 * qs + 1) * AT_TILE_BYTES, maps.q, &q_full[qs], b, h, tB * AT_TILE);
-        const int jmax = tB >= 0 ? tB : tA;
-        for (int j = 0; j <= jmax; ++j, ++g) {
+        const int b = c.bh / p.NH, h = c.bh % p.NH;
+        mbar_arrive_expect_tx(&q_full[qs], (c.tB >= 0 ? 2 : 1) * AT_TILE_BYTES);
+        load_tile(sQ + (2 * qs) * AT_TILE_BYTES, maps.q, &q_full[qs], b, h, c.tA * AT_TILE);
+        if (c.tB >= 0) load_tile(sQ + (2 * qs + 1) * AT_TILE_BYTES, maps.q, &q_full[qs], b, h, c.tB * AT_TILE);
+        return true;
+      };
+      ItemCursor cur;
+      cur.start(p);
+      bool ok = !cur.valid(p) || load_q(cur, 0);
+      int it = 0, g = 0;
+      while (ok && cur.valid(p)) {
+        ItemCursor nxt = cur;
+        nxt.next(p);
+        const int b = cur.bh / p.NH, h = cur.bh % p.NH;
+        const int jmax = cur.tB >= 0 ? cur.tB : cur.tA;
+        for (int j = 0; j <= jmax && ok; ++j, ++g) {
           const int st = g % FA_KV;
-          if (!mbar_wait(&kv_empty[st], ((g / FA_KV) & 1) ^ 1, p.err, 202)) return false;
+          if (!mbar_wait(&kv_empty[st], ((g / FA_KV) & 1) ^ 1, p.err, 202)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[st], AT_TILE_BYTES);
           load_tile(sK + st * AT_TILE_BYTES, maps.k, &k_full[st], b, h, j * AT_TILE);
           mbar_arrive_expect_tx(&v_full[st], AT_TILE_BYTES);
           load_tile(sV + st * AT_TILE_BYTES, maps.v, &v_full[st], b, h, j * AT_TILE);
+          // the next item's Q, as soon as this item's first block is on its way
+          if (j == 0 && nxt.valid(p) && !load_q(nxt, it + 1)) ok = false;
         }
+        cur = nxt;
         ++it;
-        return true;
-      });
+      }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -202,6 +246,15 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
     const uint32_t tO = tmem + FA_TM_O + x * 64 + lane_off;
     const float sl2 = p.scale_log2;
     int c = 0;  // softmax steps done by this warpgroup
+    const bool leader = (warp & 3) == 2 && lane == 0;  // first warp of the warpgroup
+    bool first_store = true;
+    uint32_t wg_phase = 0;
+    auto wg_sync = [&]() -> bool {  // bounded barrier over the 128 threads of warpgroup X
+      mbar_arrive(&wg_bar[x]);
+      const bool w = mbar_wait(&wg_bar[x], wg_phase & 1, p.err, 210);
+      ++wg_phase;
+      return __all_sync(0xffffffffu, w);
+    };
     for_each_item(p, [&](int bh, int tA, int tB) -> bool {
       const int t = x == 0 ? tA : tB;
       if (t < 0) return true;
@@ -281,26 +334,35 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
       tmem_wait_ld();
       tc_fence_before();
-      const int grow = t * AT_TILE + row;
-      if (grow < p.T) {
-        const int b = bh / p.NH, h = bh % p.NH;
-        const float inv = 1.f / l;
-        __nv_bfloat16* dst = p.o + (int64_t)b * p.o_sb + (int64_t)grow * p.o_st + (int64_t)h * p.o_sh;
+      // O rows -> swizzled staging tile -> one TMA store (rows past T are clipped)
+      const float inv = 1.f / l;
+      uint8_t* stg = sO + x * AT_TILE_BYTES;
+      if (leader && !first_store) bulk_wait_read0();  // the previous store has read the staging tile
+      if (!wg_sync()) return false;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t* src = o + 8 * k;
-          uint4 u;
-          u.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
-          u.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-          u.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
-          u.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-          reinterpret_cast<uint4*>(dst)[k] = u;
-        }
-        p.lse[(int64_t)bh * p.T + grow] = (m + __log2f(l)) * LN2;
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t* src = o + 8 * k;
+        uint4 u;
+        u.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+        u.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+        u.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+        u.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+        *reinterpret_cast<uint4*>(stg + row * 128 + ((k ^ (row & 7)) << 4)) = u;
       }
+      fence_proxy_async_smem();
+      if (!wg_sync()) return false;
+      const int b = bh / p.NH, h = bh % p.NH;
+      if (leader) {
+        store_tile(maps.o, stg, b, h, t * AT_TILE);
+        bulk_commit();
+      }
+      first_store = false;
+      const int grow = t * AT_TILE + row;
+      if (grow < p.T) p.lse[(int64_t)bh * p.T + grow] = (m + __log2f(l)) * LN2;
       return true;
     });
   }
+  if (warp >= 2 && (warp & 3) == 2 && lane == 0) bulk_wait0();  // epilogue stores done with smem
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -326,7 +388,8 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   FwdMaps maps;
   if (!make_head_map(&maps.q, q, B, NH, T, s[0], s[1], s[2]) ||
       !make_head_map(&maps.k, k, B, NH, T, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.v, v, B, NH, T, s[0], s[1], s[2]))
+      !make_head_map(&maps.v, v, B, NH, T, s[0], s[1], s[2]) ||
+      !make_head_map(&maps.o, o, B, NH, T, s[3], s[4], s[5]))
     return ATTN_ERR_CUDA;
   FwdParams p;
   p.NH = NH;

@@ -27,6 +27,14 @@ __device__ __forceinline__ void load_tile(void* dst, const TileMap& tm, uint64_t
     tma_load_4d(dst, &tm.map, bar, 0, t0, h, b);
 }
 
+// Store a 128-row tile (swizzled like load_tile) from shared memory; rows past T are clipped.
+__device__ __forceinline__ void store_tile(const TileMap& tm, const void* src, int b, int h, int t0) {
+  if (tm.h_first)
+    tma_store_4d(&tm.map, src, 0, h, t0, b);
+  else
+    tma_store_4d(&tm.map, src, 0, t0, h, b);
+}
+
 // Element strides usable by TMA: 16-byte multiples and a row pitch of at least one head.
 inline bool head_strides_ok(int64_t sb, int64_t st, int64_t sh) {
   return sb % 8 == 0 && st % 8 == 0 && sh % 8 == 0 && st >= AT_D;
