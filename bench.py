@@ -253,8 +253,7 @@ def run_ours(args, cfg):
         w["global_batch"] = args.batch
         w["name"] += f" [batch overridden to {args.batch}]"
     GB, T, C, NH = w["global_batch"], w["T"], w["C"], w["NH"]
-    assert GB % world == 0, f"global batch {GB} is not divisible by {world} GPUs"
-    B = GB // world
+    _, B = pkg.dp.shard(GB, world, rank)  # this rank's sequences (an even split of the global batch)
     M = B * T
     steps, warmup = args.steps, max(args.warmup, 3)
 

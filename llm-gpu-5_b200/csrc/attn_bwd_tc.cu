@@ -38,13 +38,21 @@
 
 namespace attn {
 
-constexpr int BA_THREADS = 448;  // warp 0 TMA, warp 1 MMA, warps 2-9 P/dS, warps 10-13 drain
+// Four warpgroups: 0 = TMA for K/V (warp 0), MMA (warp 1), TMA for Q/dO (warp 2), one idle warp;
+// 1-2 = P/dS; 3 = drain.
+// Launched at 128 registers per thread (512 threads); warpgroup 0 gives registers back so the
+// P/dS warpgroups can hold more: per SM sub-partition (one warp of each warpgroup)
+// BA_REG_LOW + 2 * BA_REG_PDS + 128 <= 4 x 128.
+constexpr int BA_THREADS = 512;
+constexpr int BA_REG_LOW = 96, BA_REG_PDS = 144;
+static_assert(BA_REG_LOW + 2 * BA_REG_PDS + 128 <= 4 * 128, "register split exceeds the launch allocation");
 constexpr uint32_t BA_TMEM_COLS = 512;
 constexpr uint32_t BA_TM_S = 0, BA_TM_DP = 128, BA_TM_P = 256, BA_TM_DV = 320, BA_TM_DK = 384, BA_TM_DQ = 448;
 constexpr int BA_MAX_CTAS = 160;  // the dQ accumulator workspace is sized for this many CTAs
-constexpr int BA_SMEM = 1024 + 4 * AT_TILE_BYTES /*K,V x2*/ + 4 * AT_TILE_BYTES /*Q,dO x2*/ +
-                        2 * AT_TILE_BYTES /*dS^T*/ + AT_TILE * AT_D * 4 /*dQ staging*/ +
-                        4 * AT_TILE * 4 /*lse2, delta x2*/ + 256;
+constexpr int BA_QS = 3;  // Q / dO / lse2 / delta stages
+constexpr int BA_SMEM = 1024 + 4 * AT_TILE_BYTES /*K,V x2*/ + 2 * BA_QS * AT_TILE_BYTES /*Q,dO*/ +
+                        2 * AT_TILE_BYTES /*dS^T*/ + AT_TILE * 128 /*dQ staging, half a tile*/ +
+                        2 * BA_QS * AT_TILE * 4 /*lse2, delta*/ + 256;
 
 struct BwdMaps {
   TileMap q, k, v, dout;
@@ -138,18 +146,18 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;                          // [2]
   uint8_t* sV = sK + 2 * AT_TILE_BYTES;        // [2]
-  uint8_t* sQ = sV + 2 * AT_TILE_BYTES;        // [2]
-  uint8_t* sDO = sQ + 2 * AT_TILE_BYTES;       // [2]
-  uint8_t* sDS = sDO + 2 * AT_TILE_BYTES;      // dS^T: two 64-query blocks of [128 keys][64]
-  uint8_t* sDQ = sDS + 2 * AT_TILE_BYTES;      // dQ staging: two [128 q][32 fp32] swizzled halves
-  float* sLse = reinterpret_cast<float*>(sDQ + AT_TILE * AT_D * 4);  // [2][128]
-  float* sDelta = sLse + 2 * AT_TILE;                                // [2][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + 2 * AT_TILE);
+  uint8_t* sQ = sV + 2 * AT_TILE_BYTES;        // [BA_QS]
+  uint8_t* sDO = sQ + BA_QS * AT_TILE_BYTES;   // [BA_QS]
+  uint8_t* sDS = sDO + BA_QS * AT_TILE_BYTES;  // dS^T: two 64-query blocks of [128 keys][64]
+  uint8_t* sDQ = sDS + 2 * AT_TILE_BYTES;      // dQ staging: one [128 q][32 fp32] swizzled half
+  float* sLse = reinterpret_cast<float*>(sDQ + AT_TILE * 128);  // [BA_QS][128]
+  float* sDelta = sLse + BA_QS * AT_TILE;                           // [BA_QS][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + BA_QS * AT_TILE);
   uint64_t* kv_full = bars;           // [2] per key tile (unit)
   uint64_t* kv_empty = kv_full + 2;   // [2]
-  uint64_t* q_full = kv_empty + 2;    // [2] per query tile
-  uint64_t* q_empty = q_full + 2;     // [2]
-  uint64_t* s_full = q_empty + 2;     // S^T in TMEM
+  uint64_t* q_full = kv_empty + 2;    // [BA_QS] per query tile
+  uint64_t* q_empty = q_full + BA_QS; // [BA_QS]
+  uint64_t* s_full = q_empty + BA_QS; // S^T in TMEM
   uint64_t* dp_full = s_full + 1;     // dP^T in TMEM
   uint64_t* p_ready = dp_full + 1;    // S^T read, P^T written (256 arrivals)
   uint64_t* dv_done = p_ready + 1;    // the dV MMA reading P^T has completed
@@ -170,6 +178,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < BA_QS; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
     }
@@ -196,123 +206,139 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      tma_prefetch_desc(&maps.q.map);
-      tma_prefetch_desc(&maps.k.map);
-      tma_prefetch_desc(&maps.v.map);
-      tma_prefetch_desc(&maps.dout.map);
-      int u = 0, n = 0;
-      bool ok = true;
-      for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
-        const int b = bh / p.NH, h = bh % p.NH;
-        for (int jt = nq - 1; jt >= 0 && ok; --jt, ++u) {
-          const int ks = u & 1;
-          if (!mbar_wait(&kv_empty[ks], ((u >> 1) & 1) ^ 1, p.err, 301)) { ok = false; break; }
-          mbar_arrive_expect_tx(&kv_full[ks], 2 * AT_TILE_BYTES);
-          load_tile(sK + ks * AT_TILE_BYTES, maps.k, &kv_full[ks], b, h, jt * AT_TILE);
-          load_tile(sV + ks * AT_TILE_BYTES, maps.v, &kv_full[ks], b, h, jt * AT_TILE);
-          for (int i = jt; i < nq; ++i, ++n) {
-            const int s = n & 1;
-            if (!mbar_wait(&q_empty[s], ((n >> 1) & 1) ^ 1, p.err, 302)) { ok = false; break; }
-            const int q0 = i * AT_TILE;
-            mbar_arrive_expect_tx(&q_full[s], 2 * AT_TILE_BYTES + 2 * AT_TILE * 4);
-            load_tile(sQ + s * AT_TILE_BYTES, maps.q, &q_full[s], b, h, q0);
-            load_tile(sDO + s * AT_TILE_BYTES, maps.dout, &q_full[s], b, h, q0);
-            bulk_load(sLse + s * AT_TILE, p.lse2 + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
-            bulk_load(sDelta + s * AT_TILE, p.delta + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
+  if (warp < 4) {  // TMA producers, MMA issuer, one idle warp
+    reg_dealloc<BA_REG_LOW>();
+    if (warp == 0) {
+      // ---------------- TMA producer: K/V per key tile ----------------
+      if (lane == 0) {
+        tma_prefetch_desc(&maps.k.map);
+        tma_prefetch_desc(&maps.v.map);
+        int u = 0;
+        bool ok = true;
+        for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
+          const int b = bh / p.NH, h = bh % p.NH;
+          for (int jt = nq - 1; jt >= 0; --jt, ++u) {
+            const int ks = u & 1;
+            if (!mbar_wait(&kv_empty[ks], ((u >> 1) & 1) ^ 1, p.err, 301)) { ok = false; break; }
+            mbar_arrive_expect_tx(&kv_full[ks], 2 * AT_TILE_BYTES);
+            load_tile(sK + ks * AT_TILE_BYTES, maps.k, &kv_full[ks], b, h, jt * AT_TILE);
+            load_tile(sV + ks * AT_TILE_BYTES, maps.v, &kv_full[ks], b, h, jt * AT_TILE);
           }
         }
       }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc_sdp = idesc_bf16_f32(128, 128, 0, 0);  // K/V and Q/dO all K-major
-      const uint32_t idesc_kv = idesc_bf16_f32(128, 64, 0, 1);    // A from TMEM, B MN-major
-      const uint32_t idesc_q = idesc_bf16_f32(128, 64, 1, 1);     // A = dS (MN-major), B = K MN-major
-      const uint32_t tS = tmem + BA_TM_S, tdP = tmem + BA_TM_DP, tP = tmem + BA_TM_P;
-      const uint32_t tdV = tmem + BA_TM_DV, tdK = tmem + BA_TM_DK, tdQ = tmem + BA_TM_DQ;
-      const uint32_t ds_addr = smem_u32(sDS);
-      // the previous tile's dK and dQ are issued after this tile's S^T
-      int pn = -1, ps = 0, pks = 0;
-      bool pfirst = false, plast = false;
-      uint32_t pk_addr = 0;
-      auto finish_prev = [&]() -> bool {
-        if (!mbar_wait(ds_ready, pn & 1, p.err, 303)) return false;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + ps * AT_TILE_BYTES);
-#pragma unroll
-        for (int k = 0; k < AT_TILE / 16; ++k)  // dK += dS^T Q   (k over the 128 queries)
-          umma_ts(tdK, tdP + (k >> 2) * 64 + (k & 3) * 8, smem_desc_sw128(q_addr + k * 2048, 8192, 1024),
-                  idesc_kv, (pfirst && k == 0) ? 0u : 1u);
-        umma_commit(dk_done);
-        if (!mbar_wait(dq_free, (pn & 1) ^ 1, p.err, 304)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < AT_TILE / 16; ++k)  // dQ = dS K   (k over the 128 keys)
-          umma_ss(tdQ, smem_desc_sw128(ds_addr + k * 2048, 16384, 1024),
-                  smem_desc_sw128(pk_addr + k * 2048, 8192, 1024), idesc_q, k > 0 ? 1u : 0u);
-        umma_commit(dq_full);
-        umma_commit(ds_free);
-        umma_commit(&q_empty[ps]);
-        if (plast) {
-          umma_commit(dkdv_full);
-          umma_commit(&kv_empty[pks]);
-        }
-        return true;
-      };
-      int u = 0, n = 0;
-      bool ok = true;
-      for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
-        for (int jt = nq - 1; jt >= 0 && ok; --jt, ++u) {
-          const int ks = u & 1;
-          if (!mbar_wait(&kv_full[ks], (u >> 1) & 1, p.err, 305)) { ok = false; break; }
-          const uint32_t k_addr = smem_u32(sK + ks * AT_TILE_BYTES), v_addr = smem_u32(sV + ks * AT_TILE_BYTES);
-          for (int i = jt; i < nq; ++i, ++n) {
-            const int s = n & 1;
-            if (!mbar_wait(&q_full[s], (n >> 1) & 1, p.err, 306)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t q_addr = smem_u32(sQ + s * AT_TILE_BYTES), do_addr = smem_u32(sDO + s * AT_TILE_BYTES);
-            // S^T = K Q^T: the P/dS warps finished reading the previous S^T (p_ready waited below)
-#pragma unroll
-            for (int k = 0; k < AT_D / 16; ++k)
-              umma_ss(tS, smem_desc_sw128(k_addr + k * 32, 16, 1024), smem_desc_sw128(q_addr + k * 32, 16, 1024),
-                      idesc_sdp, k > 0 ? 1u : 0u);
-            umma_commit(s_full);
-            if (pn >= 0 && !finish_prev()) { ok = false; break; }
-            // dP^T = V dO^T over the previous dS^T: wait for the dK MMA that reads it
-            if (!mbar_wait(dk_done, (n & 1) ^ 1, p.err, 307)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int k = 0; k < AT_D / 16; ++k)
-              umma_ss(tdP, smem_desc_sw128(v_addr + k * 32, 16, 1024), smem_desc_sw128(do_addr + k * 32, 16, 1024),
-                      idesc_sdp, k > 0 ? 1u : 0u);
-            umma_commit(dp_full);
-            // dV += P^T dO (the first tile of a key tile starts dV/dK afresh once drained)
-            if (i == jt && !mbar_wait(dkdv_free, (u & 1) ^ 1, p.err, 308)) { ok = false; break; }
-            if (!mbar_wait(p_ready, n & 1, p.err, 309)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int k = 0; k < AT_TILE / 16; ++k)
-              umma_ts(tdV, tP + k * 8, smem_desc_sw128(do_addr + k * 2048, 8192, 1024), idesc_kv,
-                      (i == jt && k == 0) ? 0u : 1u);
-            umma_commit(dv_done);
-            pn = n;
-            ps = s;
-            pks = ks;
-            pfirst = (i == jt);
-            plast = (i == nq - 1);
-            pk_addr = k_addr;
+    } else if (warp == 2) {
+      // ---------------- TMA producer: Q, dO, lse2, delta per query tile (runs ahead of K/V) ----------------
+      if (lane == 0) {
+        tma_prefetch_desc(&maps.q.map);
+        tma_prefetch_desc(&maps.dout.map);
+        int n = 0;
+        bool ok = true;
+        for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
+          const int b = bh / p.NH, h = bh % p.NH;
+          for (int jt = nq - 1; jt >= 0 && ok; --jt) {
+            for (int i = jt; i < nq; ++i, ++n) {
+              const int s = n % BA_QS;
+              if (!mbar_wait(&q_empty[s], ((n / BA_QS) & 1) ^ 1, p.err, 302)) { ok = false; break; }
+              const int q0 = i * AT_TILE;
+              mbar_arrive_expect_tx(&q_full[s], 2 * AT_TILE_BYTES + 2 * AT_TILE * 4);
+              load_tile(sQ + s * AT_TILE_BYTES, maps.q, &q_full[s], b, h, q0);
+              load_tile(sDO + s * AT_TILE_BYTES, maps.dout, &q_full[s], b, h, q0);
+              bulk_load(sLse + s * AT_TILE, p.lse2 + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
+              bulk_load(sDelta + s * AT_TILE, p.delta + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
+            }
           }
         }
       }
-      if (ok && pn >= 0) finish_prev();
+    } else if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      if (lane == 0) {
+        const uint32_t idesc_sdp = idesc_bf16_f32(128, 128, 0, 0);  // K/V and Q/dO all K-major
+        const uint32_t idesc_kv = idesc_bf16_f32(128, 64, 0, 1);    // A from TMEM, B MN-major
+        const uint32_t idesc_q = idesc_bf16_f32(128, 64, 1, 1);     // A = dS (MN-major), B = K MN-major
+        const uint32_t tS = tmem + BA_TM_S, tdP = tmem + BA_TM_DP, tP = tmem + BA_TM_P;
+        const uint32_t tdV = tmem + BA_TM_DV, tdK = tmem + BA_TM_DK, tdQ = tmem + BA_TM_DQ;
+        // shared-memory descriptors: K-major (row = 64 elements of the contraction) and MN-major
+        // (row = 64 output columns), built per use from the stage's base address
+        auto kmaj = [](const uint8_t* t) { return smem_desc_sw128(smem_u32(t), 16, 1024); };
+        auto mnmaj = [](const uint8_t* t) { return smem_desc_sw128(smem_u32(t), 8192, 1024); };
+        // The previous tile's dV, dK and dQ are issued after this tile's S^T, which goes to the tensor
+        // core as soon as the P/dS warps have read the previous S^T.
+        int pn = -1, ps = 0, pks = 0, pu = 0;
+        bool pfirst = false, plast = false;
+        auto finish_prev = [&]() -> bool {
+          // dV += P^T dO   (the first tile of a key tile starts dV/dK afresh once they are drained)
+          if (pfirst && !mbar_wait(dkdv_free, (pu & 1) ^ 1, p.err, 308)) return false;
+          tc_fence_after();
+          const uint64_t do_mn = mnmaj(sDO + ps * AT_TILE_BYTES);
+  #pragma unroll
+          for (int k = 0; k < AT_TILE / 16; ++k)
+            umma_ts(tdV, tP + k * 8, desc_step(do_mn, k * 2048), idesc_kv, (pfirst && k == 0) ? 0u : 1u);
+          umma_commit(dv_done);
+          if (!mbar_wait(ds_ready, pn & 1, p.err, 303)) return false;
+          tc_fence_after();
+          const uint64_t q_mn = mnmaj(sQ + ps * AT_TILE_BYTES), k_mn = mnmaj(sK + pks * AT_TILE_BYTES);
+          const uint64_t ds_mn = smem_desc_sw128(smem_u32(sDS), 16384, 1024);  // two 64-query blocks
+  #pragma unroll
+          for (int k = 0; k < AT_TILE / 16; ++k)  // dK += dS^T Q   (k over the 128 queries)
+            umma_ts(tdK, tdP + (k >> 2) * 64 + (k & 3) * 8, desc_step(q_mn, k * 2048),
+                    idesc_kv, (pfirst && k == 0) ? 0u : 1u);
+          umma_commit(dk_done);
+          umma_commit(&q_empty[ps]);  // dK was the last MMA to read Q (and dV the last for dO)
+          if (!mbar_wait(dq_free, (pn & 1) ^ 1, p.err, 304)) return false;
+          tc_fence_after();
+  #pragma unroll
+          for (int k = 0; k < AT_TILE / 16; ++k)  // dQ = dS K   (k over the 128 keys)
+            umma_ss(tdQ, desc_step(ds_mn, k * 2048), desc_step(k_mn, k * 2048), idesc_q, k > 0 ? 1u : 0u);
+          umma_commit(dq_full);
+          umma_commit(ds_free);
+          if (plast) {
+            umma_commit(dkdv_full);
+            umma_commit(&kv_empty[pks]);
+          }
+          return true;
+        };
+        int u = 0, n = 0;
+        bool ok = true;
+        for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
+          for (int jt = nq - 1; jt >= 0 && ok; --jt, ++u) {
+            const int ks = u & 1;
+            if (!mbar_wait(&kv_full[ks], (u >> 1) & 1, p.err, 305)) { ok = false; break; }
+            const uint64_t k_k = kmaj(sK + ks * AT_TILE_BYTES), v_k = kmaj(sV + ks * AT_TILE_BYTES);
+            for (int i = jt; i < nq; ++i, ++n) {
+              const int s = n % BA_QS;
+              if (!mbar_wait(&q_full[s], (n / BA_QS) & 1, p.err, 306)) { ok = false; break; }
+              // S^T = K Q^T once the P/dS warps have read the previous S^T (and written its P^T)
+              if (pn >= 0 && !mbar_wait(p_ready, pn & 1, p.err, 309)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t q_k = kmaj(sQ + s * AT_TILE_BYTES), do_k = kmaj(sDO + s * AT_TILE_BYTES);
+  #pragma unroll
+              for (int k = 0; k < AT_D / 16; ++k)
+                umma_ss(tS, desc_step(k_k, k * 32), desc_step(q_k, k * 32), idesc_sdp, k > 0 ? 1u : 0u);
+              umma_commit(s_full);
+              if (pn >= 0 && !finish_prev()) { ok = false; break; }
+              // dP^T = V dO^T over the previous dS^T: wait for the dK MMA that reads it
+              if (!mbar_wait(dk_done, (n & 1) ^ 1, p.err, 307)) { ok = false; break; }
+              tc_fence_after();
+  #pragma unroll
+              for (int k = 0; k < AT_D / 16; ++k)
+                umma_ss(tdP, desc_step(v_k, k * 32), desc_step(do_k, k * 32), idesc_sdp, k > 0 ? 1u : 0u);
+              umma_commit(dp_full);
+              pn = n;
+              ps = s;
+              pks = ks;
+              pu = u;
+              pfirst = (i == jt);
+              plast = (i == nq - 1);
+            }
+          }
+        }
+        if (ok && pn >= 0 && mbar_wait(p_ready, pn & 1, p.err, 309)) finish_prev();
+      }
     }
-  } else if (warp < 10) {
+  } else if (warp < 12) {
+    reg_alloc<BA_REG_PDS>();
     // ---------------- P/dS warps: one key row per thread, 64 queries per warpgroup ----------------
-    const int g = (warp - 2) >> 2;      // query half of the tile
+    const int g = (warp - 4) >> 2;      // query half of the tile
     const int quarter = warp & 3;       // TMEM lane quarter
     const int r = quarter * 32 + lane;  // key row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -326,9 +352,9 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
     for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
       for (int jt = nq - 1; jt >= 0 && ok; --jt) {
         for (int i = jt; i < nq; ++i, ++n) {
-          const int s = n & 1;
+          const int s = n % BA_QS;
           ok = __all_sync(0xffffffffu, mbar_wait(s_full, n & 1, p.err, 310) &&
-                                           mbar_wait(&q_full[s], (n >> 1) & 1, p.err, 311));
+                                           mbar_wait(&q_full[s], (n / BA_QS) & 1, p.err, 311));
           if (!ok) break;
           tc_fence_after();
           const bool diag = (i == jt);  // key r is visible to query q iff r <= q
@@ -338,30 +364,37 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           if (!ok) break;
           tc_fence_after();
           uint32_t pw[32];  // P^T as packed bf16 pairs: what the dV MMA reads, reused for dS
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t a[32];
-            tmem_ld32(tS + c * 32, a);
+          {
+            uint32_t a0[32], a1[32];  // both TMEM loads in flight before one wait
+            tmem_ld32(tS, a0);
+            tmem_ld32(tS + 32, a1);
             tmem_wait_ld();
-            const float4* l4 = reinterpret_cast<const float4*>(sLse + s * AT_TILE + g * 64 + c * 32);
-            float pr[32];
+            const float4* l4 = reinterpret_cast<const float4*>(sLse + s * AT_TILE + g * 64);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 16; ++j) {
               const float4 lv = l4[j];
-              pr[4 * j + 0] = ex2_approx(fmaf(__uint_as_float(a[4 * j + 0]), sl2, -lv.x));
-              pr[4 * j + 1] = ex2_approx(fmaf(__uint_as_float(a[4 * j + 1]), sl2, -lv.y));
-              pr[4 * j + 2] = ex2_approx(fmaf(__uint_as_float(a[4 * j + 2]), sl2, -lv.z));
-              pr[4 * j + 3] = ex2_approx(fmaf(__uint_as_float(a[4 * j + 3]), sl2, -lv.w));
+              const uint32_t* src = (j < 8 ? a0 : a1) + 4 * (j & 7);
+              float p0 = ex2_approx(fmaf(__uint_as_float(src[0]), sl2, -lv.x));
+              float p1 = ex2_approx(fmaf(__uint_as_float(src[1]), sl2, -lv.y));
+              float p2 = ex2_approx(fmaf(__uint_as_float(src[2]), sl2, -lv.z));
+              float p3 = ex2_approx(fmaf(__uint_as_float(src[3]), sl2, -lv.w));
+              if (diag) {
+                const int q = g * 64 + 4 * j;
+                if (q < r) p0 = 0.f;
+                if (q + 1 < r) p1 = 0.f;
+                if (q + 2 < r) p2 = 0.f;
+                if (q + 3 < r) p3 = 0.f;
+              }
+              pw[2 * j] = pack_bf16x2(p0, p1);
+              pw[2 * j + 1] = pack_bf16x2(p2, p3);
             }
-            if (diag) {
-#pragma unroll
-              for (int q = 0; q < 32; ++q)
-                if (g * 64 + c * 32 + q < r) pr[q] = 0.f;
-            }
-#pragma unroll
-            for (int j = 0; j < 16; ++j) pw[c * 16 + j] = pack_bf16x2(pr[2 * j], pr[2 * j + 1]);
-            tmem_st16(tP + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(pw + c * 16));
           }
+          // the P^T columns are rewritten once the previous tile's dV MMA has read them
+          ok = __all_sync(0xffffffffu, mbar_wait(dv_done, (n & 1) ^ 1, p.err, 312));
+          if (!ok) break;
+          tc_fence_after();
+          tmem_st16(tP, *reinterpret_cast<const uint32_t(*)[16]>(pw));
+          tmem_st16(tP + 16, *reinterpret_cast<const uint32_t(*)[16]>(pw + 16));
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(p_ready);
@@ -370,30 +403,34 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
                                            mbar_wait(ds_free, (n & 1) ^ 1, p.err, 314));
           if (!ok) break;
           tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t a[32];
-            tmem_ld32(tdP + c * 32, a);
+          {
+            uint32_t a0[32], a1[32];
+            tmem_ld32(tdP, a0);
+            tmem_ld32(tdP + 32, a1);
             tmem_wait_ld();
-            const float4* d4 = reinterpret_cast<const float4*>(sDelta + s * AT_TILE + g * 64 + c * 32);
-            uint32_t dk[16];
+            const float4* d4 = reinterpret_cast<const float4*>(sDelta + s * AT_TILE + g * 64);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 dv = d4[j];
-              const uint32_t w0 = pw[c * 16 + 2 * j], w1 = pw[c * 16 + 2 * j + 1];
-              const float d0 = __uint_as_float(w0 << 16) * (__uint_as_float(a[4 * j + 0]) - dv.x);
-              const float d1 = __uint_as_float(w0 & 0xffff0000u) * (__uint_as_float(a[4 * j + 1]) - dv.y);
-              const float d2 = __uint_as_float(w1 << 16) * (__uint_as_float(a[4 * j + 2]) - dv.z);
-              const float d3 = __uint_as_float(w1 & 0xffff0000u) * (__uint_as_float(a[4 * j + 3]) - dv.w);
-              dk[2 * j] = pack_bf16x2(d0, d1);
-              dk[2 * j + 1] = pack_bf16x2(d2, d3);
-            }
-            tmem_st16(tdP + c * 16, dk);  // dS^T over dP^T columns already read
+            for (int c = 0; c < 2; ++c) {
+              uint32_t dk[16];
 #pragma unroll
-            for (int u4 = 0; u4 < 4; ++u4) {  // dS^T -> 128B-swizzled [key row][64 queries] block
-              const int ch = c * 4 + u4;
-              *reinterpret_cast<uint4*>(dsrow + ((ch ^ (r & 7)) << 4)) =
-                  make_uint4(dk[4 * u4], dk[4 * u4 + 1], dk[4 * u4 + 2], dk[4 * u4 + 3]);
+              for (int j = 0; j < 8; ++j) {
+                const float4 dv = d4[c * 8 + j];
+                const uint32_t* src = (c == 0 ? a0 : a1) + 4 * j;
+                const uint32_t w0 = pw[c * 16 + 2 * j], w1 = pw[c * 16 + 2 * j + 1];
+                const float d0 = __uint_as_float(w0 << 16) * (__uint_as_float(src[0]) - dv.x);
+                const float d1 = __uint_as_float(w0 & 0xffff0000u) * (__uint_as_float(src[1]) - dv.y);
+                const float d2 = __uint_as_float(w1 << 16) * (__uint_as_float(src[2]) - dv.z);
+                const float d3 = __uint_as_float(w1 & 0xffff0000u) * (__uint_as_float(src[3]) - dv.w);
+                dk[2 * j] = pack_bf16x2(d0, d1);
+                dk[2 * j + 1] = pack_bf16x2(d2, d3);
+              }
+              tmem_st16(tdP + c * 16, dk);  // dS^T over dP^T columns already read
+#pragma unroll
+              for (int u4 = 0; u4 < 4; ++u4) {  // dS^T -> 128B-swizzled [key row][64 queries] block
+                const int ch = c * 4 + u4;
+                *reinterpret_cast<uint4*>(dsrow + ((ch ^ (r & 7)) << 4)) =
+                    make_uint4(dk[4 * u4], dk[4 * u4 + 1], dk[4 * u4 + 2], dk[4 * u4 + 3]);
+              }
             }
           }
           tmem_wait_st();
@@ -408,7 +445,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane: query row of dQ, key row of dK/dV
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const bool leader = (warp == 10 && lane == 0);
+    const bool leader = (warp == 12 && lane == 0);
     float* acc = p.dq_acc + (size_t)blockIdx.x * p.Tp * AT_D;
     uint32_t sync_phase = 0;
     auto drain_sync = [&]() -> bool {
@@ -423,73 +460,9 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
       const int b = bh / p.NH, h = bh % p.NH;
       for (int jt = nq - 1; jt >= 0 && ok; --jt, ++u) {
         for (int i = jt; i < nq; ++i, ++n) {
-          ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, p.err, 316));
-          if (!ok) break;
-          tc_fence_after();
-          uint32_t a0[32], a1[32];
-          tmem_ld32(tmem + BA_TM_DQ + lane_off, a0);
-          tmem_ld32(tmem + BA_TM_DQ + lane_off + 32, a1);
-          tmem_wait_ld();
-          tc_fence_before();
-          mbar_arrive(dq_free);
-          const int qrow = i * AT_TILE + row;
-          if (jt == 0) {
-            // key tile 0 is this query tile's last contribution: finish dQ
-            if (i > 0) {
-              // the accumulator's last reduce-add for tile i came from key tile 1, whose later
-              // tiles i+1 .. nq-1 may still be in flight
-              if (leader) {
-                bulk_wait_upto(nq - 1 - i);
-                fence_proxy_async_global();
-              }
-              if (!(ok = drain_sync())) break;
-              const float4* src = reinterpret_cast<const float4*>(acc + (size_t)qrow * AT_D);
-#pragma unroll
-              for (int c = 0; c < 16; ++c) {
-                const float4 v = src[c];
-                uint32_t* d = c < 8 ? a0 + 4 * c : a1 + 4 * (c - 8);
-                d[0] = __float_as_uint(__uint_as_float(d[0]) + v.x);
-                d[1] = __float_as_uint(__uint_as_float(d[1]) + v.y);
-                d[2] = __float_as_uint(__uint_as_float(d[2]) + v.z);
-                d[3] = __float_as_uint(__uint_as_float(d[3]) + v.w);
-              }
-            }
-            if (qrow < p.T) {
-              uint32_t w[32];
-              pack_row_bf16(w, a0, a1, p.scale);
-              store_packed_row(p.dq + (int64_t)b * p.sb + (int64_t)qrow * p.st + (int64_t)h * p.sh, w);
-            }
-          } else {
-            // an earlier contribution: into the accumulator in L2 (a TMA store from the diagonal
-            // key tile, which reaches query tile i first, reduce-adds after it)
-            if (leader) bulk_wait_read0();  // the previous bulk op has finished reading sDQ
-            if (!(ok = drain_sync())) break;
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-              uint8_t* rowp = sDQ + hf * (AT_TILE * 128) + row * 128;
-#pragma unroll
-              for (int ch = 0; ch < 8; ++ch) {
-                const uint32_t* src = (hf == 0 ? a0 : a1) + 4 * ch;
-                *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) = make_uint4(src[0], src[1], src[2], src[3]);
-              }
-            }
-            fence_proxy_async_smem();
-            if (!(ok = drain_sync())) break;
-            if (leader) {
-              fence_proxy_async_global();  // earlier generic reads of these rows come first
-              const int grow = blockIdx.x * p.Tp + i * AT_TILE;
-              if (i == jt) {
-                tma_store_2d(&maps.dq_acc, sDQ, 0, grow);
-                tma_store_2d(&maps.dq_acc, sDQ + AT_TILE * 128, 32, grow);
-              } else {
-                tma_reduce_add_2d(&maps.dq_acc, sDQ, 0, grow);
-                tma_reduce_add_2d(&maps.dq_acc, sDQ + AT_TILE * 128, 32, grow);
-              }
-              bulk_commit();
-            }
-          }
           if (i == nq - 1) {
-            // key tile jt done: dV and scale * dK out
+            // key tile jt done: dV and scale * dK out first (committed together with this
+            // tile's dQ), so the next key tile can start accumulating while dQ is drained
             ok = __all_sync(0xffffffffu, mbar_wait(dkdv_full, u & 1, p.err, 317));
             if (!ok) break;
             tc_fence_after();
@@ -518,6 +491,70 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
               store_packed_row(p.dv + off, pv);
               store_packed_row(p.dk + off, pkk);
             }
+          }
+          ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, p.err, 316));
+          if (!ok) break;
+          tc_fence_after();
+          uint32_t a0[32], a1[32];
+          tmem_ld32(tmem + BA_TM_DQ + lane_off, a0);
+          tmem_ld32(tmem + BA_TM_DQ + lane_off + 32, a1);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(dq_free);
+          const int qrow = i * AT_TILE + row;
+if (jt == 0) {
+            // key tile 0 is this query tile's last contribution: finish dQ
+            if (i > 0) {
+              // the accumulator's last reduce-add for tile i came from key tile 1, whose later
+              // tiles i+1 .. nq-1 may still be in flight
+              if (leader) {
+                bulk_wait_upto(2 * (nq - 1 - i));  // two bulk groups (halves) per tile
+                fence_proxy_async_global();
+              }
+              if (!(ok = drain_sync())) break;
+              const float4* src = reinterpret_cast<const float4*>(acc + (size_t)qrow * AT_D);
+#pragma unroll
+              for (int c = 0; c < 16; ++c) {
+                const float4 v = src[c];
+                uint32_t* d = c < 8 ? a0 + 4 * c : a1 + 4 * (c - 8);
+                d[0] = __float_as_uint(__uint_as_float(d[0]) + v.x);
+                d[1] = __float_as_uint(__uint_as_float(d[1]) + v.y);
+                d[2] = __float_as_uint(__uint_as_float(d[2]) + v.z);
+                d[3] = __float_as_uint(__uint_as_float(d[3]) + v.w);
+              }
+            }
+            if (qrow < p.T) {
+              uint32_t w[32];
+              pack_row_bf16(w, a0, a1, p.scale);
+              store_packed_row(p.dq + (int64_t)b * p.sb + (int64_t)qrow * p.st + (int64_t)h * p.sh, w);
+            }
+          } else {
+            // an earlier contribution: into the accumulator in L2 (a TMA store from the diagonal
+            // key tile, which reaches query tile i first, reduce-adds after it)
+            // two halves (d 0..31, 32..63) through the one staging buffer
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              if (leader) bulk_wait_read0();  // the previous bulk op has finished reading sDQ
+              if (!(ok = drain_sync())) break;
+              uint8_t* rowp = sDQ + row * 128;
+#pragma unroll
+              for (int ch = 0; ch < 8; ++ch) {
+                const uint32_t* src = (hf == 0 ? a0 : a1) + 4 * ch;
+                *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) = make_uint4(src[0], src[1], src[2], src[3]);
+              }
+              fence_proxy_async_smem();
+              if (!(ok = drain_sync())) break;
+              if (leader) {
+                if (hf == 0) fence_proxy_async_global();  // earlier generic reads of these rows come first
+                const int grow = blockIdx.x * p.Tp + i * AT_TILE;
+                if (i == jt)
+                  tma_store_2d(&maps.dq_acc, sDQ, 32 * hf, grow);
+                else
+                  tma_reduce_add_2d(&maps.dq_acc, sDQ, 32 * hf, grow);
+                bulk_commit();
+              }
+            }
+            if (!ok) break;
           }
         }
       }

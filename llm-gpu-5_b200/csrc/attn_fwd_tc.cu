@@ -207,22 +207,22 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
             if (cnt[x] > 0 && !mbar_wait(&p_ready[x], (cnt[x] - 1) & 1, p.err, 206)) return ok = false;
             tc_fence_after();
             if (now) {
-              const uint32_t q_addr = smem_u32(sQ + (2 * qs + x) * AT_TILE_BYTES);
-              const uint32_t k_addr = smem_u32(sK + st * AT_TILE_BYTES);
+              const uint64_t q_desc = smem_desc_sw128(smem_u32(sQ + (2 * qs + x) * AT_TILE_BYTES), 16, 1024);
+              const uint64_t k_desc = smem_desc_sw128(smem_u32(sK + st * AT_TILE_BYTES), 16, 1024);
               const uint32_t tS = tmem + FA_TM_S + x * 128;
 #pragma unroll
               for (int k = 0; k < AT_D / 16; ++k)
-                umma_ss(tS, smem_desc_sw128(q_addr + k * 32, 16, 1024), smem_desc_sw128(k_addr + k * 32, 16, 1024),
+                umma_ss(tS, desc_step(q_desc, k * 32), desc_step(k_desc, k * 32),
                         idesc_s, k > 0 ? 1u : 0u);
               umma_commit(&s_full[x]);
               ++cnt[x];
             }
             if (prev) {
-              const uint32_t v_addr = smem_u32(sV + pst * AT_TILE_BYTES);
+              const uint64_t v_desc = smem_desc_sw128(smem_u32(sV + pst * AT_TILE_BYTES), 8192, 1024);
               const uint32_t tP = tmem + FA_TM_P + x * 64, tO = tmem + FA_TM_O + x * 64;
 #pragma unroll
               for (int k = 0; k < AT_TILE / 16; ++k)
-                umma_ts(tO, tP + k * 8, smem_desc_sw128(v_addr + k * 2048, 8192, 1024), idesc_o,
+                umma_ts(tO, tP + k * 8, desc_step(v_desc, k * 2048), idesc_o,
                         (j == 1 && k == 0) ? 0u : 1u);
               umma_commit(&pv_done[x]);
             }

@@ -186,6 +186,18 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Warpgroup register reallocation (all four warps of a warpgroup execute the same one).  The
+// amounts used by a kernel must add up to no more than its launch allocation (threads x
+// registers per thread at launch) in every SM sub-partition.
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // 2^x with the hardware approximation (MUFU.EX2).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -285,6 +297,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
 }
+
+// A descriptor advanced by `bytes` (a multiple of 16) along its start address: the address field
+// is the low 14 bits of the start >> 4 and never carries for shared-memory offsets < 256 KB, so
+// the step is a plain add of a compile-time constant when the caller's loop is unrolled.
+__device__ __forceinline__ uint64_t desc_step(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
 
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, int b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |

@@ -29,6 +29,7 @@ import math
 import numpy as np
 import torch
 
+from . import dp
 from . import mha_ops as ops
 from .mha_ops import HeadView, ptr
 
@@ -199,17 +200,14 @@ class MultiHeadAttention:
 
         # one flat fp32 gradient buffer [dWqkv | dbqkv | dWo | dbo] so data-parallel training
         # all-reduces the four gradients with a single collective
-        sizes = [C * 3 * C, 3 * C, C * C, C]
-        self.flat_grads = torch.zeros(sum(sizes), dtype=torch.float32, device="cuda")
-        views, off = [], 0
-        for n in sizes:
-            views.append(self.flat_grads[off:off + n])
-            off += n
+        self.flat_grads = torch.zeros(dp.flat_grad_size(C), dtype=torch.float32, device="cuda")
+        views = {name: self.flat_grads[off:off + int(np.prod(shape))].view(shape)
+                 for name, off, shape in dp.grad_layout(C)}
         # same parameter order and init as model/gpt.py:507-510
-        self.c_attn_w = Parameter((C, C * 3), grad_storage=views[0].view(C, 3 * C))
-        self.c_attn_b = Parameter((C * 3,), init_scale=0.0, grad_storage=views[1])
-        self.c_proj_w = Parameter((C, C), grad_storage=views[2].view(C, C))
-        self.c_proj_b = Parameter((C,), init_scale=0.0, grad_storage=views[3])
+        self.c_attn_w = Parameter((C, C * 3), grad_storage=views["c_attn_w"])
+        self.c_attn_b = Parameter((C * 3,), init_scale=0.0, grad_storage=views["c_attn_b"])
+        self.c_proj_w = Parameter((C, C), grad_storage=views["c_proj_w"])
+        self.c_proj_b = Parameter((C,), init_scale=0.0, grad_storage=views["c_proj_b"])
 
         self.profiler = None  # optional: object with .range(name) -> context manager (CUDA events)
         self.grad_sync_group = None  # a torch.distributed group: backward all-reduces (SUM) into it
@@ -312,10 +310,8 @@ class MultiHeadAttention:
         with self._rng("colsum"):
             ops.colsum(gb, dt, 3 * C, M, 3 * C, self.c_attn_b.grads, accumulate=accumulate)
         if self.grad_sync_group is not None:
-            import torch.distributed as dist
             # overlaps the dX GEMM below on NCCL's stream
-            self._grad_sync_work = dist.all_reduce(self.flat_grads, op=dist.ReduceOp.SUM,
-                                                   group=self.grad_sync_group, async_op=True)
+            self._grad_sync_work = dp.allreduce_grads(self.flat_grads, self.grad_sync_group, async_op=True)
         dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_dx"):
             ops.gemm(gb, 3 * C, False, c["w_qkv"].data_ptr(), 3 * C, True, dt, dx.data_ptr(), C,
