@@ -1,24 +1,31 @@
 // tcgen05 tensor-core causal attention forward for head_dim 64, bf16 operands, fp32 accumulation.
 //
 // Replaces fused_attention_forward_kernel (core/mha_kernels.py:404-521).  A persistent kernel:
-// one CTA per SM walks a static list of items.  An item is two consecutive 128-row query tiles
-// (A = 2m, B = 2m+1) of one (batch, head); they share one stream of 128-key K/V blocks.  Items
-// are walked in pairs (m, nI-1-m) so that every pair costs the same number of blocks.
+// one CTA per SM walks a static list of work units (below).  Inside a CTA two
+// independent streams X = 0, 1 each process a list of 128-row query tiles; every stream has its
+// own TMA thread, MMA thread, softmax warpgroup, Q slots, K and V rings and TMEM columns, so one
+// stream's epilogue or short diagonal tile never stalls the other, and the two softmax
+// warpgroups keep the special-function units of every SM sub-partition busy between them.
 //
-//   MMA thread     per block j: S_X = Q_X K_j^T (X = A, B; tcgen05.mma, A and B operands from
-//                  shared memory, fp32 accumulator in TMEM), then O_X += P_X V_{j-1} for the
-//                  previous block (A = P_X read from TMEM, B = V MN-major from shared memory)
-//   softmax A, B   two warpgroups, one per query tile, one query row per thread: the row of S
-//                  is read from TMEM once (128 columns), causal mask on the diagonal block only,
-//                  row max, 2^(s*scale*log2e - m), row sum; P packed to bf16 into the tile's own
-//                  TMEM P columns, so the next S can be computed while P V runs
-// While one warpgroup computes its softmax the tensor core works for the other, and the two
-// warpgroups give each SM sub-partition two softmax warps.  The running max is only moved (and O
-// rescaled in TMEM) when it grows by more than 2^8, so rescaling is rare.  The row's log-sum-exp
-// is written instead of the T x T probabilities.
+// Work is handed out in units of two query tiles (nq-1-k, k) of one head, which cost nq+1 key
+// blocks together (the middle tile of an odd count is a unit of its own); a CTA's units alternate
+// between its two streams.
 //
-// TMEM columns: S_A [0,128), S_B [128,256), P_A [256,320), P_B [320,384), O_A [384,448),
-// O_B [448,512).
+//   TMA thread     Q of the tile (the next tile's Q is fetched while this tile streams), then
+//                  K_j and V_j for the key blocks j = 0 .. t into two-stage rings (K and V are
+//                  released separately: K after S, V after P V)
+//   MMA thread     S(j) = Q K_j^T (A and B from shared memory, fp32 in TMEM) as soon as softmax
+//                  has loaded S(j-1), then O += P(j-1) V_{j-1} (A = P from TMEM, B = V MN-major)
+//   softmax        one query row per thread: the row of S is read from TMEM once (128 columns)
+//                  and S released at once, so S(j+1) runs on the tensor core while this step
+//                  exponentiates; causal mask on the diagonal block only, row max,
+//                  2^(s*scale*log2e - m) packed to bf16 in registers, row sum; P then goes to
+//                  TMEM as soon as the previous P V has read it.  The running max is only moved
+//                  (and O rescaled in TMEM) when it grows by more than 2^8, so rescaling is rare.
+//                  Epilogue: O / l through a swizzled staging tile and one TMA store; the row's
+//                  log-sum-exp is written instead of the T x T probabilities.
+//
+// TMEM columns of stream X: S [256X, 256X+128), P [256X+128, +64), O [256X+192, +64).
 //
 // Every mbarrier wait is bounded (tc_common.cuh): a wait that gives up sets the library's device
 // error word and the kernel skips its remaining work instead of hanging.
@@ -28,108 +35,91 @@
 
 namespace attn {
 
-constexpr int FA_THREADS = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 softmax A, 6-9 softmax B
-constexpr int FA_KV = 3;         // K/V ring stages
+// Three warpgroups: 0 = TMA 0, MMA 0, TMA 1, MMA 1 (one warp each); 1 = softmax of stream 0;
+// 2 = softmax of stream 1.  Launched at 168 registers per thread (the most a 384-thread CTA can
+// have); warpgroup 0 gives registers back to the softmax warpgroups: per SM sub-partition (one
+// warp of each warpgroup) FA_REG_LOW + 2 * FA_REG_SOFT <= 3 x 168.
+constexpr int FA_THREADS = 384;
+constexpr int FA_REG_LOW = 56, FA_REG_SOFT = 224;
+static_assert(FA_REG_LOW + 2 * FA_REG_SOFT <= 3 * 168, "register split exceeds the launch allocation");
 constexpr uint32_t FA_TMEM_COLS = 512;
-constexpr uint32_t FA_TM_S = 0, FA_TM_P = 256, FA_TM_O = 384;
-constexpr int FA_SMEM = 1024 + AT_TILE_BYTES * (4 + 2 * FA_KV + 2) + 256;
+constexpr uint32_t FA_TM_S = 0, FA_TM_P = 128, FA_TM_O = 192, FA_TM_STREAM = 256;
+constexpr int FA_STREAM_BYTES = 7 * AT_TILE_BYTES;  // Q[2], K[2], V[2], O staging
+constexpr int FA_BAR_BYTES = 512;
+constexpr int FA_SMEM = 1024 + 2 * FA_STREAM_BYTES + FA_BAR_BYTES;
 
 struct FwdMaps {
   TileMap q, k, v, o;
 };
 
 struct FwdParams {
-  int NH, T, nq, n_items, n_units, BH;  // n_items = ceil(nq/2) per head, n_units = ceil(n_items/2)
+  int NH, T, nq, npairs, BH;  // npairs = ceil(nq / 2) units per head
   float scale_log2;
-  __nv_bfloat16* o;
-  int64_t o_sb, o_st, o_sh;
   float* lse;
   int* err;
 };
 
-// The item list every role of a CTA walks in the same order: units w = blockIdx.x, +gridDim.x,
-// ...; unit w is head bh = w / n_units with items m = u and n_items-1-u (u = w % n_units; one
-// item when they coincide).  Item m covers query tiles 2m and 2m+1 (tB = -1 past the end).
-// fn(bh, tA, tB) returns false to stop the walk.
-template <typename Fn>
-__device__ __forceinline__ void for_each_item(const FwdParams& p, Fn&& fn) {
-  for (int w = blockIdx.x; w < p.BH * p.n_units; w += gridDim.x) {
-    const int bh = w / p.n_units, u = w % p.n_units;
-    const int m0 = p.n_items - 1 - u, m1 = u;  // the longer item first
-    int tB = 2 * m0 + 1 < p.nq ? 2 * m0 + 1 : -1;
-    if (!fn(bh, 2 * m0, tB)) return;
-    if (m1 != m0) {
-      tB = 2 * m1 + 1 < p.nq ? 2 * m1 + 1 : -1;
-      if (!fn(bh, 2 * m1, tB)) return;
-    }
-  }
-}
-
-// The same walk as an explicit cursor, for the producer, which loads the next item's Q while
-// streaming the current item's K/V blocks.
-struct ItemCursor {
-  int w, second;  // unit index and which item of the unit
-  int bh, tA, tB;
+// The tiles of one stream, in the order all of the stream's roles visit them.  Work is cut into
+// units w = (head bh, pair k): query tiles nq-1-k and k of that head (the middle tile alone when
+// nq is odd), nq+1 key blocks per full pair.  The CTA takes units w = blockIdx.x + n*gridDim.x;
+// stream X takes its n = X, X+2, X+4, ...
+struct TileWalk {
+  int n, second;  // unit index within the CTA, and which tile of the unit
+  int bh, t;
+  __device__ __forceinline__ bool valid(const FwdParams& p) const { return bh < p.BH; }
   __device__ __forceinline__ void set(const FwdParams& p) {
-    const int u = w % p.n_units;
-    const int m = second ? u : p.n_items - 1 - u;
-    bh = w / p.n_units;
-    tA = 2 * m;
-    tB = 2 * m + 1 < p.nq ? 2 * m + 1 : -1;
+    const int w = blockIdx.x + n * gridDim.x;
+    bh = w / p.npairs;
+    const int k = w - bh * p.npairs;
+    t = second ? k : p.nq - 1 - k;
   }
-  __device__ __forceinline__ bool valid(const FwdParams& p) const { return w < p.BH * p.n_units; }
-  __device__ __forceinline__ void start(const FwdParams& p) {
-    w = blockIdx.x;
+  __device__ __forceinline__ void start(const FwdParams& p, int X) {
+    n = X;
     second = 0;
-    if (valid(p)) set(p);
+    set(p);
   }
-  __device__ __forceinline__ void next(const FwdParams& p) {
-    const int u = w % p.n_units;
-    if (!second && u != p.n_items - 1 - u) {
-      second = 1;
+  __device__ __forceinline__ void next(const FwdParams& p, int) {
+    if (!second && t != p.nq - 1 - t) {
+      second = 1;  // the pair's short tile
     } else {
       second = 0;
-      w += gridDim.x;
+      n += 2;
     }
-    if (valid(p)) set(p);
+    set(p);
   }
 };
+
+struct StreamBars {
+  uint64_t q_full[2], q_empty[2], k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full, s_free, p_ready, pv_done, wg_bar;
+};
+static_assert(2 * sizeof(StreamBars) + 16 <= FA_BAR_BYTES, "barrier area too small");
 
 __global__ void __launch_bounds__(FA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                               // [2 slots][A, B]
-  uint8_t* sK = sQ + 4 * AT_TILE_BYTES;             // [FA_KV]
-  uint8_t* sV = sK + FA_KV * AT_TILE_BYTES;         // [FA_KV]
-  uint8_t* sO = sV + FA_KV * AT_TILE_BYTES;         // [2] epilogue staging per softmax warpgroup
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sO + 2 * AT_TILE_BYTES);
-  uint64_t* q_full = bars;              // [2] per Q slot (both tiles of an item)
-  uint64_t* q_empty = q_full + 2;       // [2]
-  uint64_t* k_full = q_empty + 2;       // [FA_KV]
-  uint64_t* v_full = k_full + FA_KV;    // [FA_KV]
-  uint64_t* kv_empty = v_full + FA_KV;  // [FA_KV]
-  uint64_t* s_full = kv_empty + FA_KV;  // [2] per query tile X: S_X is in TMEM
-  uint64_t* p_ready = s_full + 2;       // [2] S_X read and P_X written (128 arrivals)
-  uint64_t* pv_done = p_ready + 2;      // [2] the P_X V MMA has completed
-  uint64_t* wg_bar = pv_done + 2;       // [2] sync of softmax warpgroup X (128 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wg_bar + 2);
+  StreamBars* sbars = reinterpret_cast<StreamBars*>(smem + 2 * FA_STREAM_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbars + 2);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_ready[s], 128);
-      mbar_init(&pv_done[s], 1);
-      mbar_init(&wg_bar[s], 128);
-    }
-    for (int s = 0; s < FA_KV; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int x = 0; x < 2; ++x) {
+      StreamBars& b = sbars[x];
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(&b.q_full[s], 1);
+        mbar_init(&b.q_empty[s], 1);
+        mbar_init(&b.k_full[s], 1);
+        mbar_init(&b.k_empty[s], 1);
+        mbar_init(&b.v_full[s], 1);
+        mbar_init(&b.v_empty[s], 1);
+      }
+      mbar_init(&b.s_full, 1);
+      mbar_init(&b.s_free, 128);
+      mbar_init(&b.p_ready, 128);
+      mbar_init(&b.pv_done, 1);
+      mbar_init(&b.wg_bar, 128);
     }
     fence_mbar_init();
   }
@@ -142,125 +132,133 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      tma_prefetch_desc(&maps.q.map);
-      tma_prefetch_desc(&maps.k.map);
-      tma_prefetch_desc(&maps.v.map);
-      auto load_q = [&](const ItemCursor& c, int it) -> bool {
-        const int qs = it & 1;
-        if (!mbar_wait(&q_empty[qs], ((it >> 1) & 1) ^ 1, p.err, 201)) return false;
-        const int b = c.bh / p.NH, h = c.bh % p.NH;
-        mbar_arrive_expect_tx(&q_full[qs], (c.tB >= 0 ? 2 : 1) * AT_TILE_BYTES);
-        load_tile(sQ + (2 * qs) * AT_TILE_BYTES, maps.q, &q_full[qs], b, h, c.tA * AT_TILE);
-        if (c.tB >= 0) load_tile(sQ + (2 * qs + 1) * AT_TILE_BYTES, maps.q, &q_full[qs], b, h, c.tB * AT_TILE);
-        return true;
-      };
-      ItemCursor cur;
-      cur.start(p);
-      bool ok = !cur.valid(p) || load_q(cur, 0);
-      int it = 0, g = 0;
-      while (ok && cur.valid(p)) {
-        ItemCursor nxt = cur;
-        nxt.next(p);
-        const int b = cur.bh / p.NH, h = cur.bh % p.NH;
-        const int jmax = cur.tB >= 0 ? cur.tB : cur.tA;
-        for (int j = 0; j <= jmax && ok; ++j, ++g) {
-          const int st = g % FA_KV;
-          if (!mbar_wait(&kv_empty[st], ((g / FA_KV) & 1) ^ 1, p.err, 202)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[st], AT_TILE_BYTES);
-          load_tile(sK + st * AT_TILE_BYTES, maps.k, &k_full[st], b, h, j * AT_TILE);
-          mbar_arrive_expect_tx(&v_full[st], AT_TILE_BYTES);
-          load_tile(sV + st * AT_TILE_BYTES, maps.v, &v_full[st], b, h, j * AT_TILE);
-          // the next item's Q, as soon as this item's first block is on its way
-          if (j == 0 && nxt.valid(p) && !load_q(nxt, it + 1)) ok = false;
+  if (warp < 4) {
+    reg_dealloc<FA_REG_LOW>();
+    const int X = warp >> 1;  // warps 0, 1: stream 0; warps 2, 3: stream 1
+    StreamBars& sb = sbars[X];
+    uint8_t* sQ = smem + X * FA_STREAM_BYTES;  // [2]
+    uint8_t* sK = sQ + 2 * AT_TILE_BYTES;      // [2]
+    uint8_t* sV = sK + 2 * AT_TILE_BYTES;      // [2]
+    if ((warp & 1) == 0) {
+      // ---------------- TMA producer of stream X ----------------
+      if (lane == 0) {
+        if (X == 0) {
+          tma_prefetch_desc(&maps.q.map);
+          tma_prefetch_desc(&maps.k.map);
+          tma_prefetch_desc(&maps.v.map);
         }
-        cur = nxt;
-        ++it;
+        auto load_q = [&](const TileWalk& c, int it) -> bool {
+          const int qs = it & 1;
+          if (!mbar_wait(&sb.q_empty[qs], ((it >> 1) & 1) ^ 1, p.err, 201)) return false;
+          mbar_arrive_expect_tx(&sb.q_full[qs], AT_TILE_BYTES);
+          load_tile(sQ + qs * AT_TILE_BYTES, maps.q, &sb.q_full[qs], c.bh / p.NH, c.bh % p.NH, c.t * AT_TILE);
+          return true;
+        };
+        TileWalk cur;
+        cur.start(p, X);
+        bool ok = !cur.valid(p) || load_q(cur, 0);
+        int it = 0, kg = 0, vg = 0;
+        while (ok && cur.valid(p)) {
+          TileWalk nxt = cur;
+          nxt.next(p, X);
+          const int b = cur.bh / p.NH, h = cur.bh % p.NH;
+          for (int j = 0; j <= cur.t && ok; ++j, ++kg, ++vg) {
+            const int ks = kg & 1, vs = vg & 1;
+            if (!mbar_wait(&sb.k_empty[ks], ((kg >> 1) & 1) ^ 1, p.err, 202)) { ok = false; break; }
+            mbar_arrive_expect_tx(&sb.k_full[ks], AT_TILE_BYTES);
+            load_tile(sK + ks * AT_TILE_BYTES, maps.k, &sb.k_full[ks], b, h, j * AT_TILE);
+            if (!mbar_wait(&sb.v_empty[vs], ((vg >> 1) & 1) ^ 1, p.err, 212)) { ok = false; break; }
+            mbar_arrive_expect_tx(&sb.v_full[vs], AT_TILE_BYTES);
+            load_tile(sV + vs * AT_TILE_BYTES, maps.v, &sb.v_full[vs], b, h, j * AT_TILE);
+            // the next tile's Q, as soon as this tile's first block is on its way
+            if (j == 0 && nxt.valid(p) && !load_q(nxt, it + 1)) ok = false;
+          }
+          cur = nxt;
+          ++it;
+        }
       }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);  // Q K-major, K K-major
-      const uint32_t idesc_o = idesc_bf16_f32(128, 64, 0, 1);   // P from TMEM, V MN-major
-      int cnt[2] = {0, 0};  // S MMAs issued per query tile X (= softmax steps of X)
-      int it = 0, g = 0;
-      bool ok = true;
-      for_each_item(p, [&](int bh, int tA, int tB) -> bool {
-        (void)bh;
-        const int qs = it & 1;
-        const int tX[2] = {tA, tB};
-        if (!mbar_wait(&q_full[qs], (it >> 1) & 1, p.err, 203)) return ok = false;
-        const int jmax = tB >= 0 ? tB : tA;
-        // block j: S_X(j) for the tiles that see it, then P_X V_{j-1}; a last pass (j = jmax+1)
-        // issues only the final P V products
-        for (int j = 0; j <= jmax + 1; ++j) {
-          const int st = (g + j) % FA_KV, pst = (g + j - 1) % FA_KV;
-          if (j <= jmax && !mbar_wait(&k_full[st], ((g + j) / FA_KV) & 1, p.err, 204)) return ok = false;
-          if (j > 0 && !mbar_wait(&v_full[pst], ((g + j - 1) / FA_KV) & 1, p.err, 205)) return ok = false;
-          for (int x = 0; x < 2; ++x) {
-            const bool now = j <= tX[x], prev = j >= 1 && j - 1 <= tX[x];
-            if (!now && !prev) continue;
-            // S_X is rewritten (and P_X read by the MMA) once softmax X has finished its step
-            if (cnt[x] > 0 && !mbar_wait(&p_ready[x], (cnt[x] - 1) & 1, p.err, 206)) return ok = false;
-            tc_fence_after();
-            if (now) {
-              const uint64_t q_desc = smem_desc_sw128(smem_u32(sQ + (2 * qs + x) * AT_TILE_BYTES), 16, 1024);
-              const uint64_t k_desc = smem_desc_sw128(smem_u32(sK + st * AT_TILE_BYTES), 16, 1024);
-              const uint32_t tS = tmem + FA_TM_S + x * 128;
+    } else {
+      // ---------------- MMA issuer of stream X ----------------
+      if (lane == 0) {
+        const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);  // Q K-major, K K-major
+        const uint32_t idesc_o = idesc_bf16_f32(128, 64, 0, 1);   // P from TMEM, V MN-major
+        const uint32_t tS = tmem + X * FA_TM_STREAM + FA_TM_S;
+        const uint32_t tP = tmem + X * FA_TM_STREAM + FA_TM_P;
+        const uint32_t tO = tmem + X * FA_TM_STREAM + FA_TM_O;
+        int scnt = 0, pcnt = 0;  // S and P V MMAs issued (= softmax steps started / finished)
+        int it = 0, kg = 0, vg = 0;
+        bool ok = true;
+        TileWalk cur;
+        for (cur.start(p, X); ok && cur.valid(p); cur.next(p, X), ++it) {
+          const int qs = it & 1;
+          if (!mbar_wait(&sb.q_full[qs], (it >> 1) & 1, p.err, 203)) { ok = false; break; }
+          const uint64_t q_desc = smem_desc_sw128(smem_u32(sQ + qs * AT_TILE_BYTES), 16, 1024);
+          for (int j = 0; j <= cur.t + 1 && ok; ++j) {
+            if (j <= cur.t) {
+              // S(j) = Q K_j^T once softmax has loaded S(j-1)
+              const int ks = kg & 1;
+              if (!mbar_wait(&sb.k_full[ks], (kg >> 1) & 1, p.err, 204)) { ok = false; break; }
+              if (scnt > 0 && !mbar_wait(&sb.s_free, (scnt - 1) & 1, p.err, 206)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t k_desc = smem_desc_sw128(smem_u32(sK + ks * AT_TILE_BYTES), 16, 1024);
 #pragma unroll
               for (int k = 0; k < AT_D / 16; ++k)
-                umma_ss(tS, desc_step(q_desc, k * 32), desc_step(k_desc, k * 32),
-                        idesc_s, k > 0 ? 1u : 0u);
-              umma_commit(&s_full[x]);
-              ++cnt[x];
+                umma_ss(tS, desc_step(q_desc, k * 32), desc_step(k_desc, k * 32), idesc_s, k > 0 ? 1u : 0u);
+              umma_commit(&sb.s_full);
+              umma_commit(&sb.k_empty[ks]);
+              if (j == cur.t) umma_commit(&sb.q_empty[qs]);  // the tile's last S read Q
+              ++scnt;
+              ++kg;
             }
-            if (prev) {
-              const uint64_t v_desc = smem_desc_sw128(smem_u32(sV + pst * AT_TILE_BYTES), 8192, 1024);
-              const uint32_t tP = tmem + FA_TM_P + x * 64, tO = tmem + FA_TM_O + x * 64;
+            if (j > 0) {
+              // O += P(j-1) V_{j-1} once softmax has written P(j-1) (and rescaled O)
+              const int vs = vg & 1;
+              if (!mbar_wait(&sb.v_full[vs], (vg >> 1) & 1, p.err, 205)) { ok = false; break; }
+              if (!mbar_wait(&sb.p_ready, pcnt & 1, p.err, 211)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t v_desc = smem_desc_sw128(smem_u32(sV + vs * AT_TILE_BYTES), 8192, 1024);
 #pragma unroll
               for (int k = 0; k < AT_TILE / 16; ++k)
-                umma_ts(tO, tP + k * 8, desc_step(v_desc, k * 2048), idesc_o,
-                        (j == 1 && k == 0) ? 0u : 1u);
-              umma_commit(&pv_done[x]);
+                umma_ts(tO, tP + k * 8, desc_step(v_desc, k * 2048), idesc_o, (j == 1 && k == 0) ? 0u : 1u);
+              umma_commit(&sb.pv_done);
+              umma_commit(&sb.v_empty[vs]);
+              ++pcnt;
+              ++vg;
             }
           }
-          if (j == jmax) umma_commit(&q_empty[qs]);  // the item's last S MMAs read Q
-          if (j > 0) umma_commit(&kv_empty[pst]);
         }
-        g += jmax + 1;
-        ++it;
-        return true;
-      });
+      }
     }
   } else {
-    // ---------------- softmax warpgroups: X = 0 (tile A) warps 2-5, X = 1 (tile B) warps 6-9 ----------------
-    const int x = (warp - 2) >> 2;
+    reg_alloc<FA_REG_SOFT>();
+    // ---------------- softmax warpgroup of stream X (warps 4-7: X = 0, 8-11: X = 1) ----------------
+    const int X = (warp - 4) >> 2;
+    StreamBars& sb = sbars[X];
+    uint8_t* stg = smem + X * FA_STREAM_BYTES + 6 * AT_TILE_BYTES;  // O staging tile
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tmem + FA_TM_S + x * 128 + lane_off;
-    const uint32_t tP = tmem + FA_TM_P + x * 64 + lane_off;
-    const uint32_t tO = tmem + FA_TM_O + x * 64 + lane_off;
+    const uint32_t tS = tmem + X * FA_TM_STREAM + FA_TM_S + lane_off;
+    const uint32_t tP = tmem + X * FA_TM_STREAM + FA_TM_P + lane_off;
+    const uint32_t tO = tmem + X * FA_TM_STREAM + FA_TM_O + lane_off;
     const float sl2 = p.scale_log2;
     int c = 0;  // softmax steps done by this warpgroup
-    const bool leader = (warp & 3) == 2 && lane == 0;  // first warp of the warpgroup
+    const bool leader = (warp & 3) == 0 && lane == 0;  // first thread of the warpgroup
     bool first_store = true;
     uint32_t wg_phase = 0;
-    auto wg_sync = [&]() -> bool {  // bounded barrier over the 128 threads of warpgroup X
-      mbar_arrive(&wg_bar[x]);
-      const bool w = mbar_wait(&wg_bar[x], wg_phase & 1, p.err, 210);
+    auto wg_sync = [&]() -> bool {  // bounded barrier over the 128 threads of the warpgroup
+      mbar_arrive(&sb.wg_bar);
+      const bool w = mbar_wait(&sb.wg_bar, wg_phase & 1, p.err, 210);
       ++wg_phase;
       return __all_sync(0xffffffffu, w);
     };
-    for_each_item(p, [&](int bh, int tA, int tB) -> bool {
-      const int t = x == 0 ? tA : tB;
-      if (t < 0) return true;
+    TileWalk cur;
+    for (cur.start(p, X); cur.valid(p); cur.next(p, X)) {
+      const int t = cur.t;
       float m = -INFINITY, l = 0.f;
+      bool ok = true;
       for (int j = 0; j <= t; ++j, ++c) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], c & 1, p.err, 207))) return false;
+        if (!__all_sync(0xffffffffu, mbar_wait(&sb.s_full, c & 1, p.err, 207))) { ok = false; break; }
         tc_fence_after();
         uint32_t sr[128];
         tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(sr));
@@ -268,8 +266,9 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
         tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
         tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
         tmem_wait_ld();
-        const bool diag = (j == t);
-        if (diag) {  // key column k is visible to query row r iff k <= r
+        tc_fence_before();
+        mbar_arrive(&sb.s_free);  // S is in registers: the next S may be computed
+        if (j == t) {  // diagonal block: key column k is visible to query row r iff k <= r
 #pragma unroll
           for (int i = 0; i < 128; ++i)
             if (i > row) sr[i] = __float_as_uint(-INFINITY);
@@ -288,28 +287,27 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
         const bool rescale = j > 0 && __any_sync(0xffffffffu, grow_m);
         const float alpha = (j > 0 && grow_m) ? ex2_approx(m - m_cand) : 1.f;
         if (grow_m) m = m_cand;
-        // P_X and O_X are touched once the previous step's P V has completed
-        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[x], (c - 1) & 1, p.err, 208))) return false;
-        tc_fence_after();
+        // P = 2^(s*scale*log2e - m) packed to bf16 in registers, the row sum in fp32
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        uint32_t pk[64];
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float a0 = ex2_approx(fmaf(__uint_as_float(sr[cc * 32 + i]), sl2, -m));
-            const float a1 = ex2_approx(fmaf(__uint_as_float(sr[cc * 32 + i + 1]), sl2, -m));
-            const float a2 = ex2_approx(fmaf(__uint_as_float(sr[cc * 32 + i + 2]), sl2, -m));
-            const float a3 = ex2_approx(fmaf(__uint_as_float(sr[cc * 32 + i + 3]), sl2, -m));
-            s0 += a0;
-            s1 += a1;
-            s2 += a2;
-            s3 += a3;
-            pk[i / 2] = pack_bf16x2(a0, a1);
-            pk[i / 2 + 1] = pack_bf16x2(a2, a3);
-          }
-          tmem_st16(tP + cc * 16, pk);
+        for (int i = 0; i < 128; i += 4) {
+          const float a0 = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, -m));
+          const float a1 = ex2_approx(fmaf(__uint_as_float(sr[i + 1]), sl2, -m));
+          const float a2 = ex2_approx(fmaf(__uint_as_float(sr[i + 2]), sl2, -m));
+          const float a3 = ex2_approx(fmaf(__uint_as_float(sr[i + 3]), sl2, -m));
+          s0 += a0;
+          s1 += a1;
+          s2 += a2;
+          s3 += a3;
+          pk[i / 2] = pack_bf16x2(a0, a1);
+          pk[i / 2 + 1] = pack_bf16x2(a2, a3);
         }
+        // P and O are rewritten once the previous step's P V has completed
+        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&sb.pv_done, (c - 1) & 1, p.err, 208))) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) tmem_st16(tP + cc * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * cc));
         if (rescale) {  // O *= 2^(m_old - m_new) on the rows whose max moved (before this P V)
           uint32_t o[64];
           tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
@@ -324,10 +322,11 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
         l += (s0 + s1) + (s2 + s3);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_ready[x]);
+        mbar_arrive(&sb.p_ready);
       }
+      if (!ok) break;
       // epilogue: O / l -> bf16 rows, lse = (m + log2 l) * ln 2
-      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[x], (c - 1) & 1, p.err, 209))) return false;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sb.pv_done, (c - 1) & 1, p.err, 209))) break;
       tc_fence_after();
       uint32_t o[64];
       tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
@@ -336,9 +335,8 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       tc_fence_before();
       // O rows -> swizzled staging tile -> one TMA store (rows past T are clipped)
       const float inv = 1.f / l;
-      uint8_t* stg = sO + x * AT_TILE_BYTES;
       if (leader && !first_store) bulk_wait_read0();  // the previous store has read the staging tile
-      if (!wg_sync()) return false;
+      if (!wg_sync()) break;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const uint32_t* src = o + 8 * k;
@@ -350,19 +348,18 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
         *reinterpret_cast<uint4*>(stg + row * 128 + ((k ^ (row & 7)) << 4)) = u;
       }
       fence_proxy_async_smem();
-      if (!wg_sync()) return false;
-      const int b = bh / p.NH, h = bh % p.NH;
+      if (!wg_sync()) break;
+      const int b = cur.bh / p.NH, h = cur.bh % p.NH;
       if (leader) {
         store_tile(maps.o, stg, b, h, t * AT_TILE);
         bulk_commit();
       }
       first_store = false;
       const int grow = t * AT_TILE + row;
-      if (grow < p.T) p.lse[(int64_t)bh * p.T + grow] = (m + __log2f(l)) * LN2;
-      return true;
-    });
+      if (grow < p.T) p.lse[(int64_t)cur.bh * p.T + grow] = (m + __log2f(l)) * LN2;
+    }
+    if (leader) bulk_wait0();  // epilogue stores done with shared memory
   }
-  if (warp >= 2 && (warp & 3) == 2 && lane == 0) bulk_wait0();  // epilogue stores done with smem
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -395,22 +392,17 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   p.NH = NH;
   p.T = T;
   p.nq = (T + AT_TILE - 1) / AT_TILE;
-  p.n_items = (p.nq + 1) / 2;
-  p.n_units = (p.n_items + 1) / 2;
+  p.npairs = (p.nq + 1) / 2;
   p.BH = B * NH;
   p.scale_log2 = scale * LOG2E;
-  p.o = reinterpret_cast<__nv_bfloat16*>(o);
-  p.o_sb = s[3];
-  p.o_st = s[4];
-  p.o_sh = s[5];
   p.lse = lse;
   p.err = dev_error_ptr();
   if (!p.err) return ATTN_ERR_CUDA;
   static uint64_t attr_done = 0;
   if (!set_smem_limit_once(attn_fwd_tc_kernel, FA_SMEM, attr_done)) return ATTN_ERR_CUDA;
-  const int64_t units = (int64_t)p.BH * p.n_units;
+  const int64_t units = (int64_t)p.BH * p.npairs;
   const int sms = current_device_sms();
-  const int grid = (int)(units < sms ? units : sms);
+  const int grid = (int)((units + 1) / 2 < sms ? (units + 1) / 2 : sms);  // at least a unit per stream
   attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);
   count_launch();
   return check_launch("attn_fwd_tc_kernel");
