@@ -61,8 +61,10 @@ int attn_device_error(int clear);
  * Replaces fused_attention_forward_kernel (core/mha_kernels.py:404-521); instead of writing the
  * normalised probabilities Scores[B*NH,T,T] it writes lse[B,NH,T].
  * dtype ATTN_F32: CUDA-core fp32 path (any D <= 128, D % 4 == 0).
- * dtype ATTN_BF16: tcgen05 tensor-core path for D == 64 (TMA-staged K/V, TMEM accumulators),
- *                  CUDA-core path otherwise; fp32 softmax statistics and accumulation.
+ * dtype ATTN_BF16: tcgen05 tensor-core path for D a multiple of 8 up to 64 (TMA-staged K/V, TMEM
+ *                  accumulators; heads narrower than 64 are zero-padded to 64 by TMA) when the
+ *                  tensors are 16-byte aligned with strides in 8-element steps, CUDA-core path
+ *                  otherwise; fp32 softmax statistics and accumulation.
  * Q/K/V share the input strides; O uses the output strides.
  */
 int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,

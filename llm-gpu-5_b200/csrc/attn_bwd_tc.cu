@@ -60,7 +60,7 @@ struct BwdMaps {
 };
 
 struct BwdParams {
-  int NH, T, nq, Tp, BH;
+  int NH, T, nq, Tp, BH, D;  // D = head_dim (<= 64; the tiles are 64 wide)
   float scale, scale_log2;
   const float* lse2;    // [BH][Tp] lse * log2 e (+inf on padding rows)
   const float* delta;   // [BH][Tp]
@@ -73,7 +73,7 @@ struct BwdParams {
 __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o,
                                      const __nv_bfloat16* __restrict__ dout,
                                      const float* __restrict__ lse, float* __restrict__ lse2,
-                                     float* __restrict__ delta, int NH, int T, int Tp,
+                                     float* __restrict__ delta, int NH, int T, int Tp, int D,
                                      int64_t o_sb, int64_t o_st, int64_t o_sh, int64_t rows) {
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (idx >= rows) return;
@@ -89,8 +89,8 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o,
   const uint4* po = reinterpret_cast<const uint4*>(o + off);
   const uint4* pd = reinterpret_cast<const uint4*>(dout + off);
   float acc = 0.f;
-#pragma unroll
-  for (int c = 0; c < AT_D / 8; ++c) {
+#pragma unroll 8
+  for (int c = 0; c < D / 8; ++c) {
     const uint4 a = po[c], g = pd[c];
     const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
@@ -133,11 +133,12 @@ __device__ __forceinline__ void pack_row_bf16(uint32_t (&out)[32], const uint32_
   }
 }
 
-// 32 packed bf16 pairs -> 8 x 16 B at dst (one 64-element row).
-__device__ __forceinline__ void store_packed_row(__nv_bfloat16* dst, const uint32_t (&w)[32]) {
+// The first D of 64 packed bf16 values (32 pairs) -> D/8 x 16 B at dst (one head row).
+__device__ __forceinline__ void store_packed_row(__nv_bfloat16* dst, const uint32_t (&w)[32], int D) {
 #pragma unroll
   for (int c = 0; c < 8; ++c)
-    reinterpret_cast<uint4*>(dst)[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    if (c < D / 8)
+      reinterpret_cast<uint4*>(dst)[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
 
 __global__ void __launch_bounds__(BA_THREADS, 1)
@@ -488,8 +489,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
             const int key = jt * AT_TILE + row;
             if (key < p.T) {
               const int64_t off = (int64_t)b * p.sb + (int64_t)key * p.st + (int64_t)h * p.sh;
-              store_packed_row(p.dv + off, pv);
-              store_packed_row(p.dk + off, pkk);
+              store_packed_row(p.dv + off, pv, p.D);
+              store_packed_row(p.dk + off, pkk, p.D);
             }
           }
           ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, p.err, 316));
@@ -526,7 +527,7 @@ if (jt == 0) {
             if (qrow < p.T) {
               uint32_t w[32];
               pack_row_bf16(w, a0, a1, p.scale);
-              store_packed_row(p.dq + (int64_t)b * p.sb + (int64_t)qrow * p.st + (int64_t)h * p.sh, w);
+              store_packed_row(p.dq + (int64_t)b * p.sb + (int64_t)qrow * p.st + (int64_t)h * p.sh, w, p.D);
             }
           } else {
             // an earlier contribution: into the accumulator in L2 (a TMA store from the diagonal
@@ -572,21 +573,21 @@ if (jt == 0) {
 // ==========================================================================================
 // host side
 // ==========================================================================================
-bool tc_bwd_supported(int D, int dtype) { return D == AT_D && dtype == ATTN_BF16; }
+bool tc_bwd_supported(int D, int dtype) { return tc_head_dim_ok(D) && dtype == ATTN_BF16; }
 
 static int bwd_grid(int BH) { return BH < BA_MAX_CTAS ? BH : BA_MAX_CTAS; }
 
 size_t attn_bwd_tc_ws(int B, int NH, int T, int D) {
   const size_t Tp = (size_t)((T + AT_TILE - 1) / AT_TILE) * AT_TILE;
   const size_t BH = (size_t)B * NH;
-  return 2 * align256(BH * Tp * 4) + align256((size_t)bwd_grid((int)BH) * Tp * D * 4);
+  (void)D;  // the dQ accumulator rows are one 64-wide head tile whatever the head_dim
+  return 2 * align256(BH * Tp * 4) + align256((size_t)bwd_grid((int)BH) * Tp * AT_D * 4);
 }
 
 int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, const void* dout,
                 const float* lse, void* dq, void* dk, void* dv, void* ws, int B, int NH, int T, int D,
                 const int64_t* s, float scale, cudaStream_t stream) {
-  (void)D;
-  if (!head_strides_ok(s[0], s[1], s[2]) || !head_strides_ok(s[3], s[4], s[5]) || !aligned(q, 16) ||
+  if (!head_strides_ok(s[0], s[1], s[2], D) || !head_strides_ok(s[3], s[4], s[5], D) || !aligned(q, 16) ||
       !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 16) || !aligned(dout, 16) || !aligned(dq, 16) ||
       !aligned(dk, 16) || !aligned(dv, 16)) {
     set_error("attn_bwd: the tensor-core path needs 16-byte aligned bf16 tensors with strides that are "
@@ -605,15 +606,15 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   float* dq_acc = reinterpret_cast<float*>(w + 2 * align256((size_t)BH * Tp * 4));
   const int64_t rows = (int64_t)BH * Tp;
   attn_bwd_prep_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
-      (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, lse2, delta, NH, T, Tp, s[3], s[4], s[5], rows);
+      (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, lse2, delta, NH, T, Tp, D, s[3], s[4], s[5], rows);
   count_launch();
   if (int rc = check_launch("attn_bwd_prep_kernel")) return rc;
 
   BwdMaps maps;
-  if (!make_head_map(&maps.q, q, B, NH, T, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.k, k, B, NH, T, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.v, v, B, NH, T, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.dout, dout, B, NH, T, s[3], s[4], s[5]))
+  if (!make_head_map(&maps.q, q, B, NH, T, D, s[0], s[1], s[2]) ||
+      !make_head_map(&maps.k, k, B, NH, T, D, s[0], s[1], s[2]) ||
+      !make_head_map(&maps.v, v, B, NH, T, D, s[0], s[1], s[2]) ||
+      !make_head_map(&maps.dout, dout, B, NH, T, D, s[3], s[4], s[5]))
     return ATTN_ERR_CUDA;
   {
     const uint64_t dims[2] = {(uint64_t)AT_D, (uint64_t)grid * Tp};
@@ -627,6 +628,7 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   p.nq = nq;
   p.Tp = Tp;
   p.BH = BH;
+  p.D = D;
   p.scale = scale;
   p.scale_log2 = scale * LOG2E;
   p.lse2 = lse2;

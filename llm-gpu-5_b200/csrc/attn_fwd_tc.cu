@@ -371,22 +371,30 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
 // ==========================================================================================
 // host side
 // ==========================================================================================
-bool tc_fwd_supported(int D, int dtype) { return D == AT_D && dtype == ATTN_BF16; }
+bool tc_fwd_supported(int D, int dtype) { return tc_head_dim_ok(D) && dtype == ATTN_BF16; }
+
+// Whether n tensors with the element strides s[0..5] (input b/t/h, output b/t/h) can go through
+// the TMA maps of the tensor-core kernels: 16-byte aligned bases, strides in 16-byte steps.
+bool tc_attn_layout_ok(const void* const* ptrs, int n, const int64_t* s, int D) {
+  if (!head_strides_ok(s[0], s[1], s[2], D) || !head_strides_ok(s[3], s[4], s[5], D)) return false;
+  for (int i = 0; i < n; ++i)
+    if (!aligned(ptrs[i], 16)) return false;
+  return true;
+}
 
 int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse, int B, int NH, int T,
                 int D, const int64_t* s, float scale, cudaStream_t stream) {
-  (void)D;
-  if (!head_strides_ok(s[0], s[1], s[2]) || !head_strides_ok(s[3], s[4], s[5]) || !aligned(q, 16) || !aligned(k, 16) ||
+  if (!head_strides_ok(s[0], s[1], s[2], D) || !head_strides_ok(s[3], s[4], s[5], D) || !aligned(q, 16) || !aligned(k, 16) ||
       !aligned(v, 16) || !aligned(o, 16)) {
     set_error("attn_fwd: the tensor-core path needs 16-byte aligned bf16 tensors with strides that are "
               "multiples of 8 elements");
     return ATTN_ERR_ARG;
   }
   FwdMaps maps;
-  if (!make_head_map(&maps.q, q, B, NH, T, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.k, k, B, NH, T, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.v, v, B, NH, T, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.o, o, B, NH, T, s[3], s[4], s[5]))
+  if (!make_head_map(&maps.q, q, B, NH, T, D, s[0], s[1], s[2]) ||
+      !make_head_map(&maps.k, k, B, NH, T, D, s[0], s[1], s[2]) ||
+      !make_head_map(&maps.v, v, B, NH, T, D, s[0], s[1], s[2]) ||
+      !make_head_map(&maps.o, o, B, NH, T, D, s[3], s[4], s[5]))
     return ATTN_ERR_CUDA;
   FwdParams p;
   p.NH = NH;

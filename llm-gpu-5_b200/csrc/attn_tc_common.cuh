@@ -1,6 +1,9 @@
-// Shared pieces of the tcgen05 attention kernels (head_dim 64, bf16): tile constants, the 4D TMA
-// maps that read a [B, T, NH, 64] or [B, NH, T, 64] operand through its element strides, and the
-// host-side checks of those strides.
+// Shared pieces of the tcgen05 attention kernels (bf16): tile constants, the 4D TMA maps that read
+// a [B, T, NH, D] or [B, NH, T, D] operand through its element strides, and the host-side checks
+// of those strides.  The kernels work on 64-wide head tiles; a head_dim D < 64 (a multiple of 8)
+// is served by the same kernels: the maps keep D as the tensor's inner extent with a 64-wide box,
+// so TMA loads fill columns D..63 with zeros (which leaves Q K^T, P V and every gradient
+// unchanged) and TMA stores clip them.
 #pragma once
 
 #include "tc_common.cuh"
@@ -8,7 +11,7 @@
 namespace attn {
 
 constexpr int AT_TILE = 128;                       // query / key rows per tile
-constexpr int AT_D = 64;                           // head_dim handled by the tensor-core kernels
+constexpr int AT_D = 64;                           // head tile width of the tensor-core kernels (head_dim <= 64)
 constexpr int AT_TILE_BYTES = AT_TILE * AT_D * 2;  // 16 KB bf16 tile, 128 B per row
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
@@ -35,19 +38,23 @@ __device__ __forceinline__ void store_tile(const TileMap& tm, const void* src, i
     tma_store_4d(&tm.map, src, 0, t0, h, b);
 }
 
+// head_dim values the tensor-core kernels serve: multiples of 8 (16-byte rows) up to the tile width.
+inline bool tc_head_dim_ok(int D) { return D >= 8 && D <= AT_D && D % 8 == 0; }
+
 // Element strides usable by TMA: 16-byte multiples and a row pitch of at least one head.
-inline bool head_strides_ok(int64_t sb, int64_t st, int64_t sh) {
-  return sb % 8 == 0 && st % 8 == 0 && sh % 8 == 0 && st >= AT_D;
+inline bool head_strides_ok(int64_t sb, int64_t st, int64_t sh, int D) {
+  return sb % 8 == 0 && st % 8 == 0 && sh % 8 == 0 && st >= D;
 }
 
-// 4D map over a bf16 tensor with element (b, t, h, d) at base[b*sb + t*st + h*sh + d]; the two
-// middle dimensions are ordered by stride so the map's strides increase.
-inline bool make_head_map(TileMap* tm, const void* base, int B, int NH, int T, int64_t sb, int64_t st,
-                          int64_t sh) {
+// 4D map over a bf16 tensor with element (b, t, h, d) at base[b*sb + t*st + h*sh + d], d < D; the
+// two middle dimensions are ordered by stride so the map's strides increase.  The box is always
+// 64 wide in d (columns D..63 read as zeros, are not written).
+inline bool make_head_map(TileMap* tm, const void* base, int B, int NH, int T, int D, int64_t sb,
+                          int64_t st, int64_t sh) {
   uint64_t dims[4], strides[3];
   uint32_t box[4];
   tm->h_first = sh <= st ? 1 : 0;
-  dims[0] = AT_D;
+  dims[0] = D;
   box[0] = AT_D;
   if (tm->h_first) {
     dims[1] = NH; dims[2] = T; dims[3] = B;

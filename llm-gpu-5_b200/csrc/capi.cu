@@ -139,6 +139,7 @@ size_t decode_ws(int, int, int, int);
 int decode(const void*, const void*, const void*, void*, float*, int, int, int, int, int64_t,
            int64_t, int64_t, int64_t, int64_t, float, int, float*, cudaStream_t);
 bool tc_fwd_supported(int D, int dtype);
+bool tc_attn_layout_ok(const void* const* ptrs, int n, const int64_t* s, int D);
 int attn_fwd_tc(const void*, const void*, const void*, void*, float*, int, int, int, int,
                 const int64_t*, float, cudaStream_t);
 bool tc_bwd_supported(int D, int dtype);
@@ -201,7 +202,9 @@ int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, i
   const size_t a = 4 * elem_size(dtype);
   ATTN_REQUIRE(aligned(q, a) && aligned(k, a) && aligned(v, a) && aligned(o, a),
                "attn_fwd: q/k/v/o must be %zu-byte aligned", a);
-  if (tc_fwd_supported(D, dtype))
+  const void* tens[4] = {q, k, v, o};
+  // tensor-core path for bf16 head_dim <= 64 whenever the layout suits TMA; CUDA cores otherwise
+  if (tc_fwd_supported(D, dtype) && tc_attn_layout_ok(tens, 4, st, D))
     return attn_fwd_tc(q, k, v, o, lse, B, NH, T, D, st, scale, as_stream(stream));
   return attn_fwd_simt(q, k, v, o, lse, B, NH, T, D, st, scale, dtype, as_stream(stream));
 }
@@ -233,7 +236,9 @@ int attn_bwd(const void* q, const void* k, const void* v, const void* o, const v
   ATTN_REQUIRE(aligned(q, a) && aligned(k, a) && aligned(v, a) && aligned(o, a) && aligned(dout, a) &&
                    aligned(dq, a) && aligned(dk, a) && aligned(dv, a),
                "attn_bwd: tensors must be %zu-byte aligned", a);
-  if (tc_bwd_supported(D, dtype))
+  const void* tens[8] = {q, k, v, o, dout, dq, dk, dv};
+  // the tensor-core workspace (attn_bwd_workspace_size) also covers the CUDA-core path
+  if (tc_bwd_supported(D, dtype) && tc_attn_layout_ok(tens, 8, st, D))
     return attn_bwd_tc(q, k, v, o, dout, lse, dq, dk, dv, workspace, B, NH, T, D, st, scale,
                        as_stream(stream));
   return attn_bwd_simt(q, k, v, o, dout, lse, dq, dk, dv, (float*)workspace, B, NH, T, D, st, scale,

@@ -14,14 +14,16 @@ template <typename TI, typename TO>
 __global__ void __launch_bounds__(256)
 gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* __restrict__ Bm,
                  int64_t ldb, int b_trans, TO* __restrict__ C, int64_t ldc,
-                 const float* __restrict__ bias, int M, int N, int K, int accumulate) {
+                 const float* __restrict__ bias, int M, int N, int K, int accumulate, int k_chunk) {
   __shared__ __align__(16) float As[SG_BK][SG_BM];
   __shared__ __align__(16) float Bs[SG_BK][SG_BN];
   const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
   const int m0 = blockIdx.y * SG_BM, n0 = blockIdx.x * SG_BN;
+  const int k_begin = blockIdx.z * k_chunk, k_end = min(K, k_begin + k_chunk);
+  const bool split = gridDim.z > 1;
   float acc[4][4] = {};
 
-  for (int k0 = 0; k0 < K; k0 += SG_BK) {
+  for (int k0 = k_begin; k0 < k_end; k0 += SG_BK) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int e = tid + 256 * i;
@@ -29,14 +31,14 @@ gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* _
       if (a_trans) { kk = e / SG_BM; mm = e % SG_BM; } else { mm = e / SG_BK; kk = e % SG_BK; }
       const int gm = m0 + mm, gk = k0 + kk;
       float val = 0.f;
-      if (gm < M && gk < K)
+      if (gm < M && gk < k_end)
         val = Elem<TI>::load(A + (a_trans ? (int64_t)gk * lda + gm : (int64_t)gm * lda + gk));
       As[kk][mm] = val;
       int nn;
       if (b_trans) { nn = e / SG_BK; kk = e % SG_BK; } else { kk = e / SG_BN; nn = e % SG_BN; }
       const int gn = n0 + nn, gk2 = k0 + kk;
       float bv = 0.f;
-      if (gn < N && gk2 < K)
+      if (gn < N && gk2 < k_end)
         bv = Elem<TI>::load(Bm + (b_trans ? (int64_t)gn * ldb + gk2 : (int64_t)gk2 * ldb + gn));
       Bs[kk][nn] = bv;
     }
@@ -62,8 +64,12 @@ gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* _
       const int gn = n0 + tx * 4 + j;
       if (gn >= N) continue;
       float val = acc[i][j];
-      if (bias) val += bias[gn];
+      if (bias && blockIdx.z == 0) val += bias[gn];
       TO* dst = C + (int64_t)gm * ldc + gn;
+      if (split) {  // float32 C only (host-checked)
+        atomicAdd(reinterpret_cast<float*>(dst), val);
+        continue;
+      }
       if (accumulate) val += Elem<TO>::load(dst);
       Elem<TO>::store(dst, val);
     }
@@ -74,19 +80,41 @@ int gemm_simt(const void* A, int64_t lda, int a_trans, const void* B, int64_t ld
               int ab_dtype, void* C, int64_t ldc, int c_dtype, const float* bias, int M, int N,
               int K, int accumulate, cudaStream_t s) {
   dim3 grid((N + SG_BN - 1) / SG_BN, (M + SG_BM - 1) / SG_BM);
+  // split K when the output tiles fill less than two waves and K is long (float32 C only)
+  int splits = 1;
+  const int64_t tiles = (int64_t)grid.x * grid.y, want = 2 * 148;
+  if (c_dtype == ATTN_F32 && tiles < want && K >= 512) {
+    splits = (int)((want + tiles - 1) / tiles);
+    const int max_splits = K / 256;  // at least 256 of K per split
+    if (splits > max_splits) splits = max_splits;
+    if (splits > 64) splits = 64;
+  }
+  int k_chunk = K;
+  if (splits > 1) {
+    k_chunk = ((K + splits - 1) / splits + SG_BK - 1) / SG_BK * SG_BK;
+    splits = (K + k_chunk - 1) / k_chunk;
+  }
+  if (splits > 1 && !accumulate) {
+    cudaError_t e = cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s);
+    if (e != cudaSuccess) {
+      set_error("gemm_simt: clearing C for the K splits failed: %s", cudaGetErrorString(e));
+      return ATTN_ERR_CUDA;
+    }
+  }
+  grid.z = splits;
   if (ab_dtype == ATTN_F32 && c_dtype == ATTN_F32)
     gemm_simt_kernel<float, float><<<grid, 256, 0, s>>>((const float*)A, lda, a_trans, (const float*)B,
-        ldb, b_trans, (float*)C, ldc, bias, M, N, K, accumulate);
+        ldb, b_trans, (float*)C, ldc, bias, M, N, K, accumulate, k_chunk);
   else if (ab_dtype == ATTN_F32 && c_dtype == ATTN_BF16)
     gemm_simt_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>((const float*)A, lda, a_trans,
-        (const float*)B, ldb, b_trans, (__nv_bfloat16*)C, ldc, bias, M, N, K, accumulate);
+        (const float*)B, ldb, b_trans, (__nv_bfloat16*)C, ldc, bias, M, N, K, accumulate, k_chunk);
   else if (ab_dtype == ATTN_BF16 && c_dtype == ATTN_F32)
     gemm_simt_kernel<__nv_bfloat16, float><<<grid, 256, 0, s>>>((const __nv_bfloat16*)A, lda, a_trans,
-        (const __nv_bfloat16*)B, ldb, b_trans, (float*)C, ldc, bias, M, N, K, accumulate);
+        (const __nv_bfloat16*)B, ldb, b_trans, (float*)C, ldc, bias, M, N, K, accumulate, k_chunk);
   else
     gemm_simt_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)A, lda,
         a_trans, (const __nv_bfloat16*)B, ldb, b_trans, (__nv_bfloat16*)C, ldc, bias, M, N, K,
-        accumulate);
+        accumulate, k_chunk);
   count_launch();
   return check_launch("gemm_simt_kernel");
 }
