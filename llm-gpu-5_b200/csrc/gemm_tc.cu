@@ -5,7 +5,7 @@
 // core/kernels.py:119-140) and the projection gradients of its backward (model/gpt.py:666-689).
 //
 // Persistent, warp-specialised kernel, one CTA per SM:
-//   warp 0      TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 3-stage ring
+//   warp 0      TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 4-stage ring
 //   warp 1      TMEM allocation and the single MMA-issuing thread: 4 x tcgen05.mma (128x256x16)
 //               per 64-deep K block, accumulating in TMEM
 //   warps 2-5   epilogue: tcgen05.ld of the 128x256 fp32 accumulator (one row per thread), bias,
@@ -23,13 +23,13 @@
 
 namespace attn {
 
-constexpr int GT_BM = 128, GT_BN = 256, GT_BK = 64, GT_STAGES = 3;
+constexpr int GT_BM = 128, GT_BN = 256, GT_BK = 64, GT_STAGES = 4;
 constexpr int GT_THREADS = 192;
 constexpr int GT_A_BYTES = GT_BM * GT_BK * 2;  // 16 KB
 constexpr int GT_B_BYTES = GT_BN * GT_BK * 2;  // 32 KB
 constexpr int GT_STAGE_BYTES = GT_A_BYTES + GT_B_BYTES;
 constexpr int GT_EPI_BYTES = GT_BM * 128;      // one 128-row x 128-byte output chunk (16 KB)
-constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + 2 * GT_EPI_BYTES + 1024 + 256;
+constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + 2 * GT_EPI_BYTES + GT_BN * 4 /*bias*/ + 1024 + 256;
 constexpr uint32_t GT_TMEM_COLS = 512;
 
 struct GemmParams {
@@ -111,7 +111,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi = smem + GT_STAGES * GT_STAGE_BYTES;  // [2] output staging chunks
-  uint64_t* full = reinterpret_cast<uint64_t*>(epi + 2 * GT_EPI_BYTES);
+  float* s_bias = reinterpret_cast<float*>(epi + 2 * GT_EPI_BYTES);  // the tile's bias columns
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_bias + GT_BN);
   uint64_t* empty = full + GT_STAGES;
   uint64_t* tfull = empty + GT_STAGES;
   uint64_t* tempty = tfull + 2;
@@ -232,6 +233,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * GT_BN;
+      const bool add_bias = p.bias && kb0 == 0;
+      if (add_bias) {  // the tile's 256 bias values, read once into shared memory
+        // (every thread has passed the previous tile's last read of s_bias: it precedes that
+        // chunk's first barrier)
+#pragma unroll
+        for (int i = 0; i < GT_BN / 128; ++i) {
+          const int n = tn * GT_BN + row + 128 * i;
+          s_bias[row + 128 * i] = n < p.N ? __ldg(p.bias + n) : 0.f;
+        }
+        named_bar_sync(1, 128);
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < GT_BN; c0 += cols) {
         uint32_t r[64];
@@ -247,10 +259,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         float v[64];
 #pragma unroll
         for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
-        if (p.bias && kb0 == 0) {
+        if (add_bias) {  // broadcast reads; columns past N hold 0
+          const float4* b4 = reinterpret_cast<const float4*>(s_bias + c0);
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i < cols && n0 + i < p.N) v[i] += __ldg(p.bias + n0 + i);
+          for (int i = 0; i < 16; ++i) {
+            if (4 * i < cols) {
+              const float4 bb = b4[i];
+              v[4 * i] += bb.x;
+              v[4 * i + 1] += bb.y;
+              v[4 * i + 2] += bb.z;
+              v[4 * i + 3] += bb.w;
+            }
+          }
         }
         uint32_t w[32];
         if (p.c_bf16) {
