@@ -175,6 +175,15 @@ int attn_cast_colsum_f32(const float* X, int64_t ldx, int M, int N, void* Y, int
                          float* out, int accumulate, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/*
+ * Y[m, n] = bf16(X[m, n]) for n < N, Y[m, N] = 1, Y[m, n] = 0 for N < n < ldy (X float32 [M][ldx],
+ * Y bf16 [M][ldy], ldy > N and a multiple of 8).  The bf16 input of the QKV projection with a ones
+ * column: the weight-gradient GEMM Y^T dQKV over N+1 rows then yields dWqkv and, as its last row,
+ * dbqkv = sum over tokens of dQKV (model/gpt.py:687-688) without a separate column-sum pass.
+ */
+int attn_cast_rows_ones_bf16(const float* x, int64_t ldx, int M, int N, void* y, int64_t ldy,
+                             void* stream);
+
 /* y[i] = bf16(x[i]) (round to nearest even), n elements. */
 int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream);
 

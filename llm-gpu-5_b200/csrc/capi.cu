@@ -130,6 +130,7 @@ int gemm_simt(const void*, int64_t, int, const void*, int64_t, int, int, void*, 
 int split_heads(const float*, float*, float*, float*, int, int, int, int, cudaStream_t);
 int merge_heads(const float*, float*, int, int, int, int, cudaStream_t);
 int cast_f32_bf16(const float*, void*, int64_t, cudaStream_t, int);
+int cast_rows_ones(const float*, int64_t, int, int, void*, int64_t, cudaStream_t, int);
 size_t colsum_ws(int, int);
 int colsum(const void*, int, int64_t, int, int, float*, int, void*, cudaStream_t);
 int cast_colsum(const float*, int64_t, int, int, void*, int64_t, float*, int, void*, cudaStream_t);
@@ -332,6 +333,16 @@ int attn_cast_colsum_f32(const float* X, int64_t ldx, int M, int N, void* Y, int
     return ATTN_ERR_WORKSPACE;
   }
   return cast_colsum(X, ldx, M, N, Y, ldy, out, accumulate, workspace, as_stream(stream));
+}
+
+int attn_cast_rows_ones_bf16(const float* x, int64_t ldx, int M, int N, void* y, int64_t ldy,
+                             void* stream) {
+  clear_error();
+  ATTN_REQUIRE(x && y, "attn_cast_rows_ones_bf16: null pointer argument");
+  ATTN_REQUIRE(M > 0 && N > 0 && ldx >= N, "attn_cast_rows_ones_bf16: bad shape");
+  ATTN_REQUIRE(ldy > N && ldy % 8 == 0, "attn_cast_rows_ones_bf16: ldy must exceed N and be a multiple of 8");
+  ATTN_REQUIRE(aligned(y, 16), "attn_cast_rows_ones_bf16: y must be 16-byte aligned");
+  return cast_rows_ones(x, ldx, M, N, y, ldy, as_stream(stream), sm_count());
 }
 
 int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream) {

@@ -173,6 +173,50 @@ int merge_heads(const float* ch, float* ctx, int B, int T, int NH, int HD, cudaS
   return check_launch("merge_heads_kernel");
 }
 
+// fp32 [M][ldx] -> bf16 [M][ldy] with a ones column appended: y[m, n] = bf16(x[m, n]) for n < N,
+// y[m, N] = 1, y[m, n] = 0 for N < n < ldy.  One thread writes 8 columns (16 bytes) of a row
+// (grid-stride over rows x ldy/8 chunks).  A GEMM with y^T as its left operand then produces the
+// column sums of its right operand as one extra output row.
+__global__ void cast_rows_ones_kernel(const float* __restrict__ x, int64_t ldx, int M, int N,
+                                      __nv_bfloat16* __restrict__ y, int64_t ldy, int vec) {
+  const int64_t chunks = ldy / 8, total = (int64_t)M * chunks;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t m = i / chunks;
+    const int n0 = (int)(i - m * chunks) * 8;
+    const float* xr = x + m * ldx;
+    float v[8];
+    if (vec && n0 + 8 <= N) {
+      const float4 a = *reinterpret_cast<const float4*>(xr + n0);
+      const float4 b = *reinterpret_cast<const float4*>(xr + n0 + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = n0 + j < N ? xr[n0 + j] : (n0 + j == N ? 1.f : 0.f);
+    }
+    uint4 u;
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]), p1 = __floats2bfloat162_rn(v[2], v[3]);
+    __nv_bfloat162 p2 = __floats2bfloat162_rn(v[4], v[5]), p3 = __floats2bfloat162_rn(v[6], v[7]);
+    u.x = *reinterpret_cast<uint32_t*>(&p0);
+    u.y = *reinterpret_cast<uint32_t*>(&p1);
+    u.z = *reinterpret_cast<uint32_t*>(&p2);
+    u.w = *reinterpret_cast<uint32_t*>(&p3);
+    *reinterpret_cast<uint4*>(y + m * ldy + n0) = u;
+  }
+}
+
+int cast_rows_ones(const float* x, int64_t ldx, int M, int N, void* y, int64_t ldy, cudaStream_t s,
+                   int sms) {
+  const int vec = (N % 4 == 0) && (ldx % 4 == 0) && aligned(x, 16);
+  const int64_t total = (int64_t)M * (ldy / 8);
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = (int64_t)sms * 8;
+  if (blocks > cap) blocks = cap;
+  cast_rows_ones_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, ldx, M, N, (__nv_bfloat16*)y, ldy, vec);
+  count_launch();
+  return check_launch("cast_rows_ones_kernel");
+}
+
 // fp32 -> bf16, 8 elements per thread per step when 16-byte aligned (grid-stride).
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                      int64_t n, int vec) {

@@ -238,15 +238,18 @@ class MultiHeadAttention:
         x = _as_tensor(gpu_input, M * C)
         if dt == torch.bfloat16:
             with self._rng("cast"):
-                x_op = ops.cast_bf16(x)
+                # bf16 x with a ones column (16-byte row pitch): the backward's weight-gradient
+                # GEMM over C + 1 rows then also produces the bias gradient
+                x_op = ops.cast_rows_ones(x.view(M, C))
                 w_qkv = ops.cast_bf16(self.c_attn_w.weights)
                 w_o = ops.cast_bf16(self.c_proj_w.weights)
         else:
-            x_op = x.clone()  # the caller may overwrite its input (residual adds are in place)
+            x_op = x.clone().view(M, C)  # the caller may overwrite its input (residual adds are in place)
             w_qkv, w_o = self.c_attn_w.weights, self.c_proj_w.weights
+        ldx = x_op.shape[1]
         qkv = torch.empty((M, 3 * C), dtype=dt, device="cuda")
         with self._rng("gemm_qkv"):
-            ops.gemm(x_op.data_ptr(), C, False, w_qkv.data_ptr(), 3 * C, False, dt, qkv.data_ptr(),
+            ops.gemm(x_op.data_ptr(), ldx, False, w_qkv.data_ptr(), 3 * C, False, dt, qkv.data_ptr(),
                      3 * C, dt, M, 3 * C, C, bias=self.c_attn_b.weights.data_ptr())
         ctx = torch.empty((M, C), dtype=dt, device="cuda")
         lse = torch.empty((B, NH, T), dtype=torch.float32, device="cuda")
@@ -304,11 +307,20 @@ class MultiHeadAttention:
                                    tv(gb), tv(gb + C * es), tv(gb + 2 * C * es), B, NH, T, D,
                                    1.0 / math.sqrt(D), dt)
         # input projection: dWqkv = x^T dQKV, dbqkv = sum(dQKV), dX = dQKV Wqkv^T  (gpt.py:687-689)
-        with self._rng("gemm_dwqkv"):
-            ops.gemm(c["x"].data_ptr(), C, True, gb, 3 * C, False, dt, self.c_attn_w.grads.data_ptr(),
-                     3 * C, torch.float32, C, 3 * C, M, accumulate=accumulate)
-        with self._rng("colsum"):
-            ops.colsum(gb, dt, 3 * C, M, 3 * C, self.c_attn_b.grads, accumulate=accumulate)
+        x_op = c["x"]
+        if x_op.shape[1] > C:
+            # x carries a ones column: the C + 1 output rows are [dWqkv; dbqkv], and dbqkv follows
+            # dWqkv in the flat gradient buffer, so one GEMM writes both
+            with self._rng("gemm_dwqkv"):
+                ops.gemm(x_op.data_ptr(), x_op.shape[1], True, gb, 3 * C, False, dt,
+                         self.c_attn_w.grads.data_ptr(), 3 * C, torch.float32, C + 1, 3 * C, M,
+                         accumulate=accumulate)
+        else:
+            with self._rng("gemm_dwqkv"):
+                ops.gemm(x_op.data_ptr(), C, True, gb, 3 * C, False, dt, self.c_attn_w.grads.data_ptr(),
+                         3 * C, torch.float32, C, 3 * C, M, accumulate=accumulate)
+            with self._rng("colsum"):
+                ops.colsum(gb, dt, 3 * C, M, 3 * C, self.c_attn_b.grads, accumulate=accumulate)
         if self.grad_sync_group is not None:
             # overlaps the dX GEMM below on NCCL's stream
             self._grad_sync_work = dp.allreduce_grads(self.flat_grads, self.grad_sync_group, async_op=True)
@@ -361,7 +373,10 @@ class MultiHeadAttention:
     @property
     def cache_input(self):
         c = self._cache
-        return None if c is None else c["x"].float().cpu().numpy()
+        if c is None:
+            return None
+        C = self.c_proj_w.weights.shape[0]
+        return c["x"][:, :C].float().cpu().numpy()  # without the bf16 path's ones column
 
     @property
     def cache_lse(self):

@@ -160,6 +160,18 @@ def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     return out
 
 
+def cast_rows_ones(x: torch.Tensor) -> torch.Tensor:
+    """float32 [M, N] -> bf16 [M, L] with L = N + 1 rounded up to a multiple of 8 (16-byte rows):
+    bf16(x), then a column of ones, then zeros.  Used as the QKV projection's input so the
+    weight-gradient GEMM also yields the bias gradient."""
+    assert x.dtype == torch.float32 and x.is_contiguous() and x.dim() == 2
+    M, N = x.shape
+    L = (N + 1 + 7) // 8 * 8
+    out = torch.empty((M, L), dtype=torch.bfloat16, device=x.device)
+    call("attn_cast_rows_ones_bf16", x.data_ptr(), N, M, N, out.data_ptr(), L, _stream())
+    return out
+
+
 def split_heads(qkv: int, q: int, k: int, v: int, B: int, T: int, NH: int, HD: int):
     """split_heads_kernel (core/mha_kernels.py:534-558) on float32 device buffers."""
     call("attn_split_heads", qkv, q, k, v, B, T, NH, HD, _stream())

@@ -224,6 +224,31 @@ def test_colsum_and_cast(pkg, cuda_dev, M, N):
     assert O.rel_err(out.cpu().numpy(), ref) < 1e-5
 
 
+@pytest.mark.parametrize("M,N", [(5, 16), (1000, 768), (333, 20)])
+def test_cast_rows_ones_and_fused_bias_gradient(pkg, cuda_dev, M, N):
+    """bf16(X) | 1 | 0..: the weight-gradient GEMM over N + 1 rows yields X^T G and, as its last
+    row, the column sums of G (the bias gradient), exactly as a separate column-sum pass would."""
+    torch = _torch()
+    rng = np.random.default_rng(M * 7 + N)
+    X = rng.standard_normal((M, N)).astype(np.float32)
+    G = rng.standard_normal((M, 3 * N)).astype(np.float32)
+    xa = pkg.mha_ops.cast_rows_ones(_dev(X))
+    torch.cuda.synchronize()
+    L = xa.shape[1]
+    assert xa.shape[0] == M and L % 8 == 0 and N < L <= N + 8
+    assert torch.equal(xa[:, :N], _dev(X).to(torch.bfloat16))
+    assert torch.all(xa[:, N] == 1) and torch.all(xa[:, N + 1:] == 0)
+    tg = _dev(G, torch.bfloat16)
+    out = torch.empty((N + 1, 3 * N), dtype=torch.float32, device="cuda")
+    pkg.mha_ops.gemm(xa.data_ptr(), L, True, tg.data_ptr(), 3 * N, False, torch.bfloat16, out.data_ptr(),
+                     3 * N, torch.float32, N + 1, 3 * N, M)
+    torch.cuda.synchronize()
+    Xb, Gb = _bf16_round(X).astype(np.float64), _bf16_round(G).astype(np.float64)
+    got = out.cpu().numpy()
+    assert O.rel_err(got[:N], Xb.T @ Gb) < 1e-5
+    assert O.rel_err(got[N], Gb.sum(0)) < 1e-5
+
+
 def test_split_merge_heads_reference_semantics(pkg, cuda_dev):
     torch = _torch()
     B, T, NH, HD = 2, 7, 3, 4
