@@ -229,8 +229,11 @@ class MultiHeadAttention:
         return C, NH, C // NH
 
     # ---------------------------------------------------------------- forward
-    def forward(self, gpu_input, B: int, T: int):
-        """x [B*T, C] float32 (device) -> DeviceBuffer [B*T, C] float32 (caller frees)."""
+    def forward(self, gpu_input, B: int, T: int, kv_cache: "KVCache | None" = None):
+        """x [B*T, C] float32 (device) -> DeviceBuffer [B*T, C] float32 (caller frees).
+
+        With ``kv_cache`` (from ``new_kv_cache``) the prompt's keys and values are also stored in
+        it, so that ``forward_decode`` can continue the sequences one token at a time."""
         C, NH, D = self._shape()
         M = B * T
         dt = self._dt
@@ -251,6 +254,8 @@ class MultiHeadAttention:
         with self._rng("gemm_qkv"):
             ops.gemm(x_op.data_ptr(), ldx, False, w_qkv.data_ptr(), 3 * C, False, dt, qkv.data_ptr(),
                      3 * C, dt, M, 3 * C, C, bias=self.c_attn_b.weights.data_ptr())
+        if kv_cache is not None:
+            kv_cache.store(qkv.view(B, T, 3 * C), 0)
         ctx = torch.empty((M, C), dtype=dt, device="cuda")
         lse = torch.empty((B, NH, T), dtype=torch.float32, device="cuda")
         es = qkv.element_size()
@@ -365,6 +370,45 @@ class MultiHeadAttention:
     def cache_v(self):
         return self._qkv_heads(2)
 
+    # ---------------------------------------------------------------- incremental decoding
+    def new_kv_cache(self, B: int, max_len: int) -> "KVCache":
+        """A key/value cache for ``B`` sequences of up to ``max_len`` tokens, in this module's
+        compute precision."""
+        C, NH, D = self._shape()
+        return KVCache(B, max_len, NH, D, self._dt)
+
+    def forward_decode(self, gpu_input, B: int, kv_cache: "KVCache"):
+        """One new token per sequence: x [B, C] float32 -> DeviceBuffer [B, C] float32.
+
+        Equals the last rows of ``forward`` over the whole sequence (causal attention, the new
+        token sees every cached one), which is what GenerationSession.generate recomputes for
+        every token (generate.py:611-628).  Here the token's key and value are appended to the
+        cache and one ``attn_decode`` call attends over it: O(L) per token instead of O(L^2).
+        No backward (inference only; the training caches are left untouched)."""
+        C, NH, D = self._shape()
+        dt = self._dt
+        L = kv_cache.length
+        if kv_cache.B != B or L >= kv_cache.max_len:
+            raise RuntimeError(f"forward_decode: cache holds {kv_cache.B} sequences, {L} of "
+                               f"{kv_cache.max_len} positions used")
+        x = _as_tensor(gpu_input, B * C).view(B, C)
+        if dt == torch.bfloat16:
+            x_op = ops.cast_bf16(x)
+            w_qkv = ops.cast_bf16(self.c_attn_w.weights)
+            w_o = ops.cast_bf16(self.c_proj_w.weights)
+        else:
+            x_op, w_qkv, w_o = x, self.c_attn_w.weights, self.c_proj_w.weights
+        qkv = torch.empty((B, 3 * C), dtype=dt, device="cuda")
+        ops.gemm(x_op.data_ptr(), C, False, w_qkv.data_ptr(), 3 * C, False, dt, qkv.data_ptr(), 3 * C, dt,
+                 B, 3 * C, C, bias=self.c_attn_b.weights.data_ptr())
+        kv_cache.store(qkv.view(B, 1, 3 * C), L)
+        q = qkv[:, :C].contiguous().view(B, NH, D)  # q and the output share one layout
+        ctx = ops.decode(q, kv_cache.k[:, :L + 1], kv_cache.v[:, :L + 1], 1.0 / math.sqrt(D))
+        out = torch.empty((B, C), dtype=torch.float32, device="cuda")
+        ops.gemm(ctx.data_ptr(), C, False, w_o.data_ptr(), C, False, dt, out.data_ptr(), C, torch.float32,
+                 B, C, C, bias=self.c_proj_b.weights.data_ptr())
+        return DeviceBuffer(out)
+
     @property
     def cache_context(self):
         c = self._cache
@@ -397,3 +441,25 @@ class MultiHeadAttention:
                                 HeadView.tokens(base + C * es, T, 3 * C, D), c["lse"], B, NH, T, D,
                                 1.0 / math.sqrt(D), self._dt)
         return p.cpu().numpy()
+
+
+class KVCache:
+    """Keys and values of B sequences in token layout [B, max_len, NH, D] (the layout the
+    projection writes and ``attn_decode`` reads), plus the number of positions filled."""
+
+    def __init__(self, B: int, max_len: int, NH: int, D: int, dtype: torch.dtype):
+        self.B, self.max_len, self.NH, self.D = B, max_len, NH, D
+        self.k = torch.empty((B, max_len, NH, D), dtype=dtype, device="cuda")
+        self.v = torch.empty((B, max_len, NH, D), dtype=dtype, device="cuda")
+        self.length = 0
+
+    def store(self, qkv: torch.Tensor, pos: int):
+        """Copy K and V of qkv [B, T, 3C] (the fused projection's output) to positions
+        pos .. pos+T-1 and extend the filled length to pos+T."""
+        B, T, C3 = qkv.shape
+        C = C3 // 3
+        if pos + T > self.max_len:
+            raise RuntimeError(f"KVCache: {pos + T} positions exceed max_len {self.max_len}")
+        self.k[:, pos:pos + T].copy_(qkv[:, :, C:2 * C].view(B, T, self.NH, self.D))
+        self.v[:, pos:pos + T].copy_(qkv[:, :, 2 * C:].view(B, T, self.NH, self.D))
+        self.length = max(self.length, pos + T)

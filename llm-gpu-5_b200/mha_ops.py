@@ -106,7 +106,10 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, scale:
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if out is None:
-        out = torch.empty_like(q)
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    # q and out are addressed with the same (b, h) strides
+    assert out.shape == q.shape and out.dtype == q.dtype and out.stride() == q.stride(), \
+        "decode: q and out must have the same shape, dtype and strides"
     need = lib.attn_decode_workspace_size(B, NH, L, D)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)

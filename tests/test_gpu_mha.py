@@ -145,3 +145,41 @@ def test_native_library_is_what_runs(pkg, cuda_dev):
     torch.cuda.synchronize()
     assert pkg.launch_count() - before >= 8
     out.free()
+
+
+@pytest.mark.parametrize("prec,tol,B,T0,steps,C,NH", [
+    ("fp32", 1e-5, 2, 5, 4, 64, 4),      # the reference's 'small' head_dim 16
+    ("bf16", 2e-2, 3, 130, 3, 256, 4),   # head_dim 64 on the tensor cores, prompt past one tile
+    ("bf16", 2e-2, 2, 17, 2, 256, 8),    # head_dim 32
+])
+def test_kv_cache_decode_matches_full_forward(pkg, cuda_dev, prec, tol, B, T0, steps, C, NH):
+    """Prompt forward with a KV cache, then one forward_decode per new token: each decode output
+    equals the corresponding row of one causal forward over the whole sequence (what
+    GenerationSession.generate recomputes per token, generate.py:611-628)."""
+    torch = _torch()
+    T = T0 + steps
+    inp = O.make_config_inputs(4, B, T, C, NH)
+    rng = np.random.default_rng(T * C)
+    inp["b_qkv"] = (rng.standard_normal(3 * C) * 0.1).astype(np.float32)  # exercise the biases too
+    inp["b_o"] = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
+                                                attention_precision=prec))
+    _load_weights(attn, inp)
+    x = inp["x"].reshape(B, T, C)
+    full = attn.forward(torch.from_numpy(np.ascontiguousarray(x.reshape(B * T, C))).cuda(), B, T)
+    ref = full.get().reshape(B, T, C)
+    full.free()
+    cache = attn.new_kv_cache(B, T)
+    prompt = attn.forward(torch.from_numpy(np.ascontiguousarray(x[:, :T0].reshape(B * T0, C))).cuda(), B, T0,
+                          kv_cache=cache)
+    assert O.rel_err(prompt.get().reshape(B, T0, C), ref[:, :T0]) < tol
+    prompt.free()
+    assert cache.length == T0
+    for t in range(T0, T):
+        y = attn.forward_decode(torch.from_numpy(np.ascontiguousarray(x[:, t])).cuda(), B, cache)
+        torch.cuda.synchronize()
+        assert O.rel_err(y.get(), ref[:, t]) < tol, (t, O.rel_err(y.get(), ref[:, t]))
+        y.free()
+    assert cache.length == T
+    with pytest.raises(RuntimeError):
+        attn.forward_decode(torch.zeros((B, C), device="cuda"), B, cache)  # cache full
