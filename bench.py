@@ -41,6 +41,9 @@ WORKLOADS = {
             global_batch=256, T=128, C=256, NH=8, prec="fp32", cpu_slice=16),
     3: dict(name="long context: causal MHA fwd+bwd, B=32 T=1024 C=512 NH=8 D=64, bf16",
             global_batch=32, T=1024, C=512, NH=8, prec="bf16", cpu_slice=1),
+    4: dict(name="generation-shaped decode: one query row per (batch, head) over an L=2048 K/V prefix, "
+                 "B=64 NH=8 D=64, bf16 K/V, fp32 softmax", global_batch=64, T=2048, C=512, NH=8, prec="bf16",
+            decode=True, cpu_slice=64),
     5: dict(name="data-parallel training step: causal MHA fwd+bwd, global B=512 T=512 C=768 NH=12 "
                  "D=64, bf16 operands / fp32 accumulation", global_batch=512, T=512, C=768, NH=12,
             prec="bf16", cpu_slice=2),
@@ -109,6 +112,19 @@ def cpu_baseline(cfg, budget_s=12.0, max_reps=30):
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return 0
+    if WORKLOADS[cfg].get("decode"):
+        w = WORKLOADS[cfg]
+        base = cpu_decode_baseline(w, reps=max(args.steps, 1))
+        line = dict(metric="causal attention decode tokens/sec", value=base["value"], unit="tokens/s",
+                    n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                    ms_per_step=base["seconds_per_sample"] * 1e3, higher_is_better=True, scaling="weak",
+                    vs_baseline=None, dtype="f32", data="synthetic", impl="reference",
+                    config=dict(workload=w["name"], batch=w["global_batch"], prefix_len=w["T"], heads=w["NH"],
+                                head_dim=w["C"] // w["NH"], parallelism="host cores"),
+                    cpu_baseline=base,
+                    e2e=dict(value=base["value"], unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+        print(json.dumps(line), flush=True)
         return 0
     from oracle import mha_oracle as oracle
     w = WORKLOADS[cfg]
@@ -396,7 +412,11 @@ def run_ours(args, cfg):
     tf = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tf):
         with open(tf) as f:
-            traffic = json.load(f).get(f"cfg{cfg}", {}).get(dom)
+            full = json.load(f).get(f"cfg{cfg}", {}).get(dom)
+        # recorded for the whole global batch on one GPU; every sequence is independent work, so
+        # a launch over this rank's B sequences moves B / global_batch of it
+        if full is not None and not args.batch:
+            traffic = full * B / GB
     total_flops = sum(op_flops(k, B, T, C, NH) for k in totals if op_flops(k, B, T, C, NH))
     line = dict(
         metric="causal attention fwd+bwd tokens/sec", value=value, unit="tokens/s", n_gpus=world,
@@ -422,12 +442,180 @@ def run_ours(args, cfg):
     return 0
 
 
+# ------------------------------------------------------------------------------ decode (cfg 4)
+def decode_inputs(B, NH, L, D, seed):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    return [rng.standard_normal(shape).astype(np.float32) for shape in ((B, NH, D), (B, L, NH, D), (B, L, NH, D))]
+
+
+def cpu_decode_baseline(w, reps=5):
+    """The oracle's float32 NumPy decode (oracle.decode_attention) over the whole workload."""
+    import numpy as np
+    from oracle import mha_oracle as oracle
+    B, L, NH = w["global_batch"], w["T"], w["NH"]
+    D = w["C"] // NH
+    q, k, v = decode_inputs(B, NH, L, D, 1004)
+    kt, vt = k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3)
+    oracle.decode_attention(q, kt, vt, 1.0 / D ** 0.5, dtype=np.float32)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.decode_attention(q, kt, vt, 1.0 / D ** 0.5, dtype=np.float32)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    return dict(value=B / best, unit="tokens/s", cores=cpu_threads(), kind="port",
+                sample=f"the whole step ({B} sequences x {NH} heads over L={L}), fp32 NumPy "
+                       f"(oracle/mha_oracle.py decode_attention), best of {reps}",
+                seconds_per_sample=best)
+
+
+def run_decode(args, cfg):
+    """One decode step = one attn_decode call for B sequences; inputs (q and two alternating
+    copies of the K/V cache, 268 MB each, so no call reads L2-resident data) are on the device."""
+    import torch
+    import importlib
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    pkg = importlib.import_module("llm-gpu-5_b200")
+    w = WORKLOADS[cfg]
+    B, L, NH = args.batch or w["global_batch"], w["T"], w["NH"]
+    D = w["C"] // NH
+    steps, warmup = args.steps, max(args.warmup, 3)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1004 + 7919 * rank)
+    q = torch.randn((B, NH, D), generator=gen, device="cuda").to(torch.bfloat16)
+    caches = [(torch.randn((B, L, NH, D), generator=gen, device="cuda").to(torch.bfloat16),
+               torch.randn((B, L, NH, D), generator=gen, device="cuda").to(torch.bfloat16)) for _ in range(2)]
+    out = torch.empty_like(q)
+    lse = torch.empty((B, NH), dtype=torch.float32, device="cuda")
+    ws = torch.empty(pkg.lib.attn_decode_workspace_size(B, NH, L, D), dtype=torch.uint8, device="cuda")
+
+    def step(i):
+        k, v = caches[i & 1]
+        pkg.mha_ops.decode(q, k, v, out=out, lse=lse, workspace=ws)
+
+    for i in range(warmup):
+        step(i)
+    clocks = ClockSampler(local)
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = pkg.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    launches = pkg.launch_count() - launches0
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / steps
+    # end to end through the public API: q from pinned host memory, the output back to the host
+    q_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    o_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    q_h.copy_(q)
+    for i in range(2):
+        q.copy_(q_h, non_blocking=True)
+        step(i)
+        o_h.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        q.copy_(q_h, non_blocking=True)
+        step(i)
+        o_h.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / steps
+    if rank != 0:
+        return 0
+    peaks, src = load_peaks()
+    kv_bytes = 2 * B * L * NH * D * 2
+    achieved = kv_bytes / (ms * 1e-3) / 1e9
+    peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    line = dict(
+        metric="causal attention decode tokens/sec", value=B * world / (ms * 1e-3), unit="tokens/s",
+        n_gpus=world, steps=steps, warmup=warmup, ms_per_step=ms, higher_is_better=True, scaling="weak",
+        vs_baseline=None, dtype="bf16", data="synthetic",
+        config=dict(workload=w["name"], batch=B, prefix_len=L, heads=NH, head_dim=D,
+                    parallelism="replicas" if world > 1 else "single GPU",
+                    l2="two alternating 268 MB K/V caches (larger than L2)"),
+        roofline=dict(bound="hbm", kernel="attn_decode", achieved=achieved, peak=peak, unit="GB/s",
+                      frac=achieved / peak, traffic=None, peak_source=f"{src} hbm_gbs",
+                      algorithmic_bytes=kv_bytes),
+        gpu_launches=launches,
+        e2e=dict(value=B * world / (e2e_ms * 1e-3), unit="tokens/s", h2d_bytes_per_step=q.numel() * 2 * world,
+                 d2h_bytes_per_step=out.numel() * 2 * world, ms_per_step=e2e_ms),
+        clocks=clk,
+    )
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_baseline(w)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ vendor libraries
+def run_vendor(args, cfg):
+    """Time NVIDIA's own B200 kernels on the same workload, for context: cuDNN attention through
+    torch.nn.functional.scaled_dot_product_attention (causal, bf16, [B, NH, T, D]) and cuBLAS
+    through torch.matmul for the six projection GEMMs.  Prints one JSON line; not a bench line."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import sdpa_kernel, SDPBackend
+    w = WORKLOADS[cfg]
+    B = args.batch or w["global_batch"]
+    T, C, NH = w["T"], w["C"], w["NH"]
+    D, M = C // NH, B * T
+    torch.manual_seed(0)
+
+    def timed(fn, reps=max(args.steps, 3)):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(reps):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        return s0.elapsed_time(s1) / reps
+
+    out = dict(workload=w["name"], batch=B)
+    q, k, v = (torch.randn(B, NH, T, D, device="cuda", dtype=torch.bfloat16).requires_grad_() for _ in range(3))
+    do = torch.randn(B, NH, T, D, device="cuda", dtype=torch.bfloat16)
+    for name, be in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION)):
+        try:
+            with sdpa_kernel(be):
+                fwd = timed(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True))
+                both = timed(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True).backward(do))
+            out[f"sdpa_{name}_fwd_ms"] = fwd
+            out[f"sdpa_{name}_fwd_bwd_ms"] = both
+        except Exception as e:  # a backend that does not support the shape on this build
+            out[f"sdpa_{name}"] = f"unavailable: {str(e).splitlines()[0][:120]}"
+    del q, k, v, do
+    x = torch.randn(M, C, device="cuda", dtype=torch.bfloat16)
+    wq = torch.randn(C, 3 * C, device="cuda", dtype=torch.bfloat16)
+    wo = torch.randn(C, C, device="cuda", dtype=torch.bfloat16)
+    g3 = torch.randn(M, 3 * C, device="cuda", dtype=torch.bfloat16)
+    g1 = torch.randn(M, C, device="cuda", dtype=torch.bfloat16)
+    gemms = dict(gemm_qkv=lambda: x @ wq, gemm_out=lambda: g1 @ wo, gemm_dwo=lambda: g1.t() @ g1,
+                 gemm_dctx=lambda: g1 @ wo.t(), gemm_dwqkv=lambda: x.t() @ g3, gemm_dx=lambda: g3 @ wq.t())
+    for name, fn in gemms.items():
+        out[f"cublas_{name}_ms"] = timed(fn)
+    print(json.dumps(dict(vendor=out)), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "vendor"], default="ours",
+                    help="vendor: time cuDNN attention and cuBLAS GEMMs on the same workload (context only)")
     ap.add_argument("--config", type=int, default=5, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
@@ -435,6 +623,10 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args, args.config)
+    if args.impl == "vendor":
+        return run_vendor(args, args.config)
+    if WORKLOADS[args.config].get("decode"):
+        return run_decode(args, args.config)
     return run_ours(args, args.config)
 
 
