@@ -184,6 +184,16 @@ int attn_cast_colsum_f32(const float* X, int64_t ldx, int M, int N, void* Y, int
 int attn_cast_rows_ones_bf16(const float* x, int64_t ldx, int M, int N, void* y, int64_t ldy,
                              void* stream);
 
+/*
+ * LayerNorm of the rows of X (float32 [M][ldx]): Y = (X - mean) * rsqrt(var + eps) * gamma + beta
+ * with the biased variance, as layernorm_kernel (core/kernels.py:75-110; the reference uses
+ * eps = 1e-5).  Y is float32 or bf16 [M][ldy]; with ones_col, Y[m, C] = 1 and the columns after it
+ * are 0 (the bf16 QKV-projection input of attn_cast_rows_ones_bf16).  Replaces the pre-attention
+ * LayerNorm of TransformerBlock.forward (model/gpt.py:778) and the cast that would follow it.
+ */
+int attn_layernorm(const float* x, int64_t ldx, const float* gamma, const float* beta, int M, int C,
+                   float eps, void* y, int64_t ldy, int y_dtype, int ones_col, void* stream);
+
 /* y[i] = bf16(x[i]) (round to nearest even), n elements. */
 int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream);
 

@@ -131,6 +131,8 @@ int split_heads(const float*, float*, float*, float*, int, int, int, int, cudaSt
 int merge_heads(const float*, float*, int, int, int, int, cudaStream_t);
 int cast_f32_bf16(const float*, void*, int64_t, cudaStream_t, int);
 int cast_rows_ones(const float*, int64_t, int, int, void*, int64_t, cudaStream_t, int);
+int layernorm_rows(const float*, int64_t, const float*, const float*, int, int, float, void*, int64_t, int, int,
+                   cudaStream_t);
 size_t colsum_ws(int, int);
 int colsum(const void*, int, int64_t, int, int, float*, int, void*, cudaStream_t);
 int cast_colsum(const float*, int64_t, int, int, void*, int64_t, float*, int, void*, cudaStream_t);
@@ -343,6 +345,18 @@ int attn_cast_rows_ones_bf16(const float* x, int64_t ldx, int M, int N, void* y,
   ATTN_REQUIRE(ldy > N && ldy % 8 == 0, "attn_cast_rows_ones_bf16: ldy must exceed N and be a multiple of 8");
   ATTN_REQUIRE(aligned(y, 16), "attn_cast_rows_ones_bf16: y must be 16-byte aligned");
   return cast_rows_ones(x, ldx, M, N, y, ldy, as_stream(stream), sm_count());
+}
+
+int attn_layernorm(const float* x, int64_t ldx, const float* gamma, const float* beta, int M, int C,
+                   float eps, void* y, int64_t ldy, int y_dtype, int ones_col, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(x && gamma && beta && y, "attn_layernorm: null pointer argument");
+  ATTN_REQUIRE(M > 0 && C > 0 && ldx >= C, "attn_layernorm: bad shape");
+  ATTN_REQUIRE(y_dtype == ATTN_F32 || y_dtype == ATTN_BF16, "attn_layernorm: bad output dtype");
+  ATTN_REQUIRE(ldy >= C + (ones_col ? 1 : 0), "attn_layernorm: ldy too small");
+  ATTN_REQUIRE(eps > 0.f, "attn_layernorm: eps must be positive");
+  ATTN_REQUIRE((const void*)x != (const void*)y, "attn_layernorm: x and y must not alias");
+  return layernorm_rows(x, ldx, gamma, beta, M, C, eps, y, ldy, y_dtype, ones_col, as_stream(stream));
 }
 
 int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream) {

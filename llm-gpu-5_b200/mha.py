@@ -244,10 +244,42 @@ class MultiHeadAttention:
                 # bf16 x with a ones column (16-byte row pitch): the backward's weight-gradient
                 # GEMM over C + 1 rows then also produces the bias gradient
                 x_op = ops.cast_rows_ones(x.view(M, C))
+        else:
+            x_op = x.clone().view(M, C)  # the caller may overwrite its input (residual adds are in place)
+        out = torch.empty((M, C), dtype=torch.float32, device="cuda")
+        self._forward_core(x_op, B, T, out, accumulate=False, kv_cache=kv_cache)
+        return DeviceBuffer(out)
+
+    def forward_residual(self, gpu_x, B: int, T: int, ln_gamma, ln_beta, eps: float = 1e-5):
+        """x += attn(LayerNorm(x)) in place on the residual stream x [B*T, C] float32.
+
+        Fuses the pre-attention part of TransformerBlock.forward (model/gpt.py:778-783):
+        ``ln1 = ln_op(x, gamma, beta)``, ``out = attn.forward(ln1)``, ``add_op(x, out)``.  One
+        LayerNorm kernel writes the QKV projection's operand directly (bf16 with the ones column on
+        the bf16 path), and the output projection adds ctx Wo + bo into x in its epilogue, so
+        neither the float32 LayerNorm output nor the attention output is written to memory.
+        ``backward`` afterwards is unchanged: its upstream gradient is dL/dx after the add."""
+        C, NH, D = self._shape()
+        M = B * T
+        dt = self._dt
+        self._cache = None
+        x = _as_tensor(gpu_x, M * C).view(M, C)
+        g, b = _as_tensor(ln_gamma, C), _as_tensor(ln_beta, C)
+        with self._rng("layernorm"):
+            x_op = ops.layernorm(x, g, b, eps, out_dtype=dt, ones_col=dt == torch.bfloat16)
+        self._forward_core(x_op, B, T, x, accumulate=True)
+
+    def _forward_core(self, x_op, B, T, out, accumulate, kv_cache=None):
+        """QKV projection of the prepared operand x_op [M, >= C], attention, output projection
+        into out [M, C] float32 (added to it when accumulate)."""
+        C, NH, D = self._shape()
+        M = B * T
+        dt = self._dt
+        if dt == torch.bfloat16:
+            with self._rng("cast"):
                 w_qkv = ops.cast_bf16(self.c_attn_w.weights)
                 w_o = ops.cast_bf16(self.c_proj_w.weights)
         else:
-            x_op = x.clone().view(M, C)  # the caller may overwrite its input (residual adds are in place)
             w_qkv, w_o = self.c_attn_w.weights, self.c_proj_w.weights
         ldx = x_op.shape[1]
         qkv = torch.empty((M, 3 * C), dtype=dt, device="cuda")
@@ -267,13 +299,11 @@ class MultiHeadAttention:
         scale = 1.0 / math.sqrt(D)
         with self._rng("attn_fwd"):
             ops.attention_forward(qv, kv, vv, ov, lse, B, NH, T, D, scale, dt)
-        out = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_out"):
             ops.gemm(ctx.data_ptr(), C, False, w_o.data_ptr(), C, False, dt, out.data_ptr(), C,
-                     torch.float32, M, C, C, bias=self.c_proj_b.weights.data_ptr())
+                     torch.float32, M, C, C, bias=self.c_proj_b.weights.data_ptr(), accumulate=accumulate)
         if getattr(self, "training", True):
             self._cache = dict(B=B, T=T, x=x_op, qkv=qkv, ctx=ctx, lse=lse, w_qkv=w_qkv, w_o=w_o)
-        return DeviceBuffer(out)
 
     # ---------------------------------------------------------------- backward
     def backward(self, gpu_dOut, B: int, T: int, accumulate=False):

@@ -175,6 +175,19 @@ def cast_rows_ones(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+              out_dtype: torch.dtype = torch.float32, ones_col: bool = False) -> torch.Tensor:
+    """Row LayerNorm of float32 x [M, C] (layernorm_kernel, core/kernels.py:75-110) -> [M, C] in
+    out_dtype, or, with ones_col (bf16), [M, L] = LN(x) | 1 | 0.. like cast_rows_ones."""
+    assert x.dtype == torch.float32 and x.is_contiguous() and x.dim() == 2
+    M, C = x.shape
+    L = (C + 1 + 7) // 8 * 8 if ones_col else C
+    out = torch.empty((M, L), dtype=out_dtype, device=x.device)
+    call("attn_layernorm", x.data_ptr(), C, gamma.data_ptr(), beta.data_ptr(), M, C, float(eps), out.data_ptr(),
+         L, dtype_code(out_dtype), int(ones_col), _stream())
+    return out
+
+
 def split_heads(qkv: int, q: int, k: int, v: int, B: int, T: int, NH: int, HD: int):
     """split_heads_kernel (core/mha_kernels.py:534-558) on float32 device buffers."""
     call("attn_split_heads", qkv, q, k, v, B, T, NH, HD, _stream())

@@ -189,6 +189,17 @@ def decode_attention(q, k_cache, v_cache, scale, dtype=np.float64):
     return out, (m + np.log(z))[..., 0]
 
 
+def layernorm(x, gamma, beta, eps=1e-5, dtype=np.float64):
+    """Row LayerNorm as layernorm_kernel (core/kernels.py:75-110): per row, mean = sum / C, then
+    the biased variance sum((x - mean)^2) / C in a second pass, rstd = 1 / sqrt(var + 1e-5) (the
+    kernel's rsqrtf), y = (x - mean) * rstd * gamma + beta.  The reference has this only as CUDA
+    source; tests/test_gpu_reference_kernels.py runs that source next to this restatement."""
+    x = np.asarray(x, dtype=dtype)
+    mean = x.mean(axis=-1, keepdims=True)
+    var = ((x - mean) ** 2).mean(axis=-1, keepdims=True)
+    return (x - mean) / np.sqrt(var + dtype(eps)) * np.asarray(gamma, dtype) + np.asarray(beta, dtype)
+
+
 def rel_err(actual, ref) -> float:
     """max|actual - ref| / max|ref|: the per-tensor relative error the tolerances are stated in."""
     a = np.asarray(actual, dtype=np.float64)

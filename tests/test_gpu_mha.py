@@ -183,3 +183,40 @@ def test_kv_cache_decode_matches_full_forward(pkg, cuda_dev, prec, tol, B, T0, s
     assert cache.length == T
     with pytest.raises(RuntimeError):
         attn.forward_decode(torch.zeros((B, C), device="cuda"), B, cache)  # cache full
+
+
+@pytest.mark.parametrize("prec,tol,B,T,C,NH", [
+    ("fp32", 1e-5, 2, 33, 64, 4),
+    ("bf16", 2e-2, 2, 200, 256, 4),
+    ("bf16", 2e-2, 1, 130, 768, 12),
+])
+def test_forward_residual_matches_block_sequence(pkg, cuda_dev, prec, tol, B, T, C, NH):
+    """forward_residual(x) == x + attn(ln_1(x)) of TransformerBlock.forward (model/gpt.py:778-783),
+    with the LayerNorm of layernorm_kernel (core/kernels.py:75-110); the backward that follows
+    sees the LayerNorm output as the attention input, exactly as after the unfused sequence."""
+    torch = _torch()
+    inp = O.make_config_inputs(5, B, T, C, NH)
+    rng = np.random.default_rng(C + T)
+    gamma = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    beta = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    inp["b_qkv"] = (rng.standard_normal(3 * C) * 0.1).astype(np.float32)
+    inp["b_o"] = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
+                                                attention_precision=prec))
+    _load_weights(attn, inp)
+    gx = torch.from_numpy(inp["x"].copy()).cuda()
+    attn.forward_residual(gx, B, T, torch.from_numpy(gamma).cuda(), torch.from_numpy(beta).cuda())
+    ln = O.layernorm(inp["x"], gamma, beta)
+    out, cache = O.mha_forward(ln, inp["w_qkv"], inp["b_qkv"], inp["w_o"], inp["b_o"], B, T, NH)
+    torch.cuda.synchronize()
+    assert O.rel_err(gx.cpu().numpy(), inp["x"] + out) < tol
+    assert O.rel_err(attn.cache_input, ln) < (tol if prec == "fp32" else 1e-2)
+    din = attn.backward(torch.from_numpy(inp["dy"]).cuda(), B, T)
+    torch.cuda.synchronize()
+    ref_din, ref_daw, ref_dab, ref_dpw, ref_dpb = O.mha_backward(cache, inp["dy"], inp["w_qkv"], inp["w_o"], B, T, NH)
+    got = dict(din=din.get(), daw=attn.c_attn_w.grads.cpu().numpy(), dab=attn.c_attn_b.grads.cpu().numpy(),
+               dpw=attn.c_proj_w.grads.cpu().numpy(), dpb=attn.c_proj_b.grads.cpu().numpy())
+    ref = dict(din=ref_din, daw=ref_daw, dab=ref_dab, dpw=ref_dpw, dpb=ref_dpb)
+    din.free()
+    for k in ref:
+        assert O.rel_err(got[k], ref[k]) < tol, (k, O.rel_err(got[k], ref[k]))

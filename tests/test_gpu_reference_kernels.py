@@ -1,0 +1,95 @@
+"""The library's kernels next to the reference's own CUDA kernels, on the same inputs.
+
+``oracle/build_ref.py`` compiles the reference's kernel sources (the strings that PyCUDA compiles at
+run time, core/kernels.py and core/mha_kernels.py) for sm_100a into oracle/_ref/libref_kernels.so
+with launchers that use the reference's launch configurations.  These tests load that library as
+the checker: ``layernorm_kernel`` (core/kernels.py:75-110) against attn_layernorm, and
+``fused_attention_forward_kernel`` (core/mha_kernels.py:404-521) against attn_fwd (float32 and the
+bf16 tensor-core path), attn_probs (its Scores output) and the LSE (its row_max + log row_sum).
+They are skipped where the reference library was not built.
+"""
+import ctypes
+import math
+import os
+
+import numpy as np
+import pytest
+
+from oracle import mha_oracle as O
+
+pytestmark = pytest.mark.gpu
+REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                   "libref_kernels.so")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.exists(REF):
+        pytest.skip("oracle/_ref/libref_kernels.so not built (python oracle/build_ref.py <reference>)")
+    lib = ctypes.CDLL(REF)
+    P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    lib.ref_layernorm.argtypes = [P, P, P, P, I, I]
+    lib.ref_layernorm.restype = I
+    lib.ref_fused_attention_forward.argtypes = [P, P, P, P, P, P, P, I, I, I, F]
+    lib.ref_fused_attention_forward.restype = I
+    return lib
+
+
+@pytest.mark.parametrize("M,C", [(1, 8), (257, 64), (1000, 768), (33, 100), (64, 2048)])
+def test_layernorm_matches_reference_kernel(pkg, cuda_dev, ref, M, C):
+    import torch
+    rng = np.random.default_rng(M + C)
+    x = (rng.standard_normal((M, C)) * 3 + 1).astype(np.float32)
+    g = rng.standard_normal(C).astype(np.float32)
+    b = rng.standard_normal(C).astype(np.float32)
+    tx, tg, tb = (torch.from_numpy(a).cuda() for a in (x, g, b))
+    y_ref = torch.empty_like(tx)
+    assert ref.ref_layernorm(tx.data_ptr(), y_ref.data_ptr(), tg.data_ptr(), tb.data_ptr(), M, C) == 0
+    y = pkg.mha_ops.layernorm(tx, tg, tb)
+    torch.cuda.synchronize()
+    yr, yo = y_ref.cpu().numpy(), y.cpu().numpy()
+    assert O.rel_err(yo, yr) < 1e-5
+    # the oracle restatement agrees with the reference kernel too
+    assert O.rel_err(O.layernorm(x, g, b), yr) < 1e-5
+    # bf16 output with the ones column: the same values rounded, then 1, then zeros
+    yb = pkg.mha_ops.layernorm(tx, tg, tb, out_dtype=torch.bfloat16, ones_col=True)
+    torch.cuda.synchronize()
+    assert yb.shape[1] % 8 == 0 and yb.shape[1] > C
+    assert O.rel_err(yb[:, :C].float().cpu().numpy(), yr) < 1e-2
+    assert torch.all(yb[:, C] == 1) and torch.all(yb[:, C + 1:] == 0)
+
+
+@pytest.mark.parametrize("H,M,D", [(3, 17, 8), (4, 128, 16), (2, 200, 64), (2, 129, 32)])
+def test_attention_forward_matches_reference_kernel(pkg, cuda_dev, ref, H, M, D):
+    import torch
+    ops = pkg.mha_ops
+    rng = np.random.default_rng(H * 1000 + M + D)
+    q, k, v = (rng.standard_normal((H, M, D)).astype(np.float32) for _ in range(3))
+    scale = 1.0 / math.sqrt(D)
+    tq, tk, tv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    scores = torch.empty((H, M, M), dtype=torch.float32, device="cuda")
+    o_ref = torch.empty((H, M, D), dtype=torch.float32, device="cuda")
+    rmax = torch.empty((H, M), dtype=torch.float32, device="cuda")
+    rsum = torch.empty((H, M), dtype=torch.float32, device="cuda")
+    assert ref.ref_fused_attention_forward(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), scores.data_ptr(),
+                                           o_ref.data_ptr(), rmax.data_ptr(), rsum.data_ptr(), H, M, D, scale) == 0
+    lse_ref = (rmax + torch.log(rsum)).cpu().numpy()
+    # float32 path of the library, on the reference's [H, M, D] head layout
+    view = lambda t: ops.HeadView.heads(t.data_ptr(), H, M, D)  # noqa: E731
+    o = torch.empty_like(tq)
+    lse = torch.empty((1, H, M), dtype=torch.float32, device="cuda")
+    ops.attention_forward(view(tq), view(tk), view(tv), view(o), lse, 1, H, M, D, scale, torch.float32)
+    p = ops.attention_probs(view(tq), view(tk), lse, 1, H, M, D, scale, torch.float32)
+    torch.cuda.synchronize()
+    assert O.rel_err(o.cpu().numpy(), o_ref.cpu().numpy()) < 1e-5
+    assert O.rel_err(lse.cpu().numpy()[0], lse_ref) < 1e-5
+    assert O.rel_err(p.cpu().numpy()[0], scores.cpu().numpy()) < 1e-5
+    # bf16 tensor-core path against the same kernel on the bf16-rounded inputs
+    bq, bk, bv = (t.to(torch.bfloat16) for t in (tq, tk, tv))
+    fq, fk, fv = (t.float().contiguous() for t in (bq, bk, bv))
+    assert ref.ref_fused_attention_forward(fq.data_ptr(), fk.data_ptr(), fv.data_ptr(), scores.data_ptr(),
+                                           o_ref.data_ptr(), rmax.data_ptr(), rsum.data_ptr(), H, M, D, scale) == 0
+    ob = torch.empty_like(bq)
+    ops.attention_forward(view(bq), view(bk), view(bv), view(ob), lse, 1, H, M, D, scale, torch.bfloat16)
+    torch.cuda.synchronize()
+    assert O.rel_err(ob.float().cpu().numpy(), o_ref.cpu().numpy()) < 2e-2
