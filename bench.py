@@ -557,6 +557,63 @@ def run_decode(args, cfg):
     return 0
 
 
+# ------------------------------------------------------------------------------ fused half-block
+def run_residual(args, cfg):
+    """x += attn(ln_1(x)), the pre-attention half of TransformerBlock.forward (model/gpt.py:778-783),
+    timed two ways on the same inputs: the reference's sequence with this library's kernels
+    (LayerNorm to float32, MultiHeadAttention.forward, residual add) and forward_residual (the
+    LayerNorm writes the QKV operand, the output projection adds into x).  Forward only."""
+    import numpy as np
+    import torch
+    import importlib
+    pkg = importlib.import_module("llm-gpu-5_b200")
+    w = WORKLOADS[cfg]
+    B = args.batch or w["global_batch"]
+    T, C, NH = w["T"], w["C"], w["NH"]
+    M = B * T
+    np.random.seed(1000 + cfg)
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
+                                                attention_precision=w["prec"]))
+    attn.training = False
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1000 + cfg)
+    x0 = torch.randn((M, C), generator=gen, device="cuda")
+    gamma = 1 + 0.1 * torch.randn(C, generator=gen, device="cuda")
+    beta = 0.1 * torch.randn(C, generator=gen, device="cuda")
+    x = x0.clone()
+
+    def unfused():
+        ln = pkg.mha_ops.layernorm(x, gamma, beta)
+        out = attn.forward(ln, B, T)
+        x.add_(out.tensor)
+        out.free()
+
+    def fused():
+        attn.forward_residual(x, B, T, gamma, beta)
+
+    res = {}
+    for name, fn in (("unfused", unfused), ("fused", fused)):
+        for _ in range(max(args.warmup, 3)):
+            x.copy_(x0)
+            fn()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        total = 0.0
+        for _ in range(args.steps):  # x is reset outside the timed spans
+            x.copy_(x0)
+            t0.record()
+            fn()
+            t1.record()
+            torch.cuda.synchronize()
+            total += t0.elapsed_time(t1)
+        res[name] = total / args.steps
+    print(json.dumps(dict(metric="pre-attention half-block forward tokens/sec", value=M / (res["fused"] * 1e-3),
+                          unit="tokens/s", fused_ms=res["fused"], unfused_ms=res["unfused"],
+                          speedup=res["unfused"] / res["fused"], dtype="bf16" if w["prec"] == "bf16" else "f32",
+                          data="synthetic", config=dict(workload=w["name"], tokens=M))), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------------------------ vendor libraries
 def run_vendor(args, cfg):
     """Time NVIDIA's own B200 kernels on the same workload, for context: cuDNN attention through
@@ -618,6 +675,8 @@ def main():
                     help="vendor: time cuDNN attention and cuBLAS GEMMs on the same workload (context only)")
     ap.add_argument("--config", type=int, default=5, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--residual", action="store_true",
+                    help="time x += attn(ln_1(x)) fused (forward_residual) against the unfused block sequence")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the global batch (small cases for profiler captures only)")
     args = ap.parse_args()
@@ -627,6 +686,8 @@ def main():
         return run_vendor(args, args.config)
     if WORKLOADS[args.config].get("decode"):
         return run_decode(args, args.config)
+    if args.residual:
+        return run_residual(args, args.config)
     return run_ours(args, args.config)
 
 
