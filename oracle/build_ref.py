@@ -9,7 +9,10 @@ executed), takes
 
 * ``LAYERNORM_KERNEL`` (core/kernels.py:73-110): ``layernorm_kernel``, one thread per row;
 * ``MHA_KERNELS_STRING`` (core/mha_kernels.py:53-...): among others
-  ``fused_attention_forward_kernel`` (core/mha_kernels.py:404-521),
+  ``fused_attention_forward_kernel`` (core/mha_kernels.py:404-521), the gradient kernels the
+  reference's GPU golden test chains (``matmul_score_kernel``, ``softmax_fused_backward``,
+  ``matmul_grad_q_kernel``, ``matmul_grad_k_kernel``, ``matmul_grad_v``) and the layout adapters
+  ``split_heads_kernel`` / ``merge_heads_kernel`` (core/mha_kernels.py:534-584),
 
 wraps the MHA string in ``extern "C"`` as SourceModule does, appends host launchers of our own that
 use the reference's launch configurations (256 threads per block and ceil(rows / 256) blocks for the
@@ -50,6 +53,44 @@ extern "C" int ref_fused_attention_forward(const float* q, const float* k, const
   const size_t smem = (size_t)(D + M + threads) * 4;  // model/gpt.py:587
   fused_attention_forward_kernel<<<dim3(H, M), threads, smem>>>(q, k, v, scores, out, row_max, row_sum, H, M,
                                                                 D, scale);
+  return (int)cudaDeviceSynchronize();
+}
+
+// The kernel-level backward chain of the reference's GPU golden test (test_mha_golden_model.py:136-156):
+// dP = dOut V^T with matmul_score_kernel (scale 1), the softmax VJP softmax_fused_backward (no softmax
+// scale, as that test), then matmul_grad_q_kernel / matmul_grad_k_kernel / matmul_grad_v.  probs is
+// the Scores output of the fused forward.  Scratch is allocated here (checker code only).
+extern "C" int ref_attention_backward(const float* q, const float* k, const float* v, const float* dout,
+                                      const float* probs, float* dq, float* dk, float* dv, int H, int M, int D) {
+  float *dprobs = 0, *dscores = 0, *rsum = 0;
+  const size_t mm = (size_t)H * M * M * sizeof(float);
+  if (cudaMalloc(&dprobs, mm) != cudaSuccess || cudaMalloc(&dscores, mm) != cudaSuccess ||
+      cudaMalloc(&rsum, (size_t)H * M * sizeof(float)) != cudaSuccess)
+    return -1;
+  const int threads = 256, softmax_threads = 64;  // test_mha_golden_model.py:118-122
+  const int score_blocks = (H * M * M + threads - 1) / threads, proj_blocks = (H * M * D + threads - 1) / threads;
+  matmul_score_kernel<<<score_blocks, threads>>>(dout, v, dprobs, H, M, D, 1.0f);
+  softmax_fused_backward<<<dim3(H, M), softmax_threads, softmax_threads * 4>>>(dprobs, probs, rsum, dscores, H, M);
+  matmul_grad_q_kernel<<<proj_blocks, threads>>>(dscores, k, dq, H, M, D);
+  matmul_grad_k_kernel<<<proj_blocks, threads>>>(dscores, q, dk, H, M, D);
+  matmul_grad_v<<<proj_blocks, threads>>>(probs, dout, dv, H, M, D);
+  const int rc = (int)cudaDeviceSynchronize();
+  cudaFree(dprobs);
+  cudaFree(dscores);
+  cudaFree(rsum);
+  return rc;
+}
+
+// The layout adapters, 256 threads per block over B*T*NH*HD elements (model/gpt.py:569-598).
+extern "C" int ref_split_heads(const float* qkv, float* q, float* k, float* v, int B, int T, int NH, int HD) {
+  const int total = B * T * NH * HD, threads = 256;
+  split_heads_kernel<<<(total + threads - 1) / threads, threads>>>(qkv, q, k, v, B, T, NH, HD);
+  return (int)cudaDeviceSynchronize();
+}
+
+extern "C" int ref_merge_heads(const float* heads, float* ctx, int B, int T, int NH, int HD) {
+  const int total = B * T * NH * HD, threads = 256;
+  merge_heads_kernel<<<(total + threads - 1) / threads, threads>>>(heads, ctx, B, T, NH, HD);
   return (int)cudaDeviceSynchronize();
 }
 '''

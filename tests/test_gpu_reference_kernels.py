@@ -6,7 +6,11 @@ with launchers that use the reference's launch configurations.  These tests load
 the checker: ``layernorm_kernel`` (core/kernels.py:75-110) against attn_layernorm, and
 ``fused_attention_forward_kernel`` (core/mha_kernels.py:404-521) against attn_fwd (float32 and the
 bf16 tensor-core path), attn_probs (its Scores output) and the LSE (its row_max + log row_sum).
-They are skipped where the reference library was not built.
+The kernel-level backward chain of the reference's GPU golden test (matmul_score_kernel,
+softmax_fused_backward, matmul_grad_q/k/v; core/mha_kernels.py:62-87, 195-236, 592-680) is run
+against attn_bwd, and split_heads_kernel / merge_heads_kernel (core/mha_kernels.py:534-584)
+against attn_split_heads / attn_merge_heads.  They are skipped where the reference library was
+not built.
 """
 import ctypes
 import math
@@ -32,6 +36,12 @@ def ref():
     lib.ref_layernorm.restype = I
     lib.ref_fused_attention_forward.argtypes = [P, P, P, P, P, P, P, I, I, I, F]
     lib.ref_fused_attention_forward.restype = I
+    lib.ref_attention_backward.argtypes = [P, P, P, P, P, P, P, P, I, I, I]
+    lib.ref_attention_backward.restype = I
+    lib.ref_split_heads.argtypes = [P, P, P, P, I, I, I, I]
+    lib.ref_split_heads.restype = I
+    lib.ref_merge_heads.argtypes = [P, P, I, I, I, I]
+    lib.ref_merge_heads.restype = I
     return lib
 
 
@@ -93,3 +103,55 @@ def test_attention_forward_matches_reference_kernel(pkg, cuda_dev, ref, H, M, D)
     ops.attention_forward(view(bq), view(bk), view(bv), view(ob), lse, 1, H, M, D, scale, torch.bfloat16)
     torch.cuda.synchronize()
     assert O.rel_err(ob.float().cpu().numpy(), o_ref.cpu().numpy()) < 2e-2
+
+
+@pytest.mark.parametrize("H,M,D", [(3, 17, 8), (4, 128, 16), (2, 130, 64)])
+def test_attention_backward_matches_reference_kernels(pkg, cuda_dev, ref, H, M, D):
+    """dQ, dK, dV of attn_bwd against the reference's own gradient kernels.  Those follow the
+    golden test and leave the softmax scale out of dS, which production applies
+    (model/gpt.py:677); dQ and dK are linear in dS, so the library's equal the reference's times
+    the scale."""
+    import torch
+    ops = pkg.mha_ops
+    rng = np.random.default_rng(H * 7 + M + D)
+    q, k, v, do = (rng.standard_normal((H, M, D)).astype(np.float32) for _ in range(4))
+    scale = 1.0 / math.sqrt(D)
+    tq, tk, tv, tdo = (torch.from_numpy(a).cuda() for a in (q, k, v, do))
+    probs = torch.empty((H, M, M), dtype=torch.float32, device="cuda")
+    o_ref = torch.empty_like(tq)
+    rmax = torch.empty((H, M), dtype=torch.float32, device="cuda")
+    rsum = torch.empty((H, M), dtype=torch.float32, device="cuda")
+    assert ref.ref_fused_attention_forward(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), probs.data_ptr(),
+                                           o_ref.data_ptr(), rmax.data_ptr(), rsum.data_ptr(), H, M, D, scale) == 0
+    rdq, rdk, rdv = (torch.empty_like(tq) for _ in range(3))
+    assert ref.ref_attention_backward(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), tdo.data_ptr(), probs.data_ptr(),
+                                      rdq.data_ptr(), rdk.data_ptr(), rdv.data_ptr(), H, M, D) == 0
+    view = lambda t: ops.HeadView.heads(t.data_ptr(), H, M, D)  # noqa: E731
+    o = torch.empty_like(tq)
+    lse = torch.empty((1, H, M), dtype=torch.float32, device="cuda")
+    ops.attention_forward(view(tq), view(tk), view(tv), view(o), lse, 1, H, M, D, scale, torch.float32)
+    dq, dk, dv = (torch.empty_like(tq) for _ in range(3))
+    ops.attention_backward(view(tq), view(tk), view(tv), view(o), view(tdo), lse, view(dq), view(dk), view(dv),
+                           1, H, M, D, scale, torch.float32)
+    torch.cuda.synchronize()
+    assert O.rel_err(dv.cpu().numpy(), rdv.cpu().numpy()) < 1e-5
+    assert O.rel_err(dq.cpu().numpy(), scale * rdq.cpu().numpy()) < 1e-5
+    assert O.rel_err(dk.cpu().numpy(), scale * rdk.cpu().numpy()) < 1e-5
+
+
+def test_split_merge_heads_match_reference_kernels(pkg, cuda_dev, ref):
+    import torch
+    B, T, NH, HD = 2, 37, 3, 16
+    C = NH * HD
+    qkv = torch.from_numpy(np.random.default_rng(5).standard_normal((B * T, 3 * C)).astype(np.float32)).cuda()
+    outs = [torch.empty((B * NH, T, HD), dtype=torch.float32, device="cuda") for _ in range(6)]
+    assert ref.ref_split_heads(qkv.data_ptr(), *(t.data_ptr() for t in outs[:3]), B, T, NH, HD) == 0
+    pkg.mha_ops.split_heads(qkv.data_ptr(), *(t.data_ptr() for t in outs[3:]), B, T, NH, HD)
+    ctx_ref = torch.empty((B * T, C), dtype=torch.float32, device="cuda")
+    ctx = torch.empty_like(ctx_ref)
+    assert ref.ref_merge_heads(outs[0].data_ptr(), ctx_ref.data_ptr(), B, T, NH, HD) == 0
+    pkg.mha_ops.merge_heads(outs[0].data_ptr(), ctx.data_ptr(), B, T, NH, HD)
+    torch.cuda.synchronize()
+    for a, b in zip(outs[:3], outs[3:]):
+        assert torch.equal(a, b)
+    assert torch.equal(ctx, ctx_ref)
