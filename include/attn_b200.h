@@ -194,6 +194,17 @@ int attn_cast_rows_ones_bf16(const float* x, int64_t ldx, int M, int N, void* y,
 int attn_layernorm(const float* x, int64_t ldx, const float* gamma, const float* beta, int M, int C,
                    float eps, void* y, int64_t ldy, int y_dtype, int ones_col, void* stream);
 
+/*
+ * LayerNorm backward (layernorm_backward_kernel, core/kernels.py:361-416): for rows of dy and the
+ * forward input x (float32 [M][C], contiguous), dx = rstd/C * (C*g - sum(g) - x_hat*sum(g*x_hat))
+ * with g = dy*gamma, written or, with accumulate_dx, added to dx (the residual branch of
+ * TransformerBlock.backward, model/gpt.py:826-838, in place); dgamma = sum over rows of dy*x_hat
+ * and dbeta = sum of dy, set or (accumulate_params) added.  dx must not alias x or dy.
+ */
+int attn_layernorm_bwd(const float* dy, const float* x, const float* gamma, int M, int C, float eps,
+                       float* dx, int accumulate_dx, float* dgamma, float* dbeta,
+                       int accumulate_params, void* stream);
+
 /* y[i] = bf16(x[i]) (round to nearest even), n elements. */
 int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream);
 

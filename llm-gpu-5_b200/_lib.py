@@ -48,6 +48,7 @@ SIGNATURES = {
     "attn_cast_f32_to_bf16": (_i, [_p, _p, _i64, _p]),
     "attn_cast_rows_ones_bf16": (_i, [_p, _i64, _i, _i, _p, _i64, _p]),
     "attn_layernorm": (_i, [_p, _i64, _p, _p, _i, _i, _f, _p, _i64, _i, _i, _p]),
+    "attn_layernorm_bwd": (_i, [_p, _p, _p, _i, _i, _f, _p, _i, _p, _p, _i, _p]),
     "attn_cast_colsum_f32": (_i, [_p, _i64, _i, _i, _p, _i64, _p, _i, _p, _sz, _p]),
     "attn_split_heads": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p]),
     "attn_merge_heads": (_i, [_p, _p, _i, _i, _i, _i, _p]),

@@ -133,6 +133,8 @@ int cast_f32_bf16(const float*, void*, int64_t, cudaStream_t, int);
 int cast_rows_ones(const float*, int64_t, int, int, void*, int64_t, cudaStream_t, int);
 int layernorm_rows(const float*, int64_t, const float*, const float*, int, int, float, void*, int64_t, int, int,
                    cudaStream_t);
+int layernorm_bwd_rows(const float*, const float*, const float*, int, int, float, float*, int, float*, float*, int,
+                       cudaStream_t, int);
 size_t colsum_ws(int, int);
 int colsum(const void*, int, int64_t, int, int, float*, int, void*, cudaStream_t);
 int cast_colsum(const float*, int64_t, int, int, void*, int64_t, float*, int, void*, cudaStream_t);
@@ -357,6 +359,18 @@ int attn_layernorm(const float* x, int64_t ldx, const float* gamma, const float*
   ATTN_REQUIRE(eps > 0.f, "attn_layernorm: eps must be positive");
   ATTN_REQUIRE((const void*)x != (const void*)y, "attn_layernorm: x and y must not alias");
   return layernorm_rows(x, ldx, gamma, beta, M, C, eps, y, ldy, y_dtype, ones_col, as_stream(stream));
+}
+
+int attn_layernorm_bwd(const float* dy, const float* x, const float* gamma, int M, int C, float eps, float* dx,
+                       int accumulate_dx, float* dgamma, float* dbeta, int accumulate_params, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(dy && x && gamma && dx && dgamma && dbeta, "attn_layernorm_bwd: null pointer argument");
+  ATTN_REQUIRE(M > 0 && C > 0, "attn_layernorm_bwd: bad shape");
+  ATTN_REQUIRE(eps > 0.f, "attn_layernorm_bwd: eps must be positive");
+  ATTN_REQUIRE((const void*)dx != (const void*)x && (const void*)dx != (const void*)dy,
+               "attn_layernorm_bwd: dx must not alias x or dy");
+  return layernorm_bwd_rows(dy, x, gamma, M, C, eps, dx, accumulate_dx, dgamma, dbeta, accumulate_params,
+                            as_stream(stream), sm_count());
 }
 
 int attn_cast_f32_to_bf16(const float* x, void* y, int64_t n, void* stream) {

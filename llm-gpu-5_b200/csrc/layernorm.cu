@@ -124,4 +124,149 @@ int layernorm_rows(const float* x, int64_t ldx, const float* gamma, const float*
   return check_launch("layernorm_rows_kernel");
 }
 
+// ---------------------------------------------------------------------------------------------
+// LayerNorm backward (layernorm_backward_kernel, core/kernels.py:361-416): per row, with
+// x_hat = (x - mean) * rstd and g = dy * gamma,
+//   dx = rstd / C * (C * g - sum(g) - x_hat * sum(g * x_hat)),
+//   dgamma += sum over rows of dy * x_hat,   dbeta += sum over rows of dy.
+// dx is written, or added to dx's current contents (accumulate_dx: the residual branch of
+// TransformerBlock.backward, dX0 = dX1 + dLN, model/gpt.py:826-838, done in place).  A persistent
+// grid walks the rows one warp per row; every lane keeps the dgamma/dbeta partials of its own
+// columns in registers across rows and adds them to the outputs once at the end.
+template <int KMAX>
+__global__ void layernorm_bwd_rows_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                          const float* __restrict__ gamma, int M, int C, float eps,
+                                          float* __restrict__ dx, int accumulate_dx, float* __restrict__ dgamma,
+                                          float* __restrict__ dbeta) {
+  const int lane = threadIdx.x % 32;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
+  const int nch = C / 4;
+  float4 pg[KMAX], pb[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) pg[k] = pb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t row = wid; row < M; row += nw) {
+    const float* xr = x + row * C;
+    const float* dyr = dy + row * C;
+    float4 xv[KMAX], gv[KMAX];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      const int c = lane + 32 * k;
+      xv[k] = c < nch ? *reinterpret_cast<const float4*>(xr + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      s += (xv[k].x + xv[k].y) + (xv[k].z + xv[k].w);
+    }
+    const float mean = warp_sum(s) / C;
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      if (lane + 32 * k < nch) {
+        xv[k].x -= mean; xv[k].y -= mean; xv[k].z -= mean; xv[k].w -= mean;
+        ss += (xv[k].x * xv[k].x + xv[k].y * xv[k].y) + (xv[k].z * xv[k].z + xv[k].w * xv[k].w);
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(ss) / C + eps);
+    float sg = 0.f, sgx = 0.f;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      const int c = lane + 32 * k;
+      if (c < nch) {
+        const float4 d = *reinterpret_cast<const float4*>(dyr + 4 * c);
+        const float4 g = *reinterpret_cast<const float4*>(gamma + 4 * c);
+        xv[k].x *= rstd; xv[k].y *= rstd; xv[k].z *= rstd; xv[k].w *= rstd;  // x_hat
+        pg[k].x += d.x * xv[k].x; pg[k].y += d.y * xv[k].y; pg[k].z += d.z * xv[k].z; pg[k].w += d.w * xv[k].w;
+        pb[k].x += d.x; pb[k].y += d.y; pb[k].z += d.z; pb[k].w += d.w;
+        gv[k] = make_float4(d.x * g.x, d.y * g.y, d.z * g.z, d.w * g.w);
+        sg += (gv[k].x + gv[k].y) + (gv[k].z + gv[k].w);
+        sgx += (gv[k].x * xv[k].x + gv[k].y * xv[k].y) + (gv[k].z * xv[k].z + gv[k].w * xv[k].w);
+      }
+    }
+    sg = warp_sum(sg);
+    sgx = warp_sum(sgx);
+    const float f = rstd / C;
+    float* dxr = dx + row * C;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      const int c = lane + 32 * k;
+      if (c < nch) {
+        float4 o;
+        o.x = f * (C * gv[k].x - sg - xv[k].x * sgx);
+        o.y = f * (C * gv[k].y - sg - xv[k].y * sgx);
+        o.z = f * (C * gv[k].z - sg - xv[k].z * sgx);
+        o.w = f * (C * gv[k].w - sg - xv[k].w * sgx);
+        if (accumulate_dx) {
+          const float4 a = *reinterpret_cast<const float4*>(dxr + 4 * c);
+          o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
+        }
+        *reinterpret_cast<float4*>(dxr + 4 * c) = o;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    const int c = lane + 32 * k;
+    if (c < nch) {
+      atomicAdd(dgamma + 4 * c, pg[k].x); atomicAdd(dgamma + 4 * c + 1, pg[k].y);
+      atomicAdd(dgamma + 4 * c + 2, pg[k].z); atomicAdd(dgamma + 4 * c + 3, pg[k].w);
+      atomicAdd(dbeta + 4 * c, pb[k].x); atomicAdd(dbeta + 4 * c + 1, pb[k].y);
+      atomicAdd(dbeta + 4 * c + 2, pb[k].z); atomicAdd(dbeta + 4 * c + 3, pb[k].w);
+    }
+  }
+}
+
+// Any C: one warp per row, scalar, parameter gradients by per-element atomics.
+__global__ void layernorm_bwd_rows_generic_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                                  const float* __restrict__ gamma, int M, int C, float eps,
+                                                  float* __restrict__ dx, int accumulate_dx,
+                                                  float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  const int lane = threadIdx.x % 32;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= M) return;
+  const float* xr = x + row * C;
+  const float* dyr = dy + row * C;
+  float s = 0.f;
+  for (int c = lane; c < C; c += 32) s += xr[c];
+  const float mean = warp_sum(s) / C;
+  float ss = 0.f;
+  for (int c = lane; c < C; c += 32) ss += (xr[c] - mean) * (xr[c] - mean);
+  const float rstd = rsqrtf(warp_sum(ss) / C + eps);
+  float sg = 0.f, sgx = 0.f;
+  for (int c = lane; c < C; c += 32) {
+    const float xh = (xr[c] - mean) * rstd, g = dyr[c] * gamma[c];
+    atomicAdd(dgamma + c, dyr[c] * xh);
+    atomicAdd(dbeta + c, dyr[c]);
+    sg += g;
+    sgx += g * xh;
+  }
+  sg = warp_sum(sg);
+  sgx = warp_sum(sgx);
+  for (int c = lane; c < C; c += 32) {
+    const float xh = (xr[c] - mean) * rstd;
+    const float o = rstd / C * (C * dyr[c] * gamma[c] - sg - xh * sgx);
+    dx[row * C + c] = accumulate_dx ? dx[row * C + c] + o : o;
+  }
+}
+
+int layernorm_bwd_rows(const float* dy, const float* x, const float* gamma, int M, int C, float eps, float* dx,
+                       int accumulate_dx, float* dgamma, float* dbeta, int accumulate_params, cudaStream_t s,
+                       int sms) {
+  if (!accumulate_params) {
+    ATTN_CUDA_TRY(cudaMemsetAsync(dgamma, 0, (size_t)C * sizeof(float), s));
+    ATTN_CUDA_TRY(cudaMemsetAsync(dbeta, 0, (size_t)C * sizeof(float), s));
+  }
+  const int warps = 8;
+  const bool vec = C % 4 == 0 && aligned(dy, 16) && aligned(x, 16) && aligned(gamma, 16) && aligned(dx, 16);
+  const int64_t row_blocks = ((int64_t)M + warps - 1) / warps;
+  if (vec && C <= 4 * 32 * 8) {
+    const int64_t cap = (int64_t)sms * 4;  // persistent: the lanes' parameter partials live across rows
+    layernorm_bwd_rows_kernel<8><<<(unsigned)(row_blocks < cap ? row_blocks : cap), 32 * warps, 0, s>>>(
+        dy, x, gamma, M, C, eps, dx, accumulate_dx, dgamma, dbeta);
+  } else {
+    layernorm_bwd_rows_generic_kernel<<<(unsigned)row_blocks, 32 * warps, 0, s>>>(dy, x, gamma, M, C, eps, dx,
+                                                                                  accumulate_dx, dgamma, dbeta);
+  }
+  count_launch();
+  return check_launch("layernorm_bwd_rows_kernel");
+}
+
 }  // namespace attn

@@ -267,7 +267,31 @@ class MultiHeadAttention:
         g, b = _as_tensor(ln_gamma, C), _as_tensor(ln_beta, C)
         with self._rng("layernorm"):
             x_op = ops.layernorm(x, g, b, eps, out_dtype=dt, ones_col=dt == torch.bfloat16)
+        # the LayerNorm input, for backward_residual (TransformerBlock keeps the same copy,
+        # cache_input_ln1, model/gpt.py:773-775)
+        ln_input = x.clone() if getattr(self, "training", True) else None
         self._forward_core(x_op, B, T, x, accumulate=True)
+        if self._cache is not None:
+            self._cache.update(ln_input=ln_input, ln_eps=eps)
+
+    def backward_residual(self, gpu_dx, B: int, T: int, ln_gamma, ln_dgamma, ln_dbeta, accumulate=False):
+        """Backward of forward_residual, in place: dx (dL/dx after the residual add) becomes
+        dL/dx before it, dx + LN_bwd(attn.backward(dx)), and the four attention gradients and the
+        LayerNorm's dgamma/dbeta are set (or accumulated).  Replaces the attention half of
+        TransformerBlock.backward (model/gpt.py:825-838): attn.backward, ln_bwd_op, a copy of dX1 and
+        the residual add, with the LayerNorm backward adding into dx directly."""
+        c = self._cache
+        if c is None or c.get("ln_input") is None:
+            raise RuntimeError("MultiHeadAttention.backward_residual() called without forward_residual caches")
+        C, NH, D = self._shape()
+        M = B * T
+        dx = _as_tensor(gpu_dx, M * C).view(M, C)
+        dln = self.backward(dx, B, T, accumulate=accumulate)
+        with self._rng("layernorm_bwd"):
+            ops.layernorm_backward(dln.tensor.view(M, C), c["ln_input"], _as_tensor(ln_gamma, C), dx,
+                                   _as_tensor(ln_dgamma, C), _as_tensor(ln_dbeta, C), c["ln_eps"],
+                                   accumulate_dx=True, accumulate_params=accumulate)
+        dln.free()
 
     def _forward_core(self, x_op, B, T, out, accumulate, kv_cache=None):
         """QKV projection of the prepared operand x_op [M, >= C], attention, output projection

@@ -188,6 +188,17 @@ def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: flo
     return out
 
 
+def layernorm_backward(dy: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor, dx: torch.Tensor,
+                       dgamma: torch.Tensor, dbeta: torch.Tensor, eps: float = 1e-5, accumulate_dx: bool = False,
+                       accumulate_params: bool = False):
+    """LayerNorm backward of layernorm_backward_kernel (core/kernels.py:361-416) on float32 [M, C]
+    rows: dx (=|+=) dLN/dx, dgamma/dbeta (=|+=) the parameter gradients."""
+    assert dy.dtype == x.dtype == dx.dtype == torch.float32 and dy.shape == x.shape == dx.shape
+    M, C = x.shape
+    call("attn_layernorm_bwd", dy.data_ptr(), x.data_ptr(), gamma.data_ptr(), M, C, float(eps), dx.data_ptr(),
+         int(accumulate_dx), dgamma.data_ptr(), dbeta.data_ptr(), int(accumulate_params), _stream())
+
+
 def split_heads(qkv: int, q: int, k: int, v: int, B: int, T: int, NH: int, HD: int):
     """split_heads_kernel (core/mha_kernels.py:534-558) on float32 device buffers."""
     call("attn_split_heads", qkv, q, k, v, B, T, NH, HD, _stream())

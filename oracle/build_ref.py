@@ -8,6 +8,7 @@ This script reads two of those files as text (``ast``, nothing of the reference 
 executed), takes
 
 * ``LAYERNORM_KERNEL`` (core/kernels.py:73-110): ``layernorm_kernel``, one thread per row;
+* ``LAYERNORM_BACKWARD_KERNEL`` (core/kernels.py:359-420): ``layernorm_backward_kernel``;
 * ``MHA_KERNELS_STRING`` (core/mha_kernels.py:53-...): among others
   ``fused_attention_forward_kernel`` (core/mha_kernels.py:404-521), the gradient kernels the
   reference's GPU golden test chains (``matmul_score_kernel``, ``softmax_fused_backward``,
@@ -53,6 +54,18 @@ extern "C" int ref_fused_attention_forward(const float* q, const float* k, const
   const size_t smem = (size_t)(D + M + threads) * 4;  // model/gpt.py:587
   fused_attention_forward_kernel<<<dim3(H, M), threads, smem>>>(q, k, v, scores, out, row_max, row_sum, H, M,
                                                                 D, scale);
+  return (int)cudaDeviceSynchronize();
+}
+
+// LayerNormBackward.__call__ (core/ops.py:410-437): zeroed dGamma/dBeta, 256 threads per block.
+extern "C" int ref_layernorm_backward(const float* dy, const float* x, const float* gamma, float* dx, float* dgamma,
+                                      float* dbeta, int rows, int channels) {
+  if (cudaMemset(dgamma, 0, (size_t)channels * 4) != cudaSuccess ||
+      cudaMemset(dbeta, 0, (size_t)channels * 4) != cudaSuccess)
+    return -1;
+  const int threads = 256;
+  layernorm_backward_kernel<<<(rows + threads - 1) / threads, threads>>>(dy, x, gamma, dx, dgamma, dbeta, rows,
+                                                                        channels);
   return (int)cudaDeviceSynchronize();
 }
 
@@ -116,12 +129,14 @@ def _nvcc() -> str:
 
 def build(reference_root: str) -> str:
     ln = _string_constant(os.path.join(reference_root, "core", "kernels.py"), "LAYERNORM_KERNEL")
+    ln_bwd = _string_constant(os.path.join(reference_root, "core", "kernels.py"), "LAYERNORM_BACKWARD_KERNEL")
     mha = _string_constant(os.path.join(reference_root, "core", "mha_kernels.py"), "MHA_KERNELS_STRING")
     os.makedirs(OUT, exist_ok=True)
     src = os.path.join(OUT, "ref_kernels.cu")
     with open(src, "w") as f:
         f.write("// Generated by oracle/build_ref.py from the reference's kernel strings; not part of the repo.\n")
         f.write(ln)
+        f.write(ln_bwd)
         f.write('\nextern "C" {\n')
         f.write(mha)
         f.write("\n}\n")

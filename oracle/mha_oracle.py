@@ -200,6 +200,21 @@ def layernorm(x, gamma, beta, eps=1e-5, dtype=np.float64):
     return (x - mean) / np.sqrt(var + dtype(eps)) * np.asarray(gamma, dtype) + np.asarray(beta, dtype)
 
 
+def layernorm_backward(dy, x, gamma, eps=1e-5, dtype=np.float64):
+    """layernorm_backward_kernel (core/kernels.py:361-416): mean and variance recomputed per row,
+    x_hat = (x - mean) * rstd, g = dy * gamma, dx = rstd / C * (C * g - sum(g) - x_hat * sum(g * x_hat)),
+    dgamma = sum over rows of dy * x_hat, dbeta = sum over rows of dy.  Returns (dx, dgamma, dbeta)."""
+    x = np.asarray(x, dtype=dtype)
+    dy = np.asarray(dy, dtype=dtype)
+    C = x.shape[-1]
+    mean = x.mean(axis=-1, keepdims=True)
+    rstd = 1.0 / np.sqrt(((x - mean) ** 2).mean(axis=-1, keepdims=True) + dtype(eps))
+    xh = (x - mean) * rstd
+    g = dy * np.asarray(gamma, dtype)
+    dx = rstd / C * (C * g - g.sum(-1, keepdims=True) - xh * (g * xh).sum(-1, keepdims=True))
+    return dx, (dy * xh).sum(0), dy.sum(0)
+
+
 def rel_err(actual, ref) -> float:
     """max|actual - ref| / max|ref|: the per-tensor relative error the tolerances are stated in."""
     a = np.asarray(actual, dtype=np.float64)

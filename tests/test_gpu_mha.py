@@ -220,3 +220,34 @@ def test_forward_residual_matches_block_sequence(pkg, cuda_dev, prec, tol, B, T,
     din.free()
     for k in ref:
         assert O.rel_err(got[k], ref[k]) < tol, (k, O.rel_err(got[k], ref[k]))
+
+
+
+@pytest.mark.parametrize("prec,tol,B,T,C,NH", [("fp32", 1e-5, 2, 33, 64, 4), ("bf16", 2e-2, 2, 130, 256, 4)])
+def test_backward_residual_matches_block_sequence(pkg, cuda_dev, prec, tol, B, T, C, NH):
+    """forward_residual + backward_residual against the attention half of TransformerBlock:
+    x1 = x + attn(ln_1(x)); dX0 = dX1 + ln_1 backward of attn.backward(dX1) (model/gpt.py:825-838)."""
+    torch = _torch()
+    inp = O.make_config_inputs(5, B, T, C, NH)
+    rng = np.random.default_rng(C * 3 + T)
+    gamma = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    beta = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
+                                                attention_precision=prec))
+    _load_weights(attn, inp)
+    gx = torch.from_numpy(inp["x"].copy()).cuda()
+    tg = torch.from_numpy(gamma).cuda()
+    attn.forward_residual(gx, B, T, tg, torch.from_numpy(beta).cuda())
+    gd = torch.from_numpy(inp["dy"].copy()).cuda()
+    dgamma = torch.full((C,), 5.0, device="cuda")
+    dbeta = torch.full((C,), 5.0, device="cuda")
+    attn.backward_residual(gd, B, T, tg, dgamma, dbeta)
+    torch.cuda.synchronize()
+    ln = O.layernorm(inp["x"], gamma, beta)
+    _, cache = O.mha_forward(ln, inp["w_qkv"], inp["b_qkv"], inp["w_o"], inp["b_o"], B, T, NH)
+    dln, daw, dab, dpw, dpb = O.mha_backward(cache, inp["dy"], inp["w_qkv"], inp["w_o"], B, T, NH)
+    dx_ln, dg_ref, db_ref = O.layernorm_backward(dln, inp["x"], gamma)
+    checks = dict(dx=(gd, inp["dy"] + dx_ln), dgamma=(dgamma, dg_ref), dbeta=(dbeta, db_ref),
+                  d_attn_w=(attn.c_attn_w.grads, daw), d_proj_b=(attn.c_proj_b.grads, dpb))
+    for k, (got, want) in checks.items():
+        assert O.rel_err(got.cpu().numpy(), want) < tol, (k, O.rel_err(got.cpu().numpy(), want))
