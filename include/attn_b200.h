@@ -40,6 +40,11 @@ extern "C" {
 #define ATTN_F32 0  /* float32                       */
 #define ATTN_BF16 1 /* bfloat16 (stored as uint16_t) */
 
+/* Epilogue activations of attn_gemm_act (the feed-forward block, model/gpt.py:327-456). */
+#define ATTN_ACT_NONE 0
+#define ATTN_ACT_GELU 1     /* C = gelu(acc + bias); aux (optional) = acc + bias          */
+#define ATTN_ACT_GELU_BWD 2 /* C = acc * gelu'(aux)                                       */
+
 /* Library version (major*10000 + minor*100 + patch). */
 int attn_version(void);
 
@@ -154,6 +159,25 @@ int attn_gemm(const void* A, int64_t lda, int a_trans,
               const void* B, int64_t ldb, int b_trans, int ab_dtype,
               void* C, int64_t ldc, int c_dtype, const float* bias,
               int M, int N, int K, int accumulate, void* stream);
+
+/*
+ * attn_gemm with the feed-forward activation in the epilogue (no accumulate), replacing the FFN's
+ * kernel sequences (model/gpt.py:345-365 and :428-449):
+ *   ATTN_ACT_GELU:     C = gelu(op(A) op(B) + bias), gelu the tanh form of activation_kernel
+ *                      (core/kernels.py:237-250); if aux is non-NULL it receives the pre-activation
+ *                      op(A) op(B) + bias (FeedForward's cache_pre_act), in C's dtype on the
+ *                      tensor cores.  Replaces matmul_2d_kernel + the cache copy + activation_kernel.
+ *   ATTN_ACT_GELU_BWD: C = (op(A) op(B)) * gelu'(aux), aux the cached pre-activation [M][ldaux]
+ *                      (gelu_backward_kernel, core/kernels.py:424-447).  With A = dOut and
+ *                      B = W_proj^T this is dHidden followed by the GELU backward.
+ * aux_dtype is ATTN_F32 or ATTN_BF16.  ATTN_BF16 operands run on tcgen05 (tanh.approx in the
+ * epilogue); ATTN_F32 operands on CUDA cores with tanhf.  ATTN_ACT_NONE behaves as attn_gemm.
+ */
+int attn_gemm_act(const void* A, int64_t lda, int a_trans,
+                  const void* B, int64_t ldb, int b_trans, int ab_dtype,
+                  void* C, int64_t ldc, int c_dtype, const float* bias,
+                  int M, int N, int K, int act, void* aux, int64_t ldaux, int aux_dtype,
+                  void* stream);
 
 /* Bytes of workspace attn_colsum needs. */
 size_t attn_colsum_workspace_size(int M, int N);

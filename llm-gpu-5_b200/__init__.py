@@ -12,7 +12,8 @@ library has not been built.
 from ._lib import AttnError, LIB_PATH, launch_count, lib  # noqa: F401  (fails loudly if unbuilt)
 from . import dp, mha_ops  # noqa: F401
 from .mha import DeviceBuffer, GPTConfig, KVCache, MultiHeadAttention, Parameter  # noqa: F401
+from .ffn import FeedForward  # noqa: F401
 from .mha_ops import get_shared_mha_module, THREADS_PER_BLOCK, SOFTMAX_BLOCK_THREADS  # noqa: F401
 
-__all__ = ["MultiHeadAttention", "GPTConfig", "Parameter", "DeviceBuffer", "KVCache", "mha_ops", "dp", "AttnError",
+__all__ = ["MultiHeadAttention", "FeedForward", "GPTConfig", "Parameter", "DeviceBuffer", "KVCache", "mha_ops", "dp", "AttnError",
            "get_shared_mha_module", "launch_count"]

@@ -19,6 +19,9 @@ ATTN_ERR_CUDA = -3
 ATTN_ERR_WORKSPACE = -4
 ATTN_F32 = 0
 ATTN_BF16 = 1
+ATTN_ACT_NONE = 0
+ATTN_ACT_GELU = 1
+ATTN_ACT_GELU_BWD = 2
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -43,6 +46,7 @@ SIGNATURES = {
                                  _i, _p]),
     "attn_probs": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _f, _i, _p]),
     "attn_gemm": (_i, [_p, _i64, _i, _p, _i64, _i, _i, _p, _i64, _i, _p, _i, _i, _i, _i, _p]),
+    "attn_gemm_act": (_i, [_p, _i64, _i, _p, _i64, _i, _i, _p, _i64, _i, _p, _i, _i, _i, _i, _p, _i64, _i, _p]),
     "attn_colsum_workspace_size": (_sz, [_i, _i]),
     "attn_colsum": (_i, [_p, _i, _i64, _i, _i, _p, _i, _p, _sz, _p]),
     "attn_cast_f32_to_bf16": (_i, [_p, _p, _i64, _p]),

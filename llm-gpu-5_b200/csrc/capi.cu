@@ -126,7 +126,8 @@ int attn_bwd_simt(const void*, const void*, const void*, const void*, const void
                   void*, void*, void*, float*, int, int, int, int, const int64_t*, float, int,
                   cudaStream_t);
 int gemm_simt(const void*, int64_t, int, const void*, int64_t, int, int, void*, int64_t, int,
-              const float*, int, int, int, int, cudaStream_t);
+              const float*, int, int, int, int, cudaStream_t, int act = ACT_NONE, void* aux = nullptr,
+              int64_t ldaux = 0, int aux_dtype = ATTN_F32);
 int split_heads(const float*, float*, float*, float*, int, int, int, int, cudaStream_t);
 int merge_heads(const float*, float*, int, int, int, int, cudaStream_t);
 int cast_f32_bf16(const float*, void*, int64_t, cudaStream_t, int);
@@ -155,7 +156,10 @@ int attn_bwd_tc(const void*, const void*, const void*, const void*, const void*,
 bool tc_gemm_supported(int M, int N, int K, int64_t lda, int a_trans, int64_t ldb, int b_trans,
                        const void* A, const void* B);
 int gemm_tc(const void*, int64_t, int, const void*, int64_t, int, void*, int64_t, int,
-            const float*, int, int, int, int, cudaStream_t);
+            const float*, int, int, int, int, cudaStream_t, int act = ACT_NONE, const void* aux = nullptr,
+            int64_t ldaux = 0, int aux_dtype = ATTN_F32);
+bool tc_gemm_act_ok(const void* C, int64_t ldc, int c_dtype, int act, const void* aux, int64_t ldaux,
+                    int aux_dtype);
 
 static size_t elem_size(int dtype) { return dtype == ATTN_F32 ? 4 : 2; }
 
@@ -307,6 +311,31 @@ int attn_gemm(const void* A, int64_t lda, int a_trans, const void* B, int64_t ld
                    as_stream(stream));
   return gemm_simt(A, lda, a_trans, B, ldb, b_trans, ab_dtype, C, ldc, c_dtype, bias, M, N, K,
                    accumulate, as_stream(stream));
+}
+
+int attn_gemm_act(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans,
+                  int ab_dtype, void* C, int64_t ldc, int c_dtype, const float* bias, int M, int N, int K, int act,
+                  void* aux, int64_t ldaux, int aux_dtype, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(A && B && C, "attn_gemm_act: null pointer argument");
+  ATTN_REQUIRE(M > 0 && N > 0 && K > 0, "attn_gemm_act: M, N, K must be positive");
+  ATTN_REQUIRE(ab_dtype == ATTN_F32 || ab_dtype == ATTN_BF16, "attn_gemm_act: bad operand dtype");
+  ATTN_REQUIRE(c_dtype == ATTN_F32 || c_dtype == ATTN_BF16, "attn_gemm_act: bad output dtype");
+  ATTN_REQUIRE(aux_dtype == ATTN_F32 || aux_dtype == ATTN_BF16, "attn_gemm_act: bad aux dtype");
+  ATTN_REQUIRE(act == ATTN_ACT_NONE || act == ATTN_ACT_GELU || act == ATTN_ACT_GELU_BWD,
+               "attn_gemm_act: unknown activation %d", act);
+  ATTN_REQUIRE(act != ATTN_ACT_GELU_BWD || aux, "attn_gemm_act: ATTN_ACT_GELU_BWD needs the pre-activation aux");
+  ATTN_REQUIRE(!aux || ldaux >= N, "attn_gemm_act: ldaux too small");
+  ATTN_REQUIRE(!aux || (aux != C), "attn_gemm_act: aux and C must not alias");
+  ATTN_REQUIRE(lda >= (a_trans ? M : K) && ldb >= (b_trans ? K : N) && ldc >= N,
+               "attn_gemm_act: leading dimensions too small");
+  if (act == ATTN_ACT_NONE) aux = nullptr;
+  if (ab_dtype == ATTN_BF16 && tc_gemm_supported(M, N, K, lda, a_trans, ldb, b_trans, A, B) &&
+      tc_gemm_act_ok(C, ldc, c_dtype, act, aux, ldaux, aux_dtype))
+    return gemm_tc(A, lda, a_trans, B, ldb, b_trans, C, ldc, c_dtype, bias, M, N, K, 0, as_stream(stream), act,
+                   aux, ldaux, aux_dtype);
+  return gemm_simt(A, lda, a_trans, B, ldb, b_trans, ab_dtype, C, ldc, c_dtype, bias, M, N, K, 0,
+                   as_stream(stream), act, aux, ldaux, aux_dtype);
 }
 
 size_t attn_colsum_workspace_size(int M, int N) {

@@ -70,4 +70,35 @@ __device__ __forceinline__ void store4(__nv_bfloat16* p, float4 v) {
   *reinterpret_cast<uint2*>(p) = u;
 }
 
+// ---- GELU of the feed-forward block ---------------------------------------------------------
+// The tanh form of activation_kernel (core/kernels.py:243-248), gelu(x) = 0.5 x (1 + tanh(u)) with
+// u = K0 (x + K1 x^3), and its derivative as gelu_backward_kernel writes it (core/kernels.py:432-440).
+// FAST selects the tanh.approx.f32 instruction (the bf16 tensor-core path, whose outputs are rounded
+// to bf16 anyway); otherwise tanhf (the float32 path, 1e-5 parity).
+constexpr float GELU_K0 = 0.7978845608f, GELU_K1 = 0.044715f, GELU_K1x3 = 0.134145f;
+enum { ACT_NONE = ATTN_ACT_NONE, ACT_GELU = ATTN_ACT_GELU, ACT_GELU_BWD = ATTN_ACT_GELU_BWD };
+
+template <bool FAST>
+__device__ __forceinline__ float gelu_tanh_of(float x) {
+  const float u = GELU_K0 * (x + GELU_K1 * x * x * x);
+  if constexpr (FAST) {
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+    return t;
+  } else {
+    return tanhf(u);
+  }
+}
+
+template <bool FAST>
+__device__ __forceinline__ float gelu_fwd(float x) {
+  return 0.5f * x * (1.f + gelu_tanh_of<FAST>(x));
+}
+
+template <bool FAST>
+__device__ __forceinline__ float gelu_grad(float x) {
+  const float t = gelu_tanh_of<FAST>(x);
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * (GELU_K0 * (1.f + GELU_K1x3 * x * x));
+}
+
 }  // namespace attn

@@ -4,6 +4,8 @@
 // the dot) generalised to the transposed operands of the projection gradients
 // (model/gpt.py:666-689).  64x64 output tile per CTA, 256 threads with a 4x4 register tile each,
 // K staged through shared memory 16 at a time with coalesced global reads for either majorness.
+// The epilogue applies the feed-forward activations of the tensor-core GEMM (ACT_GELU with an
+// optional pre-activation output, ACT_GELU_BWD scaling by gelu'(aux)) with tanhf, in float32.
 #include "common.cuh"
 
 namespace attn {
@@ -14,7 +16,8 @@ template <typename TI, typename TO>
 __global__ void __launch_bounds__(256)
 gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* __restrict__ Bm,
                  int64_t ldb, int b_trans, TO* __restrict__ C, int64_t ldc,
-                 const float* __restrict__ bias, int M, int N, int K, int accumulate, int k_chunk) {
+                 const float* __restrict__ bias, int M, int N, int K, int accumulate, int k_chunk, int act,
+                 void* __restrict__ aux, int64_t ldaux, int aux_bf16) {
   __shared__ __align__(16) float As[SG_BK][SG_BM];
   __shared__ __align__(16) float Bs[SG_BK][SG_BN];
   const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
@@ -65,6 +68,19 @@ gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* _
       if (gn >= N) continue;
       float val = acc[i][j];
       if (bias && blockIdx.z == 0) val += bias[gn];
+      if (act == ACT_GELU) {
+        if (aux) {
+          if (aux_bf16)
+            reinterpret_cast<__nv_bfloat16*>(aux)[(int64_t)gm * ldaux + gn] = __float2bfloat16_rn(val);
+          else
+            reinterpret_cast<float*>(aux)[(int64_t)gm * ldaux + gn] = val;
+        }
+        val = gelu_fwd<false>(val);
+      } else if (act == ACT_GELU_BWD) {
+        const float x = aux_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(aux)[(int64_t)gm * ldaux + gn])
+                                 : reinterpret_cast<const float*>(aux)[(int64_t)gm * ldaux + gn];
+        val *= gelu_grad<false>(x);
+      }
       TO* dst = C + (int64_t)gm * ldc + gn;
       if (split) {  // float32 C only (host-checked)
         atomicAdd(reinterpret_cast<float*>(dst), val);
@@ -78,12 +94,13 @@ gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* _
 
 int gemm_simt(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans,
               int ab_dtype, void* C, int64_t ldc, int c_dtype, const float* bias, int M, int N,
-              int K, int accumulate, cudaStream_t s) {
+              int K, int accumulate, cudaStream_t s, int act, void* aux, int64_t ldaux, int aux_dtype) {
   dim3 grid((N + SG_BN - 1) / SG_BN, (M + SG_BM - 1) / SG_BM);
+  const int aux_bf16 = aux_dtype == ATTN_BF16;
   // split K when the output tiles fill less than two waves and K is long (float32 C only)
   int splits = 1;
   const int64_t tiles = (int64_t)grid.x * grid.y, want = 2 * 148;
-  if (c_dtype == ATTN_F32 && tiles < want && K >= 512) {
+  if (c_dtype == ATTN_F32 && act == ACT_NONE && tiles < want && K >= 512) {
     splits = (int)((want + tiles - 1) / tiles);
     const int max_splits = K / 256;  // at least 256 of K per split
     if (splits > max_splits) splits = max_splits;
@@ -102,19 +119,18 @@ int gemm_simt(const void* A, int64_t lda, int a_trans, const void* B, int64_t ld
     }
   }
   grid.z = splits;
+#define SG_LAUNCH(TI, TO)                                                                                  \
+  gemm_simt_kernel<TI, TO><<<grid, 256, 0, s>>>((const TI*)A, lda, a_trans, (const TI*)B, ldb, b_trans, (TO*)C, \
+                                                ldc, bias, M, N, K, accumulate, k_chunk, act, aux, ldaux, aux_bf16)
   if (ab_dtype == ATTN_F32 && c_dtype == ATTN_F32)
-    gemm_simt_kernel<float, float><<<grid, 256, 0, s>>>((const float*)A, lda, a_trans, (const float*)B,
-        ldb, b_trans, (float*)C, ldc, bias, M, N, K, accumulate, k_chunk);
+    SG_LAUNCH(float, float);
   else if (ab_dtype == ATTN_F32 && c_dtype == ATTN_BF16)
-    gemm_simt_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>((const float*)A, lda, a_trans,
-        (const float*)B, ldb, b_trans, (__nv_bfloat16*)C, ldc, bias, M, N, K, accumulate, k_chunk);
+    SG_LAUNCH(float, __nv_bfloat16);
   else if (ab_dtype == ATTN_BF16 && c_dtype == ATTN_F32)
-    gemm_simt_kernel<__nv_bfloat16, float><<<grid, 256, 0, s>>>((const __nv_bfloat16*)A, lda, a_trans,
-        (const __nv_bfloat16*)B, ldb, b_trans, (float*)C, ldc, bias, M, N, K, accumulate, k_chunk);
+    SG_LAUNCH(__nv_bfloat16, float);
   else
-    gemm_simt_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)A, lda,
-        a_trans, (const __nv_bfloat16*)B, ldb, b_trans, (__nv_bfloat16*)C, ldc, bias, M, N, K,
-        accumulate, k_chunk);
+    SG_LAUNCH(__nv_bfloat16, __nv_bfloat16);
+#undef SG_LAUNCH
   count_launch();
   return check_launch("gemm_simt_kernel");
 }

@@ -17,6 +17,13 @@
 // Weight-gradient shapes (M, N = d_model, K = tokens) are split along K; the splits add their
 // partial tiles into C with TMA reduce-adds (C is zeroed first unless accumulating).  Outputs
 // without a 16-byte row pitch fall back to direct per-row stores (fp32 atomics for K splits).
+//
+// The epilogue can also apply the feed-forward block's activation (FeedForward, model/gpt.py:
+// 327-456): ACT_GELU writes gelu(acc + bias) to C and, when an aux output is given, the
+// pre-activation acc + bias to it through a second TMA map (matmul_2d_kernel + the in-place
+// activation_kernel + the cache_pre_act copy, model/gpt.py:345-361); ACT_GELU_BWD multiplies the
+// accumulator by gelu'(aux[m, n]) (dHidden = dOut W^T followed by gelu_backward_kernel,
+// model/gpt.py:437-438).  Activations run without K splits and without accumulation.
 #include "tc_common.cuh"
 
 #include <string.h>
@@ -42,8 +49,53 @@ struct GemmParams {
   int tma_epi;  // 1: stage output chunks in swizzled smem and write them with TMA
   int reduce;   // with tma_epi: add into C (accumulate or K splits) instead of storing
   const float* bias;
+  int act;          // ACT_NONE, ACT_GELU, ACT_GELU_BWD (tma_epi only)
+  const void* aux;  // ACT_GELU: pre-activation output (C's dtype) or null; ACT_GELU_BWD: input
+  int64_t ldaux;
+  int aux_bf16;
   int* err;
 };
+
+// The aux operand of ACT_GELU_BWD for one accumulator row: columns n0 .. n0+cols-1 as floats
+// (columns past N read as 0).  A thread reads its own row (a whole 128-byte line or two).
+__device__ __forceinline__ void load_aux_row(const GemmParams& p, int64_t m, int n0, int cols, float (&a)[64]) {
+  const bool full = n0 + cols <= p.N;
+  if (p.aux_bf16) {
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.aux) + m * p.ldaux + n0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (8 * i < cols) {
+          const uint4 u = reinterpret_cast<const uint4*>(src)[i];
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+            a[8 * i + 2 * j] = f.x;
+            a[8 * i + 2 * j + 1] = f.y;
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) a[i] = i < cols && n0 + i < p.N ? __bfloat162float(src[i]) : 0.f;
+    }
+  } else {
+    const float* src = reinterpret_cast<const float*>(p.aux) + m * p.ldaux + n0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (4 * i < cols) {
+          const float4 f = reinterpret_cast<const float4*>(src)[i];
+          a[4 * i] = f.x; a[4 * i + 1] = f.y; a[4 * i + 2] = f.z; a[4 * i + 3] = f.w;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) a[i] = i < cols && n0 + i < p.N ? src[i] : 0.f;
+    }
+  }
+}
 
 __device__ __forceinline__ void unit_coords(const GemmParams& p, int unit, int& tm, int& tn, int& kb0,
                                             int& kb1) {
@@ -107,7 +159,8 @@ __device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int
 
 __global__ void __launch_bounds__(GT_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux,
+               const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi = smem + GT_STAGES * GT_STAGE_BYTES;  // [2] output staging chunks
@@ -223,6 +276,36 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const bool leader = (warp == 2 && lane == 0);
     const int cols = p.c_bf16 ? 64 : 32;  // columns per 128-byte chunk
     int buf = 0;
+    // stage 32 packed words per thread (one 128-byte chunk row) and write the 128-row chunk at
+    // column n0 through `map`; two staging buffers alternate
+    auto emit = [&](const CUtensorMap* map, const uint32_t (&w)[32], int n0, int m0, bool reduce) {
+      if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
+      named_bar_sync(1, 128);
+      uint8_t* rowp = epi + buf * GT_EPI_BYTES + row * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) =
+            make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
+      fence_proxy_async_smem();
+      named_bar_sync(1, 128);
+      if (leader) {
+        if (reduce)
+          tma_reduce_add_2d(map, epi + buf * GT_EPI_BYTES, n0, m0);
+        else
+          tma_store_2d(map, epi + buf * GT_EPI_BYTES, n0, m0);
+        bulk_commit();
+      }
+      buf ^= 1;
+    };
+    auto pack = [&](const float (&v)[64], uint32_t (&w)[32]) {
+      if (p.c_bf16) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+      }
+    };
     int local = 0;
     for (int unit = blockIdx.x; unit < p.units; unit += gridDim.x, ++local) {
       int tm, tn, kb0, kb1;
@@ -246,6 +329,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
 #pragma unroll 1
       for (int c0 = 0; c0 < GT_BN; c0 += cols) {
+        const int n0 = tn * GT_BN + c0;
+        const int64_t m = (int64_t)tm * GT_BM + row;
+        float a[64];
+        if (p.act == ACT_GELU_BWD && n0 < p.N && m < p.M) load_aux_row(p, m, n0, cols, a);  // in flight
         uint32_t r[64];
         tmem_ld32(taddr + c0, *reinterpret_cast<uint32_t(*)[32]>(r));
         if (p.c_bf16) tmem_ld32(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
@@ -254,7 +341,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
-        const int n0 = tn * GT_BN + c0;
         if (n0 >= p.N) continue;  // uniform across the CTA
         float v[64];
 #pragma unroll
@@ -273,30 +359,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
         }
         uint32_t w[32];
-        if (p.c_bf16) {
+        if (p.act == ACT_GELU) {
+          if (p.aux) {  // the pre-activation, for the backward
+            pack(v, w);
+            emit(&tmAux, w, n0, tm * GT_BM, false);
+          }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-        } else {
+          for (int i = 0; i < 64; ++i)
+            if (i < cols) v[i] = gelu_fwd<true>(v[i]);
+        } else if (p.act == ACT_GELU_BWD) {
+          if (m < p.M) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+            for (int i = 0; i < 64; ++i)
+              if (i < cols) v[i] *= gelu_grad<true>(a[i]);
+          }
         }
-        if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
-        named_bar_sync(1, 128);
-        uint8_t* rowp = epi + buf * GT_EPI_BYTES + row * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) =
-              make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
-        fence_proxy_async_smem();
-        named_bar_sync(1, 128);
-        if (leader) {
-          if (p.reduce)
-            tma_reduce_add_2d(&tmC, epi + buf * GT_EPI_BYTES, n0, tm * GT_BM);
-          else
-            tma_store_2d(&tmC, epi + buf * GT_EPI_BYTES, n0, tm * GT_BM);
-          bulk_commit();
-        }
-        buf ^= 1;
+        pack(v, w);
+        emit(&tmC, w, n0, tm * GT_BM, p.reduce != 0);
       }
     }
     if (leader) bulk_wait0();
@@ -374,9 +453,25 @@ static int choose_splits(int tiles, int kb_total, int sms) {
   return best;
 }
 
+// Whether the epilogue can apply `act` here: it needs the TMA epilogue (16-byte aligned C and row
+// pitch), an aux output of C's dtype for ACT_GELU, and 16-byte aligned aux rows for vector reads.
+bool tc_gemm_act_ok(const void* C, int64_t ldc, int c_dtype, int act, const void* aux, int64_t ldaux,
+                    int aux_dtype) {
+  const int64_t cq = c_dtype == ATTN_BF16 ? 8 : 4, aq = aux_dtype == ATTN_BF16 ? 8 : 4;
+  if (act == ACT_NONE) return true;
+  if (!aligned(C, 16) || ldc % cq != 0) return false;
+  if (!aux) return act == ACT_GELU;
+  if (act == ACT_GELU && aux_dtype != c_dtype) return false;
+  return aligned(aux, 16) && ldaux % aq == 0;
+}
+
 int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans, void* C,
             int64_t ldc, int c_dtype, const float* bias, int M, int N, int K, int accumulate,
-            cudaStream_t s) {
+            cudaStream_t s, int act, const void* aux, int64_t ldaux, int aux_dtype) {
+  if (act != ACT_NONE && (accumulate || !tc_gemm_act_ok(C, ldc, c_dtype, act, aux, ldaux, aux_dtype))) {
+    set_error("gemm_tc: activation epilogue unsupported for this output layout");
+    return ATTN_ERR_UNSUPPORTED;
+  }
   CUtensorMap tmA, tmB;
   {
     uint64_t dims[2], strides[1];
@@ -409,7 +504,7 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   p.kb_total = (K + GT_BK - 1) / GT_BK;
   const int sms = num_sms();
   const int tiles = p.tiles_m * p.tiles_n;
-  int splits = c_dtype == ATTN_F32 ? choose_splits(tiles, p.kb_total, sms) : 1;
+  int splits = c_dtype == ATTN_F32 && act == ACT_NONE ? choose_splits(tiles, p.kb_total, sms) : 1;
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
   p.units = tiles * splits;
@@ -419,12 +514,17 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   p.accumulate = accumulate;
   p.atomic = splits > 1;
   p.bias = bias;
+  p.act = act;
+  p.aux = aux;
+  p.ldaux = ldaux;
+  p.aux_bf16 = aux_dtype == ATTN_BF16;
   p.vec_ok = aligned(C, 16) && (ldc % (p.c_bf16 ? 8 : 4) == 0);
   p.err = dev_error_ptr();
   if (!p.err) return ATTN_ERR_CUDA;
   // TMA epilogue whenever C is 16-byte aligned with 16-byte row pitch
-  CUtensorMap tmC;
+  CUtensorMap tmC, tmAux;
   memset(&tmC, 0, sizeof(tmC));
+  memset(&tmAux, 0, sizeof(tmAux));
   p.tma_epi = p.vec_ok ? 1 : 0;
   p.reduce = (accumulate || p.atomic) ? 1 : 0;
   if (p.tma_epi) {
@@ -434,6 +534,12 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
     const bool ok = p.c_bf16 ? make_tmap_bf16(&tmC, C, 2, dims, strides, box)
                              : make_tmap_f32(&tmC, C, 2, dims, strides, box);
     if (!ok) return ATTN_ERR_CUDA;
+    if (act == ACT_GELU && aux) {  // the pre-activation output, same geometry as C
+      const uint64_t astr[1] = {(uint64_t)ldaux * (p.c_bf16 ? 2 : 4)};
+      const bool ok2 = p.c_bf16 ? make_tmap_bf16(&tmAux, aux, 2, dims, astr, box)
+                                : make_tmap_f32(&tmAux, aux, 2, dims, astr, box);
+      if (!ok2) return ATTN_ERR_CUDA;
+    }
   }
   if (p.atomic && !accumulate)
     ATTN_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s));
@@ -443,7 +549,7 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
     attr_set = true;
   }
   const int grid = p.units < sms ? p.units : sms;
-  gemm_tc_kernel<<<grid, GT_THREADS, GT_SMEM, s>>>(tmA, tmB, tmC, p);
+  gemm_tc_kernel<<<grid, GT_THREADS, GT_SMEM, s>>>(tmA, tmB, tmC, tmAux, p);
   count_launch();
   return check_launch("gemm_tc_kernel");
 }

@@ -13,7 +13,7 @@ import math
 
 import torch
 
-from ._lib import ATTN_BF16, ATTN_F32, call, lib
+from ._lib import ATTN_ACT_GELU, ATTN_ACT_GELU_BWD, ATTN_ACT_NONE, ATTN_BF16, ATTN_F32, call, lib  # noqa: F401
 
 THREADS_PER_BLOCK = 256
 SOFTMAX_BLOCK_THREADS = 64
@@ -129,6 +129,16 @@ def gemm(A: int, lda: int, a_trans: bool, B: int, ldb: int, b_trans: bool, ab_dt
     """C[M,N] (=|+=) op(A) op(B) (+bias) on raw device addresses (see include/attn_b200.h)."""
     call("attn_gemm", A, lda, int(a_trans), B, ldb, int(b_trans), dtype_code(ab_dtype), C, ldc,
          dtype_code(c_dtype), bias, M, N, K, int(accumulate), _stream())
+
+
+def gemm_act(A: int, lda: int, a_trans: bool, B: int, ldb: int, b_trans: bool, ab_dtype: torch.dtype,
+             C: int, ldc: int, c_dtype: torch.dtype, M: int, N: int, K: int, act: int, aux: int | None = None,
+             ldaux: int = 0, aux_dtype: torch.dtype = torch.float32, bias: int | None = None):
+    """GEMM with the feed-forward activation in its epilogue (attn_gemm_act): ATTN_ACT_GELU writes
+    gelu(op(A) op(B) + bias) to C and the pre-activation to aux; ATTN_ACT_GELU_BWD writes
+    op(A) op(B) * gelu'(aux)."""
+    call("attn_gemm_act", A, lda, int(a_trans), B, ldb, int(b_trans), dtype_code(ab_dtype), C, ldc,
+         dtype_code(c_dtype), bias, M, N, K, int(act), aux, ldaux, dtype_code(aux_dtype), _stream())
 
 
 def colsum(X: int, x_dtype: torch.dtype, ldx: int, M: int, N: int, out: torch.Tensor,

@@ -9,6 +9,9 @@ executed), takes
 
 * ``LAYERNORM_KERNEL`` (core/kernels.py:73-110): ``layernorm_kernel``, one thread per row;
 * ``LAYERNORM_BACKWARD_KERNEL`` (core/kernels.py:359-420): ``layernorm_backward_kernel``;
+* the FeedForward kernels (core/kernels.py): ``MATMUL_2D_KERNEL`` (:117-140), ``ACTIVATION_KERNEL``
+  (:233-250), ``MATMUL_BACKWARD_WEIGHTS_KERNEL`` (:333-356), ``GELU_BACKWARD_KERNEL`` (:422-447),
+  ``REDUCE_SUM_AXIS0_KERNEL`` (:449-470), ``MATMUL_BACKWARD_INPUT_KERNEL`` (:472-497);
 * ``MHA_KERNELS_STRING`` (core/mha_kernels.py:53-...): among others
   ``fused_attention_forward_kernel`` (core/mha_kernels.py:404-521), the gradient kernels the
   reference's GPU golden test chains (``matmul_score_kernel``, ``softmax_fused_backward``,
@@ -94,6 +97,47 @@ extern "C" int ref_attention_backward(const float* q, const float* k, const floa
   return rc;
 }
 
+// FeedForward.forward's kernel sequence (model/gpt.py:345-363) with the launch geometry of core/ops.py:
+// matmul_2d_kernel on 16x16 blocks (:163-168), the pre-activation copy, activation_kernel on 256
+// threads (:255-258), matmul_2d_kernel again.  pre/act/out [M, 4C] / [M, 4C] / [M, C].
+extern "C" int ref_ffn_forward(const float* x, const float* w_fc, const float* b_fc, const float* w_proj,
+                               const float* b_proj, float* pre, float* act, float* out, int M, int C) {
+  const int H = 4 * C;
+  const dim3 blk(16, 16);
+  matmul_2d_kernel<<<dim3((H + 15) / 16, (M + 15) / 16), blk>>>(x, w_fc, b_fc, pre, M, H, C);
+  if (cudaMemcpy(act, pre, (size_t)M * H * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) return -1;
+  activation_kernel<<<(M * H + 255) / 256, 256>>>(act, M * H);
+  matmul_2d_kernel<<<dim3((C + 15) / 16, (M + 15) / 16), blk>>>(act, w_proj, b_proj, out, M, C, H);
+  return (int)cudaDeviceSynchronize();
+}
+
+// FeedForward.backward's GPU-resident path (model/gpt.py:428-443): matmul_backward_weights (16x16,
+// core/ops.py:388-394), reduce_sum_axis0 into zeroed sums (256 threads over rows, :491-498),
+// matmul_backward_input (16x16, :526-531), gelu_backward (256 threads, :462-466).  Scratch is
+// allocated here (checker code only).
+extern "C" int ref_ffn_backward(const float* dout, const float* x, const float* pre, const float* act,
+                                const float* w_fc, const float* w_proj, float* din, float* d_fc_w, float* d_fc_b,
+                                float* d_proj_w, float* d_proj_b, int M, int C) {
+  const int H = 4 * C;
+  const dim3 blk(16, 16);
+  float *dhidden = 0, *dpre = 0;
+  if (cudaMalloc(&dhidden, (size_t)M * H * 4) != cudaSuccess || cudaMalloc(&dpre, (size_t)M * H * 4) != cudaSuccess)
+    return -1;
+  if (cudaMemset(d_proj_b, 0, (size_t)C * 4) != cudaSuccess || cudaMemset(d_fc_b, 0, (size_t)H * 4) != cudaSuccess)
+    return -1;
+  matmul_backward_weights_kernel<<<dim3((C + 15) / 16, (H + 15) / 16), blk>>>(act, dout, d_proj_w, M, C, H);
+  reduce_sum_axis0_kernel<<<(M + 255) / 256, 256>>>(dout, d_proj_b, M, C, C);
+  matmul_backward_input_kernel<<<dim3((H + 15) / 16, (M + 15) / 16), blk>>>(dout, w_proj, dhidden, M, C, H);
+  gelu_backward_kernel<<<(M * H + 255) / 256, 256>>>(dhidden, pre, dpre, M * H);
+  matmul_backward_weights_kernel<<<dim3((H + 15) / 16, (C + 15) / 16), blk>>>(x, dpre, d_fc_w, M, H, C);
+  reduce_sum_axis0_kernel<<<(M + 255) / 256, 256>>>(dpre, d_fc_b, M, H, H);
+  matmul_backward_input_kernel<<<dim3((C + 15) / 16, (M + 15) / 16), blk>>>(dpre, w_fc, din, M, H, C);
+  const int rc = (int)cudaDeviceSynchronize();
+  cudaFree(dhidden);
+  cudaFree(dpre);
+  return rc;
+}
+
 // The layout adapters, 256 threads per block over B*T*NH*HD elements (model/gpt.py:569-598).
 extern "C" int ref_split_heads(const float* qkv, float* q, float* k, float* v, int B, int T, int NH, int HD) {
   const int total = B * T * NH * HD, threads = 256;
@@ -131,12 +175,17 @@ def build(reference_root: str) -> str:
     ln = _string_constant(os.path.join(reference_root, "core", "kernels.py"), "LAYERNORM_KERNEL")
     ln_bwd = _string_constant(os.path.join(reference_root, "core", "kernels.py"), "LAYERNORM_BACKWARD_KERNEL")
     mha = _string_constant(os.path.join(reference_root, "core", "mha_kernels.py"), "MHA_KERNELS_STRING")
+    ffn = [_string_constant(os.path.join(reference_root, "core", "kernels.py"), name)
+           for name in ("MATMUL_2D_KERNEL", "ACTIVATION_KERNEL", "MATMUL_BACKWARD_WEIGHTS_KERNEL",
+                        "GELU_BACKWARD_KERNEL", "REDUCE_SUM_AXIS0_KERNEL", "MATMUL_BACKWARD_INPUT_KERNEL")]
     os.makedirs(OUT, exist_ok=True)
     src = os.path.join(OUT, "ref_kernels.cu")
     with open(src, "w") as f:
         f.write("// Generated by oracle/build_ref.py from the reference's kernel strings; not part of the repo.\n")
         f.write(ln)
         f.write(ln_bwd)
+        for k in ffn:
+            f.write(k)
         f.write('\nextern "C" {\n')
         f.write(mha)
         f.write("\n}\n")

@@ -215,6 +215,55 @@ def layernorm_backward(dy, x, gamma, eps=1e-5, dtype=np.float64):
     return dx, (dy * xh).sum(0), dy.sum(0)
 
 
+# The tanh form of GELU the reference uses in activation_kernel and gelu_backward_kernel
+# (core/kernels.py:243-248, :432-440; model/gpt.py:403-410): sqrt(2/pi) and 3 * 0.044715.
+GELU_K0 = 0.7978845608
+GELU_K1 = 0.044715
+GELU_K1x3 = 0.134145
+
+
+def gelu(x, dtype=np.float64):
+    """activation_kernel (core/kernels.py:237-250): 0.5 x (1 + tanh(K0 (x + K1 x^3)))."""
+    x = np.asarray(x, dtype=dtype)
+    return 0.5 * x * (1.0 + np.tanh(GELU_K0 * (x + GELU_K1 * x ** 3)))
+
+
+def gelu_grad(x, dtype=np.float64):
+    """d gelu / dx as FeedForward's NumPy backward writes it (model/gpt.py:403-410) and
+    gelu_backward_kernel computes it (core/kernels.py:424-447)."""
+    x = np.asarray(x, dtype=dtype)
+    t = np.tanh(GELU_K0 * (x + GELU_K1 * x ** 3))
+    return 0.5 * (1.0 + t) + 0.5 * x * (1.0 - t * t) * (GELU_K0 * (1.0 + GELU_K1x3 * x * x))
+
+
+def ffn_forward(x, w_fc, b_fc, w_proj, b_proj, dtype=np.float64):
+    """FeedForward.forward (model/gpt.py:327-365): pre = x W_fc + b_fc (matmul_2d_kernel, bias after
+    the dot), act = gelu(pre) in place, out = act W_proj + b_proj.  Returns (out, cache) with the
+    three cached activations of the reference (cache_input, cache_pre_act, cache_activated)."""
+    x = np.asarray(x, dtype=dtype)
+    pre = linear(x, w_fc, b_fc, dtype)
+    act = gelu(pre, dtype)
+    out = linear(act, w_proj, b_proj, dtype)
+    return out, dict(x=x, pre=pre, act=act)
+
+
+def ffn_backward(cache, dout, w_fc, w_proj, dtype=np.float64):
+    """FeedForward.backward's NumPy path (model/gpt.py:381-426) step for step:
+    dProjW = act^T dOut, dProjB = sum(dOut), dHidden = dOut W_proj^T, dPre = dHidden * gelu'(pre),
+    dFcW = x^T dPre, dFcB = sum(dPre), dIn = dPre W_fc^T.
+    Returns (dIn, dFcW, dFcB, dProjW, dProjB)."""
+    dout = np.asarray(dout, dtype=dtype)
+    w_fc = np.asarray(w_fc, dtype=dtype)
+    w_proj = np.asarray(w_proj, dtype=dtype)
+    d_proj_w = cache["act"].T @ dout
+    d_proj_b = dout.sum(0)
+    d_pre = (dout @ w_proj.T) * gelu_grad(cache["pre"], dtype)
+    d_fc_w = cache["x"].T @ d_pre
+    d_fc_b = d_pre.sum(0)
+    d_in = d_pre @ w_fc.T
+    return d_in, d_fc_w, d_fc_b, d_proj_w, d_proj_b
+
+
 def rel_err(actual, ref) -> float:
     """max|actual - ref| / max|ref|: the per-tensor relative error the tolerances are stated in."""
     a = np.asarray(actual, dtype=np.float64)

@@ -12,7 +12,11 @@ Python, so this script installs a host-memory stand-in for ``pycuda.driver`` /
   produce the kernel-level fixture, with the exact inputs of its Layer 1 (seed 1337, H=3, M=17,
   D=8; test_mha_golden_model.py:41-45, 98-101, 513-518);
 * ``model.gpt.MultiHeadAttention`` runs its real ``forward`` (model/gpt.py:531-631) and its real
-  NumPy ``backward`` (model/gpt.py:633-698).  The four kernels ``forward`` launches are emulated on
+  NumPy ``backward`` (model/gpt.py:633-698).
+* ``model.gpt.FeedForward`` runs its real ``forward`` (model/gpt.py:327-365) and its NumPy
+  ``backward`` (``use_cpu_backward = True``, model/gpt.py:381-426), with ``activation_kernel``
+  (core/kernels.py:237-250) emulated in float32 on the host; the scenario of
+  test_ffn_gpu_backward.py:35-56 (seed 1337, C=16, M=6, dOut = output) and a wider one.  The four kernels ``forward`` launches are emulated on
   the host: ``matmul_2d_kernel`` (core/kernels.py:119-140), ``split_heads_kernel``
   (core/mha_kernels.py:534-558), ``merge_heads_kernel`` (core/mha_kernels.py:567-584) by their
   index arithmetic, and ``fused_attention_forward_kernel`` by the reference's own golden forward
@@ -170,7 +174,13 @@ def _make_kernels(golden_mod_getter):
         row_sum.view(np.float32, H * M)[:] = np.where(mask, np.exp(masked - mx[..., None]), 0.0) \
             .sum(-1).astype(np.float32).reshape(-1)
 
-    return dict(matmul_2d_kernel=matmul_2d_kernel, split_heads_kernel=split_heads_kernel,
+    def activation_kernel(D, n, **launch):
+        x = D.view(np.float32, int(n))
+        inner = np.float32(0.7978845608) * (x + np.float32(0.044715) * (x * x * x))
+        x[:] = np.float32(0.5) * x * (np.float32(1.0) + np.tanh(inner))
+
+    return dict(matmul_2d_kernel=matmul_2d_kernel, activation_kernel=activation_kernel,
+                split_heads_kernel=split_heads_kernel,
                 merge_heads_kernel=merge_heads_kernel,
                 fused_attention_forward_kernel=fused_attention_forward_kernel)
 
@@ -238,6 +248,47 @@ def _run_reference_mha(gpt, cuda, B, T, C, NH, param_seed, data_seed, x=None, do
                 B=B, T=T, C=C, NH=NH)
 
 
+def _run_reference_ffn(gpt, cuda, C, M, seed, dout_seed=None, bias_scale=0.0):
+    """FeedForward forward + NumPy backward.  dout_seed None: dOut = output, the synthetic loss
+    0.5 * sum(out^2) of test_ffn_gpu_backward.py:51-53; otherwise dOut ~ N(0, 1)."""
+    np.random.seed(seed)
+    config = gpt.GPTConfig(vocab_size=64, embedding_dim=C, num_heads=2, max_len=8)
+    ffn = gpt.FeedForward(config)
+    if bias_scale:  # the reference initialises both biases to zero; give them values
+        brng = np.random.RandomState(seed + 1)
+        for p in (ffn.c_fc_b, ffn.c_proj_b):
+            cuda.memcpy_htod(p.gpu_weights, brng.normal(0.0, bias_scale, size=p.shape).astype(np.float32))
+    x = np.random.normal(0.0, 1.0, size=(M, C)).astype(np.float32)
+    gx = cuda.mem_alloc(x.nbytes)
+    cuda.memcpy_htod(gx, x)
+    gout = ffn.forward(gx, 1, M)
+    out = np.empty((M, C), np.float32)
+    cuda.memcpy_dtoh(out, gout)
+    pre = np.empty((M, 4 * C), np.float32)
+    cuda.memcpy_dtoh(pre, ffn.cache_pre_act)
+    act = np.empty((M, 4 * C), np.float32)
+    cuda.memcpy_dtoh(act, ffn.cache_activated)
+    dout = out.copy() if dout_seed is None else \
+        np.random.RandomState(dout_seed).normal(0.0, 1.0, size=(M, C)).astype(np.float32)
+    gd = cuda.mem_alloc(dout.nbytes)
+    cuda.memcpy_htod(gd, dout)
+    ffn.use_cpu_backward = True
+    gdin = ffn.backward(gd, 1, M, accumulate=False)
+    din = np.empty((M, C), np.float32)
+    cuda.memcpy_dtoh(din, gdin)
+
+    def dl(p, which):
+        h = np.empty(p.shape, np.float32)
+        cuda.memcpy_dtoh(h, getattr(p, which))
+        return h
+
+    return dict(x=x, dy=dout, out=out, pre=pre, act=act, din=din,
+                w_fc=dl(ffn.c_fc_w, "gpu_weights"), b_fc=dl(ffn.c_fc_b, "gpu_weights"),
+                w_proj=dl(ffn.c_proj_w, "gpu_weights"), b_proj=dl(ffn.c_proj_b, "gpu_weights"),
+                d_fc_w=dl(ffn.c_fc_w, "gpu_grads"), d_fc_b=dl(ffn.c_fc_b, "gpu_grads"),
+                d_proj_w=dl(ffn.c_proj_w, "gpu_grads"), d_proj_b=dl(ffn.c_proj_b, "gpu_grads"), C=C, M=M)
+
+
 def main(ref_root):
     ref_root = os.path.abspath(ref_root)
     state = {}
@@ -265,6 +316,11 @@ def main(ref_root):
             res = _run_reference_mha(gpt, cuda, B, T, C, NH, 5000 + s, 6000 + s)
             res.pop("cache_attn_weights")  # T×T; the oracle rebuilds it, keep fixtures small
             np.savez_compressed(os.path.join(HERE, f"mha_b{B}_t{T}_c{C}_nh{NH}.npz"), **res)
+
+        # FeedForward: test_ffn_gpu_backward.py's scenario, then a wider one with biases
+        np.savez(os.path.join(HERE, "ffn_c16_m6.npz"), **_run_reference_ffn(gpt, cuda, 16, 6, 1337))
+        np.savez_compressed(os.path.join(HERE, "ffn_c64_m40.npz"),
+                            **_run_reference_ffn(gpt, cuda, 64, 40, 2024, dout_seed=2025, bias_scale=0.5))
     finally:
         os.chdir(cwd)
     print("golden fixtures written to", HERE)

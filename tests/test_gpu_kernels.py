@@ -309,3 +309,76 @@ def test_gemm_tc_unaligned_output_pitch(pkg, cuda_dev, M, N, K, at, bt, pad):
         assert O.rel_err(got[:, :N], ref + (C0[:, :N] if acc else 0)) < 1e-3
         np.testing.assert_array_equal(got[:, N:], C0[:, N:])  # padding columns untouched
     assert pkg.lib.attn_device_error(1) == 0
+
+
+@pytest.mark.parametrize("dtype,M,N,K,at,bt,pad", [
+    ("bf16", 300, 3072, 768, False, False, 0),   # FFN c_fc shape: tensor cores, 12 column tiles
+    ("bf16", 1000, 200, 64, False, True, 0),     # ragged N: partial 64-column chunks
+    ("bf16", 130, 1024, 256, True, False, 0),    # MN-major A
+    ("bf16", 256, 512, 128, False, False, 1),    # unaligned output pitch: CUDA-core epilogue
+    ("f32", 77, 96, 40, False, False, 0),
+    ("f32", 64, 256, 128, False, True, 0),
+])
+def test_gemm_act_gelu_matches_oracle(pkg, cuda_dev, dtype, M, N, K, at, bt, pad):
+    """The feed-forward epilogues of attn_gemm_act: ATTN_ACT_GELU (activation plus the cached
+    pre-activation, with and without the cache) and ATTN_ACT_GELU_BWD, against the oracle's
+    tanh-GELU (activation_kernel / gelu_backward_kernel, core/kernels.py:237-250, :424-447)."""
+    torch = _torch()
+    ops = pkg.mha_ops
+    rng = np.random.default_rng(M * 3 + N + K)
+    A = rng.standard_normal((K, M) if at else (M, K)).astype(np.float32) / np.sqrt(K) * 2
+    Bm = rng.standard_normal((N, K) if bt else (K, N)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    if dtype == "bf16":
+        A, Bm = _bf16_round(A), _bf16_round(Bm)
+    tA, tB, tbias = _dev(A, tdt), _dev(Bm, tdt), _dev(bias)
+    acc = (A.T if at else A).astype(np.float64) @ (Bm.T if bt else Bm).astype(np.float64)
+    tol = F32_TOL if dtype == "f32" else 1e-2
+    ld = N + pad
+    for c_dt in ((tdt, torch.float32) if dtype == "bf16" else (tdt,)):
+        # forward: act = gelu(acc + bias), pre = acc + bias
+        act = torch.full((M, ld), 7.0, dtype=c_dt, device="cuda")
+        pre = torch.full((M, ld), 7.0, dtype=c_dt, device="cuda")
+        ops.gemm_act(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, tdt, act.data_ptr(), ld, c_dt,
+                     M, N, K, ops.ATTN_ACT_GELU, aux=pre.data_ptr(), ldaux=ld, aux_dtype=c_dt, bias=tbias.data_ptr())
+        torch.cuda.synchronize()
+        want_pre = acc + bias
+        assert O.rel_err(pre.float().cpu().numpy()[:, :N], want_pre) < tol
+        assert O.rel_err(act.float().cpu().numpy()[:, :N], O.gelu(want_pre)) < tol
+        if pad:
+            assert (act.float().cpu().numpy()[:, N:] == 7.0).all() and (pre.float().cpu().numpy()[:, N:] == 7.0).all()
+        act2 = torch.empty((M, ld), dtype=c_dt, device="cuda")  # inference: no pre-activation cache
+        ops.gemm_act(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, tdt, act2.data_ptr(), ld, c_dt,
+                     M, N, K, ops.ATTN_ACT_GELU, bias=tbias.data_ptr())
+        torch.cuda.synchronize()
+        assert torch.equal(act2[:, :N], act[:, :N])
+        # backward: d = acc * gelu'(aux), aux a cached pre-activation in either dtype
+        for aux_dt in (torch.float32, tdt):
+            aux = (rng.standard_normal((M, ld)) * 1.5).astype(np.float32)
+            if aux_dt == torch.bfloat16:
+                aux = _bf16_round(aux)
+            taux = _dev(aux, aux_dt)
+            d = torch.full((M, ld), 7.0, dtype=c_dt, device="cuda")
+            ops.gemm_act(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, tdt, d.data_ptr(), ld, c_dt,
+                         M, N, K, ops.ATTN_ACT_GELU_BWD, aux=taux.data_ptr(), ldaux=ld, aux_dtype=aux_dt)
+            torch.cuda.synchronize()
+            assert O.rel_err(d.float().cpu().numpy()[:, :N], acc * O.gelu_grad(aux[:, :N])) < tol, (c_dt, aux_dt)
+    assert pkg.lib.attn_device_error(1) == 0
+
+
+def test_gemm_act_rejects_bad_arguments(pkg, cuda_dev):
+    torch = _torch()
+    ops = pkg.mha_ops
+    a = torch.zeros((64, 64), dtype=torch.bfloat16, device="cuda")
+    c = torch.zeros((64, 64), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(pkg.AttnError):  # GELU_BWD without its pre-activation
+        ops.gemm_act(a.data_ptr(), 64, False, a.data_ptr(), 64, False, torch.bfloat16, c.data_ptr(), 64,
+                     torch.bfloat16, 64, 64, 64, ops.ATTN_ACT_GELU_BWD)
+    with pytest.raises(pkg.AttnError):  # unknown activation
+        ops.gemm_act(a.data_ptr(), 64, False, a.data_ptr(), 64, False, torch.bfloat16, c.data_ptr(), 64,
+                     torch.bfloat16, 64, 64, 64, 9)
+    with pytest.raises(pkg.AttnError):  # aux aliasing the output
+        ops.gemm_act(a.data_ptr(), 64, False, a.data_ptr(), 64, False, torch.bfloat16, c.data_ptr(), 64,
+                     torch.bfloat16, 64, 64, 64, ops.ATTN_ACT_GELU, aux=c.data_ptr(), ldaux=64,
+                     aux_dtype=torch.bfloat16)

@@ -97,3 +97,17 @@ def test_rel_err_catches_planted_mistake():
     bad[1, 16, 3] += 1e-3 * np.abs(out).max()
     assert O.rel_err(bad, g["out"]) > 1e-5
     assert O.rel_err(out, g["out"]) < 1e-6
+
+
+@pytest.mark.parametrize("name", ["ffn_c16_m6", "ffn_c64_m40"])
+def test_ffn_oracle_matches_reference_feedforward(name):
+    """The FFN restatement against model/gpt.py's FeedForward run with its NumPy backward; the
+    reference's own parity tolerance (test_ffn_gpu_backward.py:25)."""
+    g = np.load(os.path.join(GOLDEN, name + ".npz"))
+    out, cache = O.ffn_forward(g["x"], g["w_fc"], g["b_fc"], g["w_proj"], g["b_proj"])
+    np.testing.assert_allclose(cache["pre"], g["pre"], **TOL)
+    np.testing.assert_allclose(cache["act"], g["act"], **TOL)
+    np.testing.assert_allclose(out, g["out"], **TOL)
+    d_in, dfw, dfb, dpw, dpb = O.ffn_backward(cache, g["dy"], g["w_fc"], g["w_proj"])
+    for got, key in ((d_in, "din"), (dfw, "d_fc_w"), (dfb, "d_fc_b"), (dpw, "d_proj_w"), (dpb, "d_proj_b")):
+        np.testing.assert_allclose(got, g[key], **TOL, err_msg=key)
