@@ -559,14 +559,16 @@ def run_decode(args, cfg):
 
 # ------------------------------------------------------------------------------ fused half-block
 def run_residual(args, cfg):
-    """x += attn(ln_1(x)), the pre-attention half of TransformerBlock.forward (model/gpt.py:778-783),
-    timed two ways on the same inputs: the reference's sequence with this library's kernels
-    (LayerNorm to float32, MultiHeadAttention.forward, residual add) and forward_residual (the
-    LayerNorm writes the QKV operand, the output projection adds into x).  Forward only."""
+    """x += attn(ln_1(x)), the pre-attention half of TransformerBlock (model/gpt.py:778-783 forward,
+    :823-838 backward), timed two ways on the same inputs: the reference's sequence with this
+    library's kernels (LayerNorm to float32, MultiHeadAttention.forward, residual add; backward:
+    attn.backward, the LayerNorm backward to its own buffer, the residual add) and the fused
+    forward_residual / backward_residual.  Forward alone (inference) and forward + backward."""
     import numpy as np
     import torch
     import importlib
     pkg = importlib.import_module("llm-gpu-5_b200")
+    ops = pkg.mha_ops
     w = WORKLOADS[cfg]
     B = args.batch or w["global_batch"]
     T, C, NH = w["T"], w["C"], w["NH"]
@@ -574,43 +576,178 @@ def run_residual(args, cfg):
     np.random.seed(1000 + cfg)
     attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
                                                 attention_precision=w["prec"]))
-    attn.training = False
     gen = torch.Generator(device="cuda")
     gen.manual_seed(1000 + cfg)
     x0 = torch.randn((M, C), generator=gen, device="cuda")
+    dy0 = torch.randn((M, C), generator=gen, device="cuda")
     gamma = 1 + 0.1 * torch.randn(C, generator=gen, device="cuda")
     beta = 0.1 * torch.randn(C, generator=gen, device="cuda")
-    x = x0.clone()
+    dgamma, dbeta = torch.zeros(C, device="cuda"), torch.zeros(C, device="cuda")
+    x, dy = x0.clone(), dy0.clone()
 
-    def unfused():
-        ln = pkg.mha_ops.layernorm(x, gamma, beta)
+    def unfused_fwd():
+        ln = ops.layernorm(x, gamma, beta)
         out = attn.forward(ln, B, T)
         x.add_(out.tensor)
         out.free()
 
-    def fused():
+    def fused_fwd():
         attn.forward_residual(x, B, T, gamma, beta)
 
+    def unfused_step():
+        x_in = x.clone()  # cache_input_ln1 (model/gpt.py:773-775)
+        unfused_fwd()
+        dln = attn.backward(dy, B, T)
+        dxn = torch.empty_like(x)
+        ops.layernorm_backward(dln.tensor.view(M, C), x_in, gamma, dxn, dgamma, dbeta)
+        dx0 = dy.clone()  # dX0 = dX1 + dLN (model/gpt.py:833-835)
+        dx0.add_(dxn)
+        dln.free()
+
+    def fused_step():
+        attn.forward_residual(x, B, T, gamma, beta)
+        attn.backward_residual(dy, B, T, gamma, dgamma, dbeta)
+
     res = {}
-    for name, fn in (("unfused", unfused), ("fused", fused)):
+    for name, fn, training in (("unfused_fwd", unfused_fwd, False), ("fused_fwd", fused_fwd, False),
+                               ("unfused_fwd_bwd", unfused_step, True), ("fused_fwd_bwd", fused_step, True)):
+        attn.training = training
         for _ in range(max(args.warmup, 3)):
             x.copy_(x0)
+            dy.copy_(dy0)
             fn()
         torch.cuda.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         total = 0.0
-        for _ in range(args.steps):  # x is reset outside the timed spans
+        for _ in range(args.steps):  # x and dY are reset outside the timed spans
             x.copy_(x0)
+            dy.copy_(dy0)
             t0.record()
             fn()
             t1.record()
             torch.cuda.synchronize()
             total += t0.elapsed_time(t1)
         res[name] = total / args.steps
-    print(json.dumps(dict(metric="pre-attention half-block forward tokens/sec", value=M / (res["fused"] * 1e-3),
-                          unit="tokens/s", fused_ms=res["fused"], unfused_ms=res["unfused"],
-                          speedup=res["unfused"] / res["fused"], dtype="bf16" if w["prec"] == "bf16" else "f32",
+    print(json.dumps(dict(metric="pre-attention half-block fwd+bwd tokens/sec",
+                          value=M / (res["fused_fwd_bwd"] * 1e-3), unit="tokens/s",
+                          ms=res, speedup_fwd=res["unfused_fwd"] / res["fused_fwd"],
+                          speedup_fwd_bwd=res["unfused_fwd_bwd"] / res["fused_fwd_bwd"],
+                          dtype="bf16" if w["prec"] == "bf16" else "f32",
                           data="synthetic", config=dict(workload=w["name"], tokens=M))), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ feed-forward block
+def ffn_op_flops(op, M, C):
+    H = 4 * C
+    return 2 * M * C * H if op in ("gemm_fc_gelu", "gemm_proj", "gemm_dwproj", "gemm_dhidden_gelu", "gemm_dwfc",
+                                   "gemm_dx") else None
+
+
+def run_ffn(args, cfg):
+    """FeedForward forward + backward (model/gpt.py:327-456) at the workload's token count and
+    d_model (hidden 4 x d_model), bf16 operands / fp32 accumulation: six tcgen05 GEMMs, GELU and its
+    derivative in their epilogues.  Prints one JSON line with per-op times and TFLOP/s against the
+    measured bf16 peak, and, for context, the same computation as cuBLAS GEMMs plus PyTorch's
+    tanh-GELU kernels (torch.matmul, F.gelu, aten.gelu_backward, column sums)."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+    import importlib
+    pkg = importlib.import_module("llm-gpu-5_b200")
+    w = WORKLOADS[cfg]
+    B = args.batch or w["global_batch"]
+    T, C = w["T"], w["C"]
+    M, H = B * T, 4 * w["C"]
+    steps, warmup = args.steps, max(args.warmup, 3)
+    np.random.seed(1000 + cfg)
+    ffn = pkg.FeedForward(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=w["NH"], max_len=T,
+                                        attention_precision=w["prec"]))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2000 + cfg)
+    for p in (ffn.c_fc_b, ffn.c_proj_b):
+        p.weights.copy_(0.1 * torch.randn(p.shape, generator=gen, device="cuda"))
+    x = torch.randn((M, C), generator=gen, device="cuda")
+    dy = torch.randn((M, C), generator=gen, device="cuda")
+
+    def step():
+        out = ffn.forward(x, B, T)
+        din = ffn.backward(dy, B, T)
+        out.free()
+        din.free()
+
+    for _ in range(warmup):
+        step()
+    prof = EventProfiler()
+    ffn.profiler = prof
+    step()
+    prof.spans.clear()
+    clocks = ClockSampler(0)
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = pkg.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = pkg.launch_count() - launches0
+    ms = t0.elapsed_time(t1) / steps
+    ffn.profiler = None
+    totals = prof.totals()
+    peaks, src = load_peaks()
+    peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    per_op = {}
+    for k, (t, n) in totals.items():
+        d = dict(ms_per_step=t / steps, launches_per_step=n / steps)
+        f = ffn_op_flops(k, M, C)
+        if f:
+            d["tflops"] = f / (t / n * 1e-3) / 1e12
+        per_op[k] = d
+    gemm_flops = 12 * M * C * H
+    gemm_ms = sum(totals[k][0] for k in totals if ffn_op_flops(k, M, C)) / steps
+    dom = max((k for k in totals if ffn_op_flops(k, M, C)), key=lambda k: totals[k][0])
+    dom_ach = ffn_op_flops(dom, M, C) / (totals[dom][0] / totals[dom][1] * 1e-3) / 1e12
+
+    # the same math on NVIDIA's libraries (bf16 everywhere; context only)
+    xb, dyb = x.bfloat16(), dy.bfloat16()
+    wfc, wpr = ffn.c_fc_w.weights.bfloat16(), ffn.c_proj_w.weights.bfloat16()
+    bfc, bpr = ffn.c_fc_b.weights.bfloat16(), ffn.c_proj_b.weights.bfloat16()
+
+    def vendor_step():
+        pre = torch.addmm(bfc, xb, wfc)
+        act = F.gelu(pre, approximate="tanh")
+        torch.addmm(bpr, act, wpr)
+        act.t() @ dyb
+        dyb.sum(0)
+        dpre = torch.ops.aten.gelu_backward(dyb @ wpr.t(), pre, approximate="tanh")
+        xb.t() @ dpre
+        dpre.sum(0)
+        dpre @ wfc.t()
+
+    for _ in range(warmup):
+        vendor_step()
+    torch.cuda.synchronize()
+    v0, v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    v0.record()
+    for _ in range(steps):
+        vendor_step()
+    v1.record()
+    torch.cuda.synchronize()
+    vendor_ms = v0.elapsed_time(v1) / steps
+    print(json.dumps(dict(
+        metric="feed-forward fwd+bwd tokens/sec", value=M / (ms * 1e-3), unit="tokens/s", n_gpus=1, steps=steps,
+        warmup=warmup, ms_per_step=ms, higher_is_better=True, dtype="bf16" if w["prec"] == "bf16" else "f32",
+        data="synthetic",
+        config=dict(workload=f"FeedForward fwd+bwd, {M} tokens (B={B} T={T}), C={C} -> {H} -> {C}, tanh-GELU",
+                    tokens=M, d_model=C, hidden=H, l2="inputs larger than L2 (no flush)"),
+        roofline=dict(bound="tensor", kernel=dom, achieved=dom_ach, peak=peak, unit="TFLOP/s", frac=dom_ach / peak,
+                      peak_source=f"{src} bf16_tflops_sustained"),
+        gemm_tflops=gemm_flops / (gemm_ms * 1e-3) / 1e12, step_tflops=gemm_flops / (ms * 1e-3) / 1e12,
+        breakdown=per_op, gpu_launches=launches, clocks=clk,
+        vendor=dict(cublas_plus_torch_gelu_ms=vendor_ms, speedup=vendor_ms / ms))), flush=True)
     return 0
 
 
@@ -677,6 +814,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--residual", action="store_true",
                     help="time x += attn(ln_1(x)) fused (forward_residual) against the unfused block sequence")
+    ap.add_argument("--ffn", action="store_true",
+                    help="time FeedForward fwd+bwd (C -> 4C -> C) at the workload's token count and d_model")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the global batch (small cases for profiler captures only)")
     args = ap.parse_args()
@@ -688,6 +827,8 @@ def main():
         return run_decode(args, args.config)
     if args.residual:
         return run_residual(args, args.config)
+    if args.ffn:
+        return run_ffn(args, args.config)
     return run_ours(args, args.config)
 
 

@@ -78,7 +78,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 static bool make_tmap(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int rank,
-                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is unavailable");
@@ -93,7 +93,8 @@ static bool make_tmap(CUtensorMap* map, CUtensorMapDataType dt, const void* base
     if (i < rank - 1) st[i] = strides_bytes[i];
   }
   CUresult r = fn(map, dt, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d): rank %d dims %llu x %llu", (int)r, rank,
@@ -104,13 +105,13 @@ static bool make_tmap(CUtensorMap* map, CUtensorMapDataType dt, const void* base
 }
 
 bool make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box) {
-  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides_bytes, box);
+                    const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
+  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides_bytes, box, swizzle_bytes);
 }
 
 bool make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                   const uint64_t* strides_bytes, const uint32_t* box) {
-  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, rank, dims, strides_bytes, box);
+                   const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
+  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, rank, dims, strides_bytes, box, swizzle_bytes);
 }
 
 static int sm_count() {

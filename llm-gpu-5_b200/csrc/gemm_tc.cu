@@ -8,9 +8,14 @@
 //   warp 0      TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 4-stage ring
 //   warp 1      TMEM allocation and the single MMA-issuing thread: 4 x tcgen05.mma (128x256x16)
 //               per 64-deep K block, accumulating in TMEM
-//   warps 2-5   epilogue: tcgen05.ld of the 128x256 fp32 accumulator (one row per thread), bias,
-//               conversion, then 128-byte-wide column chunks staged in swizzled shared memory and
-//               written by TMA stores (or TMA reduce-adds when accumulating into C)
+//   warps 2..   epilogue, groups of four warps (one warp per TMEM lane quarter in each), each group
+//               owning a column span of the tile: tcgen05.ld of the fp32 accumulator (one row per
+//               thread), bias, activation, conversion, then column chunks staged in swizzled shared
+//               memory (two buffers per group) and written by TMA stores (or TMA reduce-adds when
+//               accumulating into C).  Two shapes, a template parameter: four epilogue warps with
+//               128-byte chunk rows (the default), or eight warps in two groups of 128 columns with
+//               64-byte chunk rows, which doubles the epilogue's issue slots and memory parallelism
+//               for ACT_GELU_BWD (its epilogue reads a second operand).
 // The accumulator is double-buffered in TMEM (2 x 256 columns) so the epilogue of one tile
 // overlaps the main loop of the next.  Either operand may be K-major or MN-major (the transposed
 // operands of the weight gradients); TMA writes both in the canonical 128B-swizzled layouts.
@@ -24,20 +29,34 @@
 // activation_kernel + the cache_pre_act copy, model/gpt.py:345-361); ACT_GELU_BWD multiplies the
 // accumulator by gelu'(aux[m, n]) (dHidden = dOut W^T followed by gelu_backward_kernel,
 // model/gpt.py:437-438).  Activations run without K splits and without accumulation.
-#include "tc_common.cuh"
+#include "attn_tc_common.cuh"
 
 #include <string.h>
 
 namespace attn {
 
 constexpr int GT_BM = 128, GT_BN = 256, GT_BK = 64, GT_STAGES = 4;
-constexpr int GT_THREADS = 192;
 constexpr int GT_A_BYTES = GT_BM * GT_BK * 2;  // 16 KB
 constexpr int GT_B_BYTES = GT_BN * GT_BK * 2;  // 32 KB
 constexpr int GT_STAGE_BYTES = GT_A_BYTES + GT_B_BYTES;
-constexpr int GT_EPI_BYTES = GT_BM * 128;      // one 128-row x 128-byte output chunk (16 KB)
-constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + 2 * GT_EPI_BYTES + GT_BN * 4 /*bias*/ + 1024 + 256;
+constexpr int GT_EPI_STAGING = 32 * 1024;      // output staging: two buffers per epilogue group
+constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + GT_EPI_STAGING + GT_BN * 4 /*bias*/ + 1024 + 256;
+
+// Epilogue shape for EW epilogue warps (4 or 8).
+template <int EW>
+struct Epi {
+  static constexpr int threads = 32 * EW;             // epilogue threads
+  static constexpr int kthreads = 64 + threads;       // whole CTA
+  static constexpr int groups = EW / 4;
+  static constexpr int span = GT_BN / groups;         // tile columns per group
+  static constexpr int row_bytes = EW == 8 ? 64 : 128;  // one chunk row: 16/32 fp32 or 32/64 bf16 columns
+  static constexpr int vecs = row_bytes / 16;         // 16-byte pieces per chunk row
+  static constexpr int words = row_bytes / 4;         // 32-bit words per chunk row
+  static constexpr int buf_bytes = GT_BM * row_bytes;
+  static_assert(groups * 2 * buf_bytes == GT_EPI_STAGING, "staging layout");
+};
 constexpr uint32_t GT_TMEM_COLS = 512;
+static_assert(GT_SMEM <= 227 * 1024, "GEMM shared memory exceeds the per-CTA limit");
 
 struct GemmParams {
   int M, N, K;
@@ -56,45 +75,44 @@ struct GemmParams {
   int* err;
 };
 
-// The aux operand of ACT_GELU_BWD for one accumulator row: columns n0 .. n0+cols-1 as floats
-// (columns past N read as 0).  A thread reads its own row (a whole 128-byte line or two).
-__device__ __forceinline__ void load_aux_row(const GemmParams& p, int64_t m, int n0, int cols, float (&a)[64]) {
-  const bool full = n0 + cols <= p.N;
-  if (p.aux_bf16) {
-    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.aux) + m * p.ldaux + n0;
-    if (full) {
+// The aux operand of ACT_GELU_BWD (C's dtype) for one accumulator row and one 64-byte output chunk
+// starting at column n0, as raw words (columns past N read as 0; rows past M are not read).  The
+// thread reads its own row: one 64-byte piece of a line, issued a chunk ahead of its use.
+template <int V>
+__device__ __forceinline__ void fetch_aux_chunk(const GemmParams& p, int64_t m, int n0, uint4 (&dst)[V]) {
+  constexpr int W = 4 * V;  // words per chunk row
+  const int cols = p.c_bf16 ? 2 * W : W;
+  if (m >= p.M || n0 >= p.N) return;
+  const int esz = p.c_bf16 ? 2 : 4;
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(p.aux) + (m * p.ldaux + n0) * esz;
+  if (n0 + cols <= p.N) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (8 * i < cols) {
-          const uint4 u = reinterpret_cast<const uint4*>(src)[i];
-          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    for (int j = 0; j < V; ++j) dst[j] = __ldg(reinterpret_cast<const uint4*>(src) + j);
+    return;
+  }
+  uint32_t t[W];
+  if (p.c_bf16) {
+    const unsigned short* s16 = reinterpret_cast<const unsigned short*>(src);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
-            a[8 * i + 2 * j] = f.x;
-            a[8 * i + 2 * j + 1] = f.y;
-          }
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 64; ++i) a[i] = i < cols && n0 + i < p.N ? __bfloat162float(src[i]) : 0.f;
+    for (int i = 0; i < W; ++i) {
+      const uint32_t lo = n0 + 2 * i < p.N ? s16[2 * i] : 0u;
+      const uint32_t hi = n0 + 2 * i + 1 < p.N ? s16[2 * i + 1] : 0u;
+      t[i] = lo | (hi << 16);
     }
   } else {
-    const float* src = reinterpret_cast<const float*>(p.aux) + m * p.ldaux + n0;
-    if (full) {
+    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if (4 * i < cols) {
-          const float4 f = reinterpret_cast<const float4*>(src)[i];
-          a[4 * i] = f.x; a[4 * i + 1] = f.y; a[4 * i + 2] = f.z; a[4 * i + 3] = f.w;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 64; ++i) a[i] = i < cols && n0 + i < p.N ? src[i] : 0.f;
-    }
+    for (int i = 0; i < W; ++i) t[i] = n0 + i < p.N ? s32[i] : 0u;
   }
+#pragma unroll
+  for (int j = 0; j < V; ++j) dst[j] = make_uint4(t[4 * j], t[4 * j + 1], t[4 * j + 2], t[4 * j + 3]);
+}
+
+// Word w of a raw aux chunk (w a compile-time index after unrolling).
+template <int V>
+__device__ __forceinline__ uint32_t aux_word(const uint4 (&raw)[V], int w) {
+  const uint4 q = raw[w >> 2];
+  return (w & 3) == 0 ? q.x : (w & 3) == 1 ? q.y : (w & 3) == 2 ? q.z : q.w;
 }
 
 __device__ __forceinline__ void unit_coords(const GemmParams& p, int unit, int& tm, int& tn, int& kb0,
@@ -106,65 +124,40 @@ __device__ __forceinline__ void unit_coords(const GemmParams& p, int unit, int& 
   kb1 = min(p.kb_total, kb0 + p.kb_per_split);
 }
 
-__device__ __forceinline__ void epilogue_store32(const GemmParams& p, int m, int n0, const uint32_t (&r)[32],
-                                                 bool add_bias) {
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-  if (add_bias && p.bias) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (n0 + i < p.N) v[i] += __ldg(p.bias + n0 + i);
-  }
-  const bool full = n0 + 32 <= p.N;
+// Direct per-row stores of one chunk (C without a 16-byte row pitch): cols values of row m from
+// column n0, bias already added; fp32 atomics for K splits, read-add-write when accumulating.
+template <int NV>
+__device__ __forceinline__ void store_chunk_direct(const GemmParams& p, int64_t m, int n0, const float (&v)[NV],
+                                                   int cols) {
   if (p.c_bf16) {
-    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)m * p.ldc + n0;
-    if (full && p.vec_ok) {
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + m * p.ldc + n0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint4 u;
-        u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
-        u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
-        u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
-        u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
-        reinterpret_cast<uint4*>(c)[i] = u;
-      }
-    } else {
-      for (int i = 0; i < 32; ++i)
-        if (n0 + i < p.N) c[i] = __float2bfloat16_rn(v[i]);
-    }
+    for (int i = 0; i < NV; ++i)
+      if (i < cols && n0 + i < p.N) c[i] = __float2bfloat16_rn(v[i]);
     return;
   }
-  float* c = reinterpret_cast<float*>(p.C) + (int64_t)m * p.ldc + n0;
-  if (p.atomic) {
-    for (int i = 0; i < 32; ++i)
-      if (n0 + i < p.N) atomicAdd(c + i, v[i]);
-    return;
-  }
-  if (full && p.vec_ok) {
+  float* c = reinterpret_cast<float*>(p.C) + m * p.ldc + n0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      if (p.accumulate) {
-        const float4 e = reinterpret_cast<const float4*>(c)[i];
-        o.x += e.x; o.y += e.y; o.z += e.z; o.w += e.w;
-      }
-      reinterpret_cast<float4*>(c)[i] = o;
+  for (int i = 0; i < NV; ++i) {
+    if (i < cols && n0 + i < p.N) {
+      if (p.atomic)
+        atomicAdd(c + i, v[i]);
+      else
+        c[i] = p.accumulate ? c[i] + v[i] : v[i];
     }
-  } else {
-    for (int i = 0; i < 32; ++i)
-      if (n0 + i < p.N) c[i] = p.accumulate ? c[i] + v[i] : v[i];
   }
 }
 
-__global__ void __launch_bounds__(GT_THREADS, 1)
+template <int EW>
+__global__ void __launch_bounds__(Epi<EW>::kthreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux,
                const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi = smem + GT_STAGES * GT_STAGE_BYTES;  // [2] output staging chunks
-  float* s_bias = reinterpret_cast<float*>(epi + 2 * GT_EPI_BYTES);  // the tile's bias columns
+  using E = Epi<EW>;
+  uint8_t* epi = smem + GT_STAGES * GT_STAGE_BYTES;  // output staging buffers, two per epilogue group
+  float* s_bias = reinterpret_cast<float*>(epi + GT_EPI_STAGING);  // the tile's bias columns
   uint64_t* full = reinterpret_cast<uint64_t*>(s_bias + GT_BN);
   uint64_t* empty = full + GT_STAGES;
   uint64_t* tfull = empty + GT_STAGES;
@@ -179,7 +172,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], E::threads);
     }
     fence_mbar_init();
   }
@@ -266,46 +259,60 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (ok) umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
       }
     }
-  } else if (p.tma_epi) {
-    // Epilogue through shared memory: each thread owns one accumulator row; a chunk of 128 bytes
-    // per row (32 fp32 or 64 bf16 columns) goes to a 128B-swizzled staging buffer (conflict-free
-    // 16-byte stores) and one thread writes the 128-row chunk with a TMA store, or a TMA
-    // reduce-add when accumulating or splitting K.  Two staging buffers alternate.
-    const int q = warp & 3;
+  } else {
+    // Epilogue: each thread owns one accumulator row of its group's column span.  A chunk of
+    // E::row_bytes per row goes to a swizzled staging buffer (conflict-free 16-byte stores; the
+    // 128B or 64B swizzle of C's tensor map) and the group's leader writes the 128-row chunk with
+    // a TMA store, or a TMA reduce-add when accumulating or splitting K.  Each group alternates two
+    // staging buffers and synchronises on its own named barrier.  Without a 16-byte row pitch (no
+    // TMA map for C) the threads store their rows directly instead.
+    constexpr int V = E::vecs, W = E::words;
+    const int ew = warp - 2;
+    const int h = ew >> 2;                 // the group: tile columns h * E::span ..
+    const int q = warp & 3;                // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
-    const bool leader = (warp == 2 && lane == 0);
-    const int cols = p.c_bf16 ? 64 : 32;  // columns per 128-byte chunk
+    const int bar = 1 + h;
+    const bool leader = (ew & 3) == 0 && lane == 0;
+    const int cols = p.c_bf16 ? 2 * W : W;  // columns per chunk
+    const int nchunks = E::span / cols;
+    const bool bwd = p.act == ACT_GELU_BWD;
+    const int sw = E::row_bytes == 128 ? (row & 7) : ((row >> 1) & 3);  // swizzle of this row's pieces
+    uint8_t* gepi = epi + 2 * h * E::buf_bytes;
+    float* gbias = s_bias + h * E::span;
     int buf = 0;
-    // stage 32 packed words per thread (one 128-byte chunk row) and write the 128-row chunk at
-    // column n0 through `map`; two staging buffers alternate
-    auto emit = [&](const CUtensorMap* map, const uint32_t (&w)[32], int n0, int m0, bool reduce) {
+    auto emit = [&](const CUtensorMap* map, const uint32_t (&w)[W], int n0, int m0, bool reduce) {
       if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
-      named_bar_sync(1, 128);
-      uint8_t* rowp = epi + buf * GT_EPI_BYTES + row * 128;
+      named_bar_sync(bar, 128);
+      uint8_t* rowp = gepi + buf * E::buf_bytes + row * E::row_bytes;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) << 4)) =
-            make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
+      for (int j = 0; j < V; ++j)
+        *reinterpret_cast<uint4*>(rowp + ((j ^ sw) << 4)) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
       fence_proxy_async_smem();
-      named_bar_sync(1, 128);
+      named_bar_sync(bar, 128);
       if (leader) {
         if (reduce)
-          tma_reduce_add_2d(map, epi + buf * GT_EPI_BYTES, n0, m0);
+          tma_reduce_add_2d(map, gepi + buf * E::buf_bytes, n0, m0);
         else
-          tma_store_2d(map, epi + buf * GT_EPI_BYTES, n0, m0);
+          tma_store_2d(map, gepi + buf * E::buf_bytes, n0, m0);
         bulk_commit();
       }
       buf ^= 1;
     };
-    auto pack = [&](const float (&v)[64], uint32_t (&w)[32]) {
+    auto pack = [&](const float (&v)[2 * W], uint32_t (&w)[W]) {
       if (p.c_bf16) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+        for (int i = 0; i < W; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+        for (int i = 0; i < W; ++i) w[i] = __float_as_uint(v[i]);
       }
     };
+    uint4 pf[V] = {};  // ACT_GELU_BWD: the aux chunk of the next (tile, chunk), fetched a chunk ahead
+    if (bwd && (int)blockIdx.x < p.units) {
+      int tm, tn, kb0, kb1;
+      unit_coords(p, blockIdx.x, tm, tn, kb0, kb1);
+      fetch_aux_chunk<V>(p, (int64_t)tm * GT_BM + row, tn * GT_BN + h * E::span, pf);
+    }
     int local = 0;
     for (int unit = blockIdx.x; unit < p.units; unit += gridDim.x, ++local) {
       int tm, tn, kb0, kb1;
@@ -315,40 +322,59 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, p.err, 104));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * GT_BN;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * GT_BN + h * E::span;
+      const int64_t m = (int64_t)tm * GT_BM + row;
       const bool add_bias = p.bias && kb0 == 0;
-      if (add_bias) {  // the tile's 256 bias values, read once into shared memory
-        // (every thread has passed the previous tile's last read of s_bias: it precedes that
-        // chunk's first barrier)
+      if (add_bias) {  // the group's bias values, read once into shared memory (every thread of the
+        // group has passed the barriers that follow its last read of the previous tile's)
 #pragma unroll
-        for (int i = 0; i < GT_BN / 128; ++i) {
-          const int n = tn * GT_BN + row + 128 * i;
-          s_bias[row + 128 * i] = n < p.N ? __ldg(p.bias + n) : 0.f;
+        for (int i = 0; i < E::span / 128; ++i) {
+          const int n = tn * GT_BN + h * E::span + row + 128 * i;
+          gbias[row + 128 * i] = n < p.N ? __ldg(p.bias + n) : 0.f;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(bar, 128);
       }
 #pragma unroll 1
-      for (int c0 = 0; c0 < GT_BN; c0 += cols) {
-        const int n0 = tn * GT_BN + c0;
-        const int64_t m = (int64_t)tm * GT_BM + row;
-        float a[64];
-        if (p.act == ACT_GELU_BWD && n0 < p.N && m < p.M) load_aux_row(p, m, n0, cols, a);  // in flight
-        uint32_t r[64];
-        tmem_ld32(taddr + c0, *reinterpret_cast<uint32_t(*)[32]>(r));
-        if (p.c_bf16) tmem_ld32(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
-        tmem_wait_ld();
-        if (c0 + cols >= GT_BN) {  // accumulator fully read: hand it back to the MMA thread
+      for (int c = 0; c < nchunks; ++c) {
+        const int n0 = tn * GT_BN + h * E::span + c * cols;
+        uint4 cur[V];
+        if (bwd) {
+#pragma unroll
+          for (int j = 0; j < V; ++j) cur[j] = pf[j];
+          if (c + 1 < nchunks) {
+            fetch_aux_chunk<V>(p, m, n0 + cols, pf);
+          } else if (unit + (int)gridDim.x < p.units) {
+            int tm2, tn2, k0, k1;
+            unit_coords(p, unit + gridDim.x, tm2, tn2, k0, k1);
+            fetch_aux_chunk<V>(p, (int64_t)tm2 * GT_BM + row, tn2 * GT_BN + h * E::span, pf);
+          }
+        }
+        uint32_t r[2 * W];
+        if (n0 < p.N) {  // uniform across the group
+          const uint32_t ta = taddr + c * cols;
+          if constexpr (W == 32) {
+            tmem_ld32(ta, *reinterpret_cast<uint32_t(*)[32]>(r));
+            if (p.c_bf16) tmem_ld32(ta + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+          } else {
+            if (p.c_bf16)
+              tmem_ld32(ta, *reinterpret_cast<uint32_t(*)[32]>(r));
+            else
+              tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tmem_wait_ld();
+        }
+        if (c + 1 == nchunks) {  // accumulator fully read: hand it back to the MMA thread
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
-        if (n0 >= p.N) continue;  // uniform across the CTA
-        float v[64];
+        if (n0 >= p.N) continue;
+        float v[2 * W];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 2 * W; ++i) v[i] = __uint_as_float(r[i]);
         if (add_bias) {  // broadcast reads; columns past N hold 0
-          const float4* b4 = reinterpret_cast<const float4*>(s_bias + c0);
+          const float4* b4 = reinterpret_cast<const float4*>(gbias + c * cols);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < 2 * W / 4; ++i) {
             if (4 * i < cols) {
               const float4 bb = b4[i];
               v[4 * i] += bb.x;
@@ -358,20 +384,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
           }
         }
-        uint32_t w[32];
+        if (!p.tma_epi) {  // activations always take the TMA path (host-checked)
+          if (m < p.M) store_chunk_direct(p, m, n0, v, cols);
+          continue;
+        }
+        uint32_t w[W];
         if (p.act == ACT_GELU) {
           if (p.aux) {  // the pre-activation, for the backward
             pack(v, w);
             emit(&tmAux, w, n0, tm * GT_BM, false);
           }
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
+          for (int i = 0; i < 2 * W; ++i)
             if (i < cols) v[i] = gelu_fwd<true>(v[i]);
-        } else if (p.act == ACT_GELU_BWD) {
-          if (m < p.M) {
+        } else if (bwd) {
+          if (p.c_bf16) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (i < cols) v[i] *= gelu_grad<true>(a[i]);
+            for (int i = 0; i < 2 * W; ++i) {
+              const uint32_t u = aux_word(cur, i >> 1);
+              v[i] *= gelu_grad<true>(__uint_as_float((i & 1) ? (u & 0xffff0000u) : (u << 16)));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < W; ++i) v[i] *= gelu_grad<true>(__uint_as_float(aux_word(cur, i)));
           }
         }
         pack(v, w);
@@ -379,31 +414,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     }
     if (leader) bulk_wait0();
-  } else {
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;
-    int local = 0;
-    for (int unit = blockIdx.x; unit < p.units; unit += gridDim.x, ++local) {
-      int tm, tn, kb0, kb1;
-      unit_coords(p, unit, tm, tn, kb0, kb1);
-      const int acc = local & 1;
-      const uint32_t acc_ph = (local >> 1) & 1;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, p.err, 104));
-      if (!ok) break;
-      tc_fence_after();
-      const int m = tm * GT_BM + row;
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * GT_BN;
-#pragma unroll 1
-      for (int c0 = 0; c0 < GT_BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c0, r);
-        tmem_wait_ld();
-        const int n0 = tn * GT_BN + c0;
-        if (m < p.M && n0 < p.N) epilogue_store32(p, m, n0, r, kb0 == 0);
-      }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -454,15 +464,14 @@ static int choose_splits(int tiles, int kb_total, int sms) {
 }
 
 // Whether the epilogue can apply `act` here: it needs the TMA epilogue (16-byte aligned C and row
-// pitch), an aux output of C's dtype for ACT_GELU, and 16-byte aligned aux rows for vector reads.
+// pitch) and an aux operand of C's dtype with 16-byte aligned rows.
 bool tc_gemm_act_ok(const void* C, int64_t ldc, int c_dtype, int act, const void* aux, int64_t ldaux,
                     int aux_dtype) {
   const int64_t cq = c_dtype == ATTN_BF16 ? 8 : 4, aq = aux_dtype == ATTN_BF16 ? 8 : 4;
   if (act == ACT_NONE) return true;
   if (!aligned(C, 16) || ldc % cq != 0) return false;
   if (!aux) return act == ACT_GELU;
-  if (act == ACT_GELU && aux_dtype != c_dtype) return false;
-  return aligned(aux, 16) && ldaux % aq == 0;
+  return aux_dtype == c_dtype && aligned(aux, 16) && ldaux % aq == 0;
 }
 
 int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans, void* C,
@@ -527,29 +536,33 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   memset(&tmAux, 0, sizeof(tmAux));
   p.tma_epi = p.vec_ok ? 1 : 0;
   p.reduce = (accumulate || p.atomic) ? 1 : 0;
+  const bool wide = act == ACT_GELU_BWD;  // eight epilogue warps, 64-byte chunk rows
+  const int row_bytes = wide ? Epi<8>::row_bytes : Epi<4>::row_bytes;
   if (p.tma_epi) {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)ldc * (p.c_bf16 ? 2 : 4)};
-    const uint32_t box[2] = {(uint32_t)(p.c_bf16 ? 64 : 32), (uint32_t)GT_BM};
-    const bool ok = p.c_bf16 ? make_tmap_bf16(&tmC, C, 2, dims, strides, box)
-                             : make_tmap_f32(&tmC, C, 2, dims, strides, box);
+    const uint32_t box[2] = {(uint32_t)(row_bytes / (p.c_bf16 ? 2 : 4)), (uint32_t)GT_BM};  // one chunk
+    const bool ok = p.c_bf16 ? make_tmap_bf16(&tmC, C, 2, dims, strides, box, row_bytes)
+                             : make_tmap_f32(&tmC, C, 2, dims, strides, box, row_bytes);
     if (!ok) return ATTN_ERR_CUDA;
     if (act == ACT_GELU && aux) {  // the pre-activation output, same geometry as C
       const uint64_t astr[1] = {(uint64_t)ldaux * (p.c_bf16 ? 2 : 4)};
-      const bool ok2 = p.c_bf16 ? make_tmap_bf16(&tmAux, aux, 2, dims, astr, box)
-                                : make_tmap_f32(&tmAux, aux, 2, dims, astr, box);
+      const bool ok2 = p.c_bf16 ? make_tmap_bf16(&tmAux, aux, 2, dims, astr, box, row_bytes)
+                                : make_tmap_f32(&tmAux, aux, 2, dims, astr, box, row_bytes);
       if (!ok2) return ATTN_ERR_CUDA;
     }
   }
   if (p.atomic && !accumulate)
     ATTN_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s));
-  static bool attr_set = false;
-  if (!attr_set) {
-    ATTN_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GT_SMEM));
-    attr_set = true;
-  }
+  static uint64_t attr4 = 0, attr8 = 0;
   const int grid = p.units < sms ? p.units : sms;
-  gemm_tc_kernel<<<grid, GT_THREADS, GT_SMEM, s>>>(tmA, tmB, tmC, tmAux, p);
+  if (wide) {
+    if (!set_smem_limit_once(gemm_tc_kernel<8>, GT_SMEM, attr8)) return ATTN_ERR_CUDA;
+    gemm_tc_kernel<8><<<grid, Epi<8>::kthreads, GT_SMEM, s>>>(tmA, tmB, tmC, tmAux, p);
+  } else {
+    if (!set_smem_limit_once(gemm_tc_kernel<4>, GT_SMEM, attr4)) return ATTN_ERR_CUDA;
+    gemm_tc_kernel<4><<<grid, Epi<4>::kthreads, GT_SMEM, s>>>(tmA, tmB, tmC, tmAux, p);
+  }
   count_launch();
   return check_launch("gemm_tc_kernel");
 }

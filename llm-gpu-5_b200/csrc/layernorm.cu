@@ -132,7 +132,8 @@ int layernorm_rows(const float* x, int64_t ldx, const float* gamma, const float*
 // dx is written, or added to dx's current contents (accumulate_dx: the residual branch of
 // TransformerBlock.backward, dX0 = dX1 + dLN, model/gpt.py:826-838, done in place).  A persistent
 // grid walks the rows one warp per row; every lane keeps the dgamma/dbeta partials of its own
-// columns in registers across rows and adds them to the outputs once at the end.
+// columns in registers across rows, the CTA's warps combine them in shared memory, and the CTA
+// adds its sums to the outputs once (2 C global atomics per CTA).
 template <int KMAX>
 __global__ void layernorm_bwd_rows_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                           const float* __restrict__ gamma, int M, int C, float eps,
@@ -142,6 +143,9 @@ __global__ void layernorm_bwd_rows_kernel(const float* __restrict__ dy, const fl
   const int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
   const int nch = C / 4;
+  __shared__ float s_pg[4 * 32 * KMAX], s_pb[4 * 32 * KMAX];
+  for (int i = threadIdx.x; i < C; i += blockDim.x) s_pg[i] = s_pb[i] = 0.f;
+  __syncthreads();
   float4 pg[KMAX], pb[KMAX];
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) pg[k] = pb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -206,11 +210,16 @@ __global__ void layernorm_bwd_rows_kernel(const float* __restrict__ dy, const fl
   for (int k = 0; k < KMAX; ++k) {
     const int c = lane + 32 * k;
     if (c < nch) {
-      atomicAdd(dgamma + 4 * c, pg[k].x); atomicAdd(dgamma + 4 * c + 1, pg[k].y);
-      atomicAdd(dgamma + 4 * c + 2, pg[k].z); atomicAdd(dgamma + 4 * c + 3, pg[k].w);
-      atomicAdd(dbeta + 4 * c, pb[k].x); atomicAdd(dbeta + 4 * c + 1, pb[k].y);
-      atomicAdd(dbeta + 4 * c + 2, pb[k].z); atomicAdd(dbeta + 4 * c + 3, pb[k].w);
+      atomicAdd(s_pg + 4 * c, pg[k].x); atomicAdd(s_pg + 4 * c + 1, pg[k].y);
+      atomicAdd(s_pg + 4 * c + 2, pg[k].z); atomicAdd(s_pg + 4 * c + 3, pg[k].w);
+      atomicAdd(s_pb + 4 * c, pb[k].x); atomicAdd(s_pb + 4 * c + 1, pb[k].y);
+      atomicAdd(s_pb + 4 * c + 2, pb[k].z); atomicAdd(s_pb + 4 * c + 3, pb[k].w);
     }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    atomicAdd(dgamma + i, s_pg[i]);
+    atomicAdd(dbeta + i, s_pb[i]);
   }
 }
 

@@ -316,13 +316,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; }
 
 // ---- host: tensor maps ---------------------------------------------------------------------------
-// Encode a 2D/3D bf16 tensor map with 128-byte swizzle.  dims/strides innermost first; strides in
-// bytes for dims 1..rank-1.  Returns false (with the error set) on failure.
+// Encode a 2D/3D/4D bf16 tensor map with a 128-byte (or, with swizzle_bytes = 64, 64-byte) swizzle.
+// dims/strides innermost first; strides in bytes for dims 1..rank-1.  Returns false (with the error
+// set) on failure.
 bool make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box);
-// Same for float32 elements (128-byte swizzle).
+                    const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes = 128);
+// Same for float32 elements.
 bool make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                   const uint64_t* strides_bytes, const uint32_t* box);
+                   const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes = 128);
 
 // Device address of the library's error word on the current device (resolved once per device).
 int* dev_error_ptr();
