@@ -193,18 +193,60 @@ class EventProfiler:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock and clock-event (throttle) reasons sampled while the timed region runs: NVML read
+    every 10 ms from a thread (read-only queries), or nvidia-smi every 200 ms where NVML is not
+    importable.  The device is matched to the CUDA device by PCI bus id."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.lines = []
+        self.samples = []
+        self.reason_bits = 0
+        self.max_mhz = None
+        self._nvml = None
+        self._stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        handle = None
+        try:
+            import torch
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            handle = None
+        if handle is None:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        return pynvml, handle
 
     def start(self):
+        try:
+            nv, h = self._nvml_handle()
+            self._nvml = (nv, h)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                        self.reason_bits |= int(nv.nvmlDeviceGetCurrentClocksThrottleReasons(h))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.01)
+            self._t = threading.Thread(target=poll, daemon=True)
+            self._t.start()
+            return
+        except Exception:
+            self._nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
@@ -220,6 +262,14 @@ class ClockSampler:
             self.lines.append(ln.strip())
 
     def stop(self):
+        if self._nvml is not None:
+            self._stop.set()
+            self._t.join(timeout=2)
+            if not self.samples:
+                return None
+            reasons = sorted(k for k, bit in self.BITS.items() if self.reason_bits & bit)
+            return dict(sm_mhz=statistics.median(self.samples), sm_max_mhz=self.max_mhz, reasons=reasons,
+                        samples=len(self.samples), source="nvml 10 ms")
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -244,7 +294,8 @@ class ClockSampler:
                     reasons.add(nm)
         if not sm:
             return None
-        return dict(sm_mhz=statistics.median(sm), sm_max_mhz=mx, reasons=sorted(reasons), samples=len(sm))
+        return dict(sm_mhz=statistics.median(sm), sm_max_mhz=mx, reasons=sorted(reasons), samples=len(sm),
+                    source="nvidia-smi 200 ms")
 
 
 # ------------------------------------------------------------------------------ GPU arm
