@@ -360,10 +360,6 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           tc_fence_after();
           const bool diag = (i == jt);  // key r is visible to query q iff r <= q
           // ---- P^T = 2^(S^T * scale * log2 e - lse2)
-          // the P^T columns are rewritten once the previous tile's dV MMA has read them
-          ok = __all_sync(0xffffffffu, mbar_wait(dv_done, (n & 1) ^ 1, p.err, 312));
-          if (!ok) break;
-          tc_fence_after();
           uint32_t pw[32];  // P^T as packed bf16 pairs: what the dV MMA reads, reused for dS
           {
             uint32_t a0[32], a1[32];  // both TMEM loads in flight before one wait
