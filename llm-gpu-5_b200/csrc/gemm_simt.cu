@@ -306,36 +306,53 @@ colsum_partial_kernel(const T* __restrict__ X, int64_t ldx, int M, int N, int ro
 #pragma unroll
   for (int i = 0; i < V; ++i) acc[i] = 0.f;
   const bool full = vec && (c0 + V <= N);
-  for (int r = r0 + ty; r < r1; r += TY) {
-    const T* row = X + (int64_t)r * ldx + c0;
-    float v[V];
-    if (full) {
-      if constexpr (sizeof(T) == 4) {
-        const float4 a = *reinterpret_cast<const float4*>(row);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-      } else {
-        const uint4 u = *reinterpret_cast<const uint4*>(row);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  // U rows per thread per step, their loads issued before any use (memory-level parallelism):
+  // 4 for float32 (0.263 -> 0.213 ms for the [262144, 768] dY cast + column sums); the bf16 form
+  // measured slower unrolled (0.284 -> 0.521 ms at [262144, 2304]) and keeps one row per step
+  constexpr int U = sizeof(T) == 4 ? 4 : 1;
+  for (int rb = r0 + ty; rb < r1; rb += U * TY) {
+    float v[U][V];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-          v[2 * i] = f.x;
-          v[2 * i + 1] = f.y;
+    for (int u = 0; u < U; ++u) {
+      const int r = rb + u * TY;
+      const T* row = X + (int64_t)r * ldx + c0;
+      if (r >= r1) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[u][i] = 0.f;
+      } else if (full) {
+        if constexpr (sizeof(T) == 4) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(row));
+          v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
+        } else {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(row));
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+            v[u][2 * i] = f.x;
+            v[u][2 * i + 1] = f.y;
+          }
         }
-      }
-    } else {
+      } else {
 #pragma unroll
-      for (int i = 0; i < V; ++i) v[i] = (c0 + i < N) ? Elem<T>::load(row + i) : 0.f;
+        for (int i = 0; i < V; ++i) v[u][i] = (c0 + i < N) ? Elem<T>::load(row + i) : 0.f;
+      }
     }
 #pragma unroll
-    for (int i = 0; i < V; ++i) acc[i] += v[i];
-    if constexpr (CAST) {
-      __nv_bfloat16* y = Y + (int64_t)r * ldy + c0;
-      if (full) {
-        *reinterpret_cast<uint2*>(y) = make_uint2(bf16x2_bits(v[0], v[1]), bf16x2_bits(v[2], v[3]));
-      } else {
-        for (int i = 0; i < V; ++i)
-          if (c0 + i < N) y[i] = __float2bfloat16_rn(v[i]);
+    for (int u = 0; u < U; ++u) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] += v[u][i];
+      const int r = rb + u * TY;
+      if constexpr (CAST) {
+        if (r < r1) {
+          __nv_bfloat16* y = Y + (int64_t)r * ldy + c0;
+          if (full) {
+            *reinterpret_cast<uint2*>(y) = make_uint2(bf16x2_bits(v[u][0], v[u][1]), bf16x2_bits(v[u][2], v[u][3]));
+          } else {
+            for (int i = 0; i < V; ++i)
+              if (c0 + i < N) y[i] = __float2bfloat16_rn(v[u][i]);
+          }
+        }
       }
     }
   }
