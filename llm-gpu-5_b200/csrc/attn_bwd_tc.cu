@@ -70,28 +70,25 @@ struct BwdParams {
   int* err;
 };
 
+// Eight lanes per row: lane c of a row reads the row's 16-byte pieces c (O and dO), so a row's 128
+// bytes of each are read by one coalesced request; the partial dot products meet by shuffles.
 __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o,
                                      const __nv_bfloat16* __restrict__ dout,
                                      const float* __restrict__ lse, float* __restrict__ lse2,
                                      float* __restrict__ delta, int NH, int T, int Tp, int D,
                                      int64_t o_sb, int64_t o_st, int64_t o_sh, int64_t rows) {
-  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (idx >= rows) return;
-  const int64_t bh = idx / Tp;
-  const int t = (int)(idx % Tp);
-  if (t >= T) {
-    lse2[idx] = INFINITY;  // padding rows: P = 2^(s - inf) = 0
-    delta[idx] = 0.f;
-    return;
-  }
-  const int b = (int)(bh / NH), h = (int)(bh % NH);
-  const int64_t off = b * o_sb + (int64_t)t * o_st + (int64_t)h * o_sh;
-  const uint4* po = reinterpret_cast<const uint4*>(o + off);
-  const uint4* pd = reinterpret_cast<const uint4*>(dout + off);
+  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t idx = gid >> 3;  // the row (all 8 lanes of a group share it; rows is padded per group)
+  const int c = (int)(gid & 7);
+  const bool live = idx < rows;
+  const int64_t bh = live ? idx / Tp : 0;
+  const int t = live ? (int)(idx % Tp) : 0;
   float acc = 0.f;
-#pragma unroll 8
-  for (int c = 0; c < D / 8; ++c) {
-    const uint4 a = po[c], g = pd[c];
+  if (live && t < T && c < D / 8) {
+    const int b = (int)(bh / NH), h = (int)(bh % NH);
+    const int64_t off = b * o_sb + (int64_t)t * o_st + (int64_t)h * o_sh;
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + off) + c);
+    const uint4 g = __ldg(reinterpret_cast<const uint4*>(dout + off) + c);
     const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -100,6 +97,15 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o,
       acc = fmaf(fa.x, fg.x, acc);
       acc = fmaf(fa.y, fg.y, acc);
     }
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  if (!live || c != 0) return;
+  if (t >= T) {
+    lse2[idx] = INFINITY;  // padding rows: P = 2^(s - inf) = 0
+    delta[idx] = 0.f;
+    return;
   }
   delta[idx] = acc;
   lse2[idx] = lse[bh * T + t] * LOG2E;
@@ -601,7 +607,7 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   float* delta = reinterpret_cast<float*>(w + align256((size_t)BH * Tp * 4));
   float* dq_acc = reinterpret_cast<float*>(w + 2 * align256((size_t)BH * Tp * 4));
   const int64_t rows = (int64_t)BH * Tp;
-  attn_bwd_prep_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
+  attn_bwd_prep_kernel<<<(unsigned)((rows * 8 + 255) / 256), 256, 0, stream>>>(
       (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, lse2, delta, NH, T, Tp, D, s[3], s[4], s[5], rows);
   count_launch();
   if (int rc = check_launch("attn_bwd_prep_kernel")) return rc;
