@@ -44,8 +44,10 @@ namespace attn {
 // P/dS warpgroups can hold more: per SM sub-partition (one warp of each warpgroup)
 // BA_REG_LOW + 2 * BA_REG_PDS + 128 <= 4 x 128.
 constexpr int BA_THREADS = 512;
+constexpr int BA_LAUNCH_REGS = 128;  // registers per thread at launch (512 threads); checked on the host
 constexpr int BA_REG_LOW = 96, BA_REG_PDS = 144;
-static_assert(BA_REG_LOW + 2 * BA_REG_PDS + 128 <= 4 * 128, "register split exceeds the launch allocation");
+static_assert(BA_REG_LOW + 2 * BA_REG_PDS + BA_LAUNCH_REGS <= 4 * BA_LAUNCH_REGS,
+              "register split exceeds the launch allocation");
 constexpr uint32_t BA_TMEM_COLS = 512;
 constexpr uint32_t BA_TM_S = 0, BA_TM_DP = 128, BA_TM_P = 256, BA_TM_DV = 320, BA_TM_DK = 384, BA_TM_DQ = 448;
 constexpr int BA_MAX_CTAS = 160;  // the dQ accumulator workspace is sized for this many CTAs
@@ -646,6 +648,8 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   if (!p.err) return ATTN_ERR_CUDA;
   static uint64_t attr_done = 0;
   if (!set_smem_limit_once(attn_bwd_tc_kernel, BA_SMEM, attr_done)) return ATTN_ERR_CUDA;
+  static int launch_regs = 0;
+  if (!launch_regs_match(attn_bwd_tc_kernel, BA_LAUNCH_REGS, launch_regs, "attn_bwd_tc_kernel")) return ATTN_ERR_CUDA;
   attn_bwd_tc_kernel<<<grid, BA_THREADS, BA_SMEM, stream>>>(maps, p);
   count_launch();
   return check_launch("attn_bwd_tc_kernel");

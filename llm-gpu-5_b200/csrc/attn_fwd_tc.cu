@@ -40,8 +40,9 @@ namespace attn {
 // have); warpgroup 0 gives registers back to the softmax warpgroups: per SM sub-partition (one
 // warp of each warpgroup) FA_REG_LOW + 2 * FA_REG_SOFT <= 3 x 168.
 constexpr int FA_THREADS = 384;
+constexpr int FA_LAUNCH_REGS = 168;  // registers per thread at launch (384 threads); checked on the host
 constexpr int FA_REG_LOW = 56, FA_REG_SOFT = 224;
-static_assert(FA_REG_LOW + 2 * FA_REG_SOFT <= 3 * 168, "register split exceeds the launch allocation");
+static_assert(FA_REG_LOW + 2 * FA_REG_SOFT <= 3 * FA_LAUNCH_REGS, "register split exceeds the launch allocation");
 constexpr uint32_t FA_TMEM_COLS = 512;
 constexpr uint32_t FA_TM_S = 0, FA_TM_P = 128, FA_TM_O = 192, FA_TM_STREAM = 256;
 constexpr int FA_STREAM_BYTES = 7 * AT_TILE_BYTES;  // Q[2], K[2], V[2], O staging
@@ -408,6 +409,8 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   if (!p.err) return ATTN_ERR_CUDA;
   static uint64_t attr_done = 0;
   if (!set_smem_limit_once(attn_fwd_tc_kernel, FA_SMEM, attr_done)) return ATTN_ERR_CUDA;
+  static int launch_regs = 0;
+  if (!launch_regs_match(attn_fwd_tc_kernel, FA_LAUNCH_REGS, launch_regs, "attn_fwd_tc_kernel")) return ATTN_ERR_CUDA;
   const int64_t units = (int64_t)p.BH * p.npairs;
   const int sms = current_device_sms();
   const int grid = (int)((units + 1) / 2 < sms ? (units + 1) / 2 : sms);  // at least a unit per stream

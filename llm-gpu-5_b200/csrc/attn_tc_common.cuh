@@ -98,4 +98,25 @@ inline bool set_smem_limit_once(Kernel kernel, int bytes, uint64_t& done) {
   return true;
 }
 
+// Whether `kernel` was built with the launch register allocation its setmaxnreg split was sized
+// for (read once; `cached` holds it).  A kernel that moves registers between warpgroups must not
+// launch otherwise: a warpgroup could wait for registers that never free up.
+template <typename Kernel>
+inline bool launch_regs_match(Kernel kernel, int expected, int& cached, const char* name) {
+  if (cached == 0) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncGetAttributes(%s) failed: %s", name, cudaGetErrorString(e));
+      return false;
+    }
+    cached = fa.numRegs;
+  }
+  if (cached != expected) {
+    set_error("%s: built with %d registers per thread, its register split needs %d", name, cached, expected);
+    return false;
+  }
+  return true;
+}
+
 }  // namespace attn
