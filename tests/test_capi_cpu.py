@@ -91,3 +91,36 @@ def test_import_fails_loudly_without_library(tmp_path, monkeypatch):
     with pytest.raises(ImportError, match="no non-CUDA fallback"):
         spec.loader.exec_module(mod)
     sys.modules.pop("_lib_probe", None)
+
+
+def test_bad_arguments_of_the_block_entry_points():
+    """The FFN GEMM, LayerNorm and LayerNorm-backward entry points validate before launching."""
+    pkg = load_pkg()
+    L = pkg.lib
+    before = pkg.launch_count()
+    fake = 1 << 20  # never dereferenced: validation fails first
+    # unknown activation
+    rc = L.attn_gemm_act(fake, 64, 0, fake, 64, 0, 1, fake, 64, 1, None, 64, 64, 64, 9, None, 0, 1, None)
+    assert rc == -1 and "activation" in L.attn_last_error_string().decode()
+    # GELU backward without the cached pre-activation
+    rc = L.attn_gemm_act(fake, 64, 0, fake, 64, 0, 1, fake, 64, 1, None, 64, 64, 64, 2, None, 0, 1, None)
+    assert rc == -1 and "aux" in L.attn_last_error_string().decode()
+    # the pre-activation output aliasing C
+    rc = L.attn_gemm_act(fake, 64, 0, fake, 64, 0, 1, fake, 64, 1, None, 64, 64, 64, 1, fake, 64, 1, None)
+    assert rc == -1 and "alias" in L.attn_last_error_string().decode()
+    # aux pitch below N
+    rc = L.attn_gemm_act(fake, 64, 0, fake, 64, 0, 1, fake, 64, 1, None, 64, 64, 64, 1, fake + 4096, 32, 1, None)
+    assert rc == -1 and "ldaux" in L.attn_last_error_string().decode()
+    # LayerNorm: eps must be positive, output must not alias the input, ones column needs room
+    rc = L.attn_layernorm(fake, 64, fake, fake, 8, 64, 0.0, fake + 8192, 64, 0, 0, None)
+    assert rc == -1 and "eps" in L.attn_last_error_string().decode()
+    rc = L.attn_layernorm(fake, 64, fake, fake, 8, 64, 1e-5, fake, 64, 0, 0, None)
+    assert rc == -1 and "alias" in L.attn_last_error_string().decode()
+    rc = L.attn_layernorm(fake, 64, fake, fake, 8, 64, 1e-5, fake + 8192, 64, 1, 1, None)
+    assert rc == -1 and "ldy" in L.attn_last_error_string().decode()
+    # LayerNorm backward: null pointers, dx aliasing x or dy
+    rc = L.attn_layernorm_bwd(None, fake, fake, 8, 64, 1e-5, fake, 0, fake, fake, 0, None)
+    assert rc == -1 and "null" in L.attn_last_error_string().decode()
+    rc = L.attn_layernorm_bwd(fake, fake + 4096, fake, 8, 64, 1e-5, fake + 4096, 0, fake, fake, 0, None)
+    assert rc == -1 and "alias" in L.attn_last_error_string().decode()
+    assert pkg.launch_count() == before
