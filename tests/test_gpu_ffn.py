@@ -98,8 +98,14 @@ def test_ffn_fixture_with_biases(pkg, cuda_dev):
         np.testing.assert_allclose(getattr(ffn, attr).grads.cpu().numpy(), 2 * g[key], rtol=1e-4, atol=2e-5)
 
 
-@pytest.mark.parametrize("prec,tol,M,C", [("fp32", 1e-5, 74, 64), ("bf16", 2e-2, 74, 64), ("bf16", 2e-2, 1024, 256),
-                                          ("bf16", 2e-2, 600, 768), ("fp32", 1e-5, 300, 96)])
+@pytest.mark.parametrize("prec,tol,M,C", [
+    ("fp32", 1e-5, 74, 64), ("bf16", 2e-2, 74, 64), ("bf16", 2e-2, 1024, 256), ("bf16", 2e-2, 600, 768),
+    ("fp32", 1e-5, 300, 96),
+    # edge shapes: one token, tiny widths (CUDA-core paths), hidden sizes that leave partial 256-column
+    # tiles and partial 64- or 32-column epilogue chunks on the tensor cores (4C = 288, 544), and a
+    # contraction (C = 136) that is not a multiple of the 64-deep K block
+    ("fp32", 1e-5, 2, 8), ("bf16", 2e-2, 2, 8), ("fp32", 1e-5, 6, 24), ("bf16", 2e-2, 130, 40),
+    ("bf16", 2e-2, 1000, 72), ("bf16", 2e-2, 4098, 136)])
 def test_ffn_matches_oracle(pkg, cuda_dev, prec, tol, M, C):
     inp = _inputs(M, C, M + C)
     if prec == "bf16":  # the oracle sees the operands the tensor cores see
