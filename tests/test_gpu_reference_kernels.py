@@ -159,7 +159,7 @@ def test_split_merge_heads_match_reference_kernels(pkg, cuda_dev, ref):
     assert torch.equal(ctx, ctx_ref)
 
 
-@pytest.mark.parametrize("M,C", [(1, 8), (300, 64), (1000, 768), (33, 100)])
+@pytest.mark.parametrize("M,C", [(1, 8), (300, 64), (1000, 768), (33, 100), (7, 2000), (9, 30)])
 def test_layernorm_backward_matches_reference_kernel(pkg, cuda_dev, ref, M, C):
     import torch
     rng = np.random.default_rng(M * 3 + C)
