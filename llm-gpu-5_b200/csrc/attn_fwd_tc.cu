@@ -9,7 +9,9 @@
 //
 // Work is handed out in units of two query tiles (nq-1-k, k) of one head, which cost nq+1 key
 // blocks together (the middle tile of an odd count is a unit of its own); a CTA's units alternate
-// between its two streams.
+// between its two streams.  When that leaves fewer than eight units per stream (few heads, long
+// sequences), whole units would leave the last round part-empty, so the units are then single
+// query tiles taken longest first (all heads' last tile, then the one before, ...).
 //
 //   TMA thread     Q of the tile (the next tile's Q is fetched while this tile streams), then
 //                  K_j and V_j for the key blocks j = 0 .. t into two-stage rings (K and V are
@@ -62,14 +64,23 @@ struct FwdParams {
 
 // The tiles of one stream, in the order all of the stream's roles visit them.  Work is cut into
 // units w = (head bh, pair k): query tiles nq-1-k and k of that head (the middle tile alone when
-// nq is odd), nq+1 key blocks per full pair.  The CTA takes units w = blockIdx.x + n*gridDim.x;
+// nq is odd), nq+1 key blocks per full pair; or, with SINGLES (a template parameter, so the pair
+// walk compiles as it would alone), units w = single tiles ordered by cost, tile nq-1-(w / BH) of
+// head w % BH.  The CTA takes units w = blockIdx.x + n*gridDim.x;
 // stream X takes its n = X, X+2, X+4, ...
+template <bool SINGLES>
 struct TileWalk {
   int n, second;  // unit index within the CTA, and which tile of the unit
   int bh, t;
   __device__ __forceinline__ bool valid(const FwdParams& p) const { return bh < p.BH; }
   __device__ __forceinline__ void set(const FwdParams& p) {
     const int w = blockIdx.x + n * gridDim.x;
+    if constexpr (SINGLES) {
+      const int level = w / p.BH;
+      t = p.nq - 1 - level;
+      bh = level < p.nq ? w - level * p.BH : p.BH;  // past the last tile: not valid
+      return;
+    }
     bh = w / p.npairs;
     const int k = w - bh * p.npairs;
     t = second ? k : p.nq - 1 - k;
@@ -80,7 +91,7 @@ struct TileWalk {
     set(p);
   }
   __device__ __forceinline__ void next(const FwdParams& p, int) {
-    if (!second && t != p.nq - 1 - t) {
+    if (!SINGLES && !second && t != p.nq - 1 - t) {
       second = 1;  // the pair's short tile
     } else {
       second = 0;
@@ -96,8 +107,10 @@ struct StreamBars {
 };
 static_assert(2 * sizeof(StreamBars) + 16 <= FA_BAR_BYTES, "barrier area too small");
 
+template <bool SINGLES>
 __global__ void __launch_bounds__(FA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
+  using TileWalk = attn::TileWalk<SINGLES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   StreamBars* sbars = reinterpret_cast<StreamBars*>(smem + 2 * FA_STREAM_BYTES);
@@ -407,14 +420,23 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   p.lse = lse;
   p.err = dev_error_ptr();
   if (!p.err) return ATTN_ERR_CUDA;
-  static uint64_t attr_done = 0;
-  if (!set_smem_limit_once(attn_fwd_tc_kernel, FA_SMEM, attr_done)) return ATTN_ERR_CUDA;
-  static int launch_regs = 0;
-  if (!launch_regs_match(attn_fwd_tc_kernel, FA_LAUNCH_REGS, launch_regs, "attn_fwd_tc_kernel")) return ATTN_ERR_CUDA;
-  const int64_t units = (int64_t)p.BH * p.npairs;
   const int sms = current_device_sms();
+  const bool singles = (int64_t)p.BH * p.npairs < (int64_t)8 * 2 * sms;
+  const int64_t units = (int64_t)p.BH * (singles ? p.nq : p.npairs);
   const int grid = (int)((units + 1) / 2 < sms ? (units + 1) / 2 : sms);  // at least a unit per stream
-  attn_fwd_tc_kernel<<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);
+  static uint64_t attr_pairs = 0, attr_singles = 0;
+  static int regs_pairs = 0, regs_singles = 0;
+  if (singles) {
+    if (!set_smem_limit_once(attn_fwd_tc_kernel<true>, FA_SMEM, attr_singles) ||
+        !launch_regs_match(attn_fwd_tc_kernel<true>, FA_LAUNCH_REGS, regs_singles, "attn_fwd_tc_kernel"))
+      return ATTN_ERR_CUDA;
+    attn_fwd_tc_kernel<true><<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);
+  } else {
+    if (!set_smem_limit_once(attn_fwd_tc_kernel<false>, FA_SMEM, attr_pairs) ||
+        !launch_regs_match(attn_fwd_tc_kernel<false>, FA_LAUNCH_REGS, regs_pairs, "attn_fwd_tc_kernel"))
+      return ATTN_ERR_CUDA;
+    attn_fwd_tc_kernel<false><<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);
+  }
   count_launch();
   return check_launch("attn_fwd_tc_kernel");
 }
