@@ -61,6 +61,19 @@ uint64_t attn_launch_count(void);
  */
 int attn_device_error(int clear);
 
+/* The code attn_wait_selftest leaves in the device error word. */
+#define ATTN_SELFTEST_SITE 900
+
+/*
+ * Failure-detection self-test, with no counterpart in the reference (whose kernels have no
+ * bounded waits): launches a one-warp kernel whose mbarrier wait can never complete, with a limit
+ * of limit_us microseconds (1 .. 1000000).  The wait gives up after that limit, sets the device
+ * error word to ATTN_SELFTEST_SITE (if it was 0) and the kernel returns, the same path a real
+ * wait inside the tensor-core kernels takes; the context stays usable.  Read the word with
+ * attn_device_error(1), which also clears it.
+ */
+int attn_wait_selftest(int limit_us, void* stream);
+
 /*
  * Causal attention forward: O = softmax(scale * Q K^T + causal mask) V, plus lse.
  * Replaces fused_attention_forward_kernel (core/mha_kernels.py:404-521); instead of writing the

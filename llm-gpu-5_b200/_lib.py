@@ -22,6 +22,7 @@ ATTN_BF16 = 1
 ATTN_ACT_NONE = 0
 ATTN_ACT_GELU = 1
 ATTN_ACT_GELU_BWD = 2
+ATTN_SELFTEST_SITE = 900
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -35,6 +36,7 @@ SIGNATURES = {
     "attn_last_error_string": (ctypes.c_char_p, []),
     "attn_launch_count": (ctypes.c_uint64, []),
     "attn_device_error": (_i, [_i]),
+    "attn_wait_selftest": (_i, [_i, _p]),
     "attn_fwd": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i, _p]),
     "attn_bwd_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "attn_bwd": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _i, _i, _i, _i,

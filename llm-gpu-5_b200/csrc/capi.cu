@@ -143,6 +143,7 @@ int cast_colsum(const float*, int64_t, int, int, void*, int64_t, float*, int, vo
 int attn_probs_launch(const void*, const void*, const float*, float*, int, int, int, int, int64_t,
                       int64_t, int64_t, float, int, cudaStream_t);
 size_t decode_ws(int, int, int, int);
+int wait_selftest(int, cudaStream_t);
 int decode(const void*, const void*, const void*, void*, float*, int, int, int, int, int64_t,
            int64_t, int64_t, int64_t, int64_t, float, int, float*, cudaStream_t);
 bool tc_fwd_supported(int D, int dtype);
@@ -200,6 +201,12 @@ int attn_device_error(int clear) {
     cudaMemcpy(p, &z, sizeof(int), cudaMemcpyHostToDevice);
   }
   return v;
+}
+
+int attn_wait_selftest(int limit_us, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(limit_us >= 1 && limit_us <= 1000000, "attn_wait_selftest: limit_us must be 1 .. 1000000");
+  return wait_selftest(limit_us, as_stream(stream));
 }
 
 int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int NH, int T,
