@@ -93,3 +93,55 @@ def test_shard_and_layout():
     assert [(n, o) for n, o, _ in lay] == [("c_attn_w", 0), ("c_attn_b", 768 * 2304),
                                           ("c_proj_w", 768 * 2304 + 2304), ("c_proj_b", 768 * 2304 + 2304 + 768 * 768)]
     assert dp.flat_grad_size(768) == 2362368  # 9.45 MB of fp32 per all-reduce at d_model 768
+
+
+def _rank_that_may_leave(rank, world, port, q):
+    """Rank 1 leaves between steps (after joining, before the gradient all-reduce); rank 0 goes on
+    to the all-reduce of the flat gradient buffer, which must end with an error, not wait forever."""
+    import datetime
+    import time
+    try:
+        import torch
+        import torch.distributed as dist
+        dp = load_pkg().dp
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=10))
+        if rank == 1:
+            q.put((rank, "left", 0.0))
+            q.close()
+            q.join_thread()  # the message is out before the process goes
+            os._exit(0)  # gone, with no collective in flight
+        time.sleep(1.0)  # let the other rank go first
+        t0 = time.perf_counter()
+        try:
+            dp.allreduce_grads(torch.zeros(dp.flat_grad_size(C), dtype=torch.float64))
+            q.put((rank, "completed", time.perf_counter() - t0))
+        except Exception as e:  # the expected outcome: the collective fails
+            q.put((rank, "error:" + type(e).__name__, time.perf_counter() - t0))
+        q.close()
+        q.join_thread()
+        os._exit(0)  # skip destroy_process_group: its peer is gone
+    except Exception as e:
+        q.put((rank, "setup error " + repr(e), 0.0))
+
+
+@pytest.mark.timeout(180)
+def test_rank_that_leaves_ends_the_survivors_all_reduce_with_an_error():
+    """Failure detection on the host: a rank that exits between steps makes the surviving rank's
+    next gradient all-reduce raise within the process group's timeout instead of hanging."""
+    import torch.multiprocessing as mp
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_that_may_leave, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict((r, (what, t)) for r, what, t in (q.get(timeout=120) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert results[1][0] == "left", results
+    what, took = results[0]
+    assert what.startswith("error:"), results
+    assert took < 30.0, results  # bounded by the 10 s process-group timeout (plus slack)
