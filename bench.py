@@ -469,6 +469,21 @@ def run_ours(args, cfg):
         if full is not None and not args.batch:
             traffic = full * B / GB
     total_flops = sum(op_flops(k, B, T, C, NH) for k in totals if op_flops(k, B, T, C, NH))
+    # the attention core (QK^T, PV, dP, dV, dQ, dK: 12*D per causal pair, no credit for recomputing S)
+    # and the six projection GEMMs, each over its own event-timed kernels, and their sum
+    groups = {}
+    for k, (t, n) in totals.items():
+        f = op_flops(k, B, T, C, NH)
+        if f:
+            g = "attention_core" if k.startswith("attn_") else "projections"
+            fl, tm = groups.get(g, (0, 0.0))
+            groups[g] = (fl + f * n / steps, tm + t / steps)
+    tflops = {g: dict(tflop_per_step=fl / 1e12, ms_per_step=tm, tflops=fl / (tm * 1e-3) / 1e12)
+              for g, (fl, tm) in groups.items()}
+    if groups:
+        fl = sum(v[0] for v in groups.values())
+        tm = sum(v[1] for v in groups.values())
+        tflops["sum"] = dict(tflop_per_step=fl / 1e12, ms_per_step=tm, tflops=fl / (tm * 1e-3) / 1e12)
     line = dict(
         metric="causal attention fwd+bwd tokens/sec", value=value, unit="tokens/s", n_gpus=world,
         steps=steps, warmup=warmup, ms_per_step=ms, higher_is_better=True, scaling="strong",
@@ -479,6 +494,7 @@ def run_ours(args, cfg):
                       frac=achieved / peak, traffic=traffic,
                       peak_source=f"{src} bf16_tflops_sustained"),
         step_tflops=total_flops / (ms * 1e-3) / 1e12 if world == 1 else None,
+        tflops=tflops,
         breakdown=per_op,
         gpu_launches=launches,
         e2e=dict(value=GB * T / (e2e_ms * 1e-3), unit="tokens/s", h2d_bytes_per_step=h2d * world,
