@@ -123,6 +123,29 @@ def test_attention_bf16_matches_oracle(pkg, cuda_dev, B, NH, T, D, layout):
         assert O.rel_err(g, r) < BF16_TOL, (name, O.rel_err(g, r))
 
 
+@pytest.mark.parametrize("dtype,D", [("bf16", 64), ("bf16", 32), ("f32", 64)])
+def test_attention_long_rows(pkg, cuda_dev, dtype, D):
+    """T = 2048 (16 key tiles per row) with large scores whose row maximum keeps growing along the
+    keys: the forward's lazy rescaling (the running max moves only when it grows by more than 2^8)
+    and the backward over many key tiles, against the oracle."""
+    B, NH, T = 1, 2, 2048
+    rng = np.random.default_rng(2048 + D)
+    q, k, v, do = (2.5 * rng.standard_normal((B, NH, T, D)) for _ in range(4))
+    u = rng.standard_normal(D)
+    u /= np.linalg.norm(u)
+    q += 2.0 * u
+    k += (4.0 * np.arange(T) / T)[None, None, :, None] * u  # later keys score higher
+    q, k, v, do = (a.astype(np.float32) for a in (q, k, v, do))
+    if dtype == "bf16":
+        q, k, v, do = (_bf16_round(a) for a in (q, k, v, do))
+    got = _run_attention(pkg, q, k, v, do, dtype, "tokens")
+    ref = _oracle(q, k, v, do)
+    tol = BF16_TOL if dtype == "bf16" else F32_TOL
+    for name, g, r in zip(("o", "lse", "dq", "dk", "dv"), got, ref):
+        assert O.rel_err(g, r) < tol, (name, O.rel_err(g, r))
+    assert pkg.lib.attn_device_error(1) == 0
+
+
 def test_kernel_golden_fixture(pkg, cuda_dev):
     """The reference's Layer-1 golden case (seed 1337, H=3, M=17, D=8) through the fp32 kernels."""
     torch = _torch()
