@@ -19,6 +19,7 @@
 //                     P^T = 2^(S^T*scale*log2e - lse2) into its own TMEM columns (so S^T of the
 //                     next tile can be computed while dS is formed), dS^T = P^T (dP^T - delta)
 //                     to TMEM over the dP^T columns already read and to shared memory for dQ
+//                     (two dS buffers, so tile n's dS never waits for tile n-1's dQ MMA)
 //      4 drain warps  per tile: the dQ partial from TMEM to a per-CTA fp32 accumulator (a TMA
 //                     store from the diagonal key tile, which reaches a query tile first, TMA
 //                     reduce-adds after it, all into L2-resident memory); for key tile 0 (each
@@ -51,9 +52,9 @@ static_assert(BA_REG_LOW + 2 * BA_REG_PDS + BA_LAUNCH_REGS <= 4 * BA_LAUNCH_REGS
 constexpr uint32_t BA_TMEM_COLS = 512;
 constexpr uint32_t BA_TM_S = 0, BA_TM_DP = 128, BA_TM_P = 256, BA_TM_DV = 320, BA_TM_DK = 384, BA_TM_DQ = 448;
 constexpr int BA_MAX_CTAS = 160;  // the dQ accumulator workspace is sized for this many CTAs
-constexpr int BA_QS = 3;  // Q / dO / lse2 / delta stages
+constexpr int BA_QS = 2;  // Q / dO / lse2 / delta stages (two, to leave room for two dS buffers)
 constexpr int BA_SMEM = 1024 + 4 * AT_TILE_BYTES /*K,V x2*/ + 2 * BA_QS * AT_TILE_BYTES /*Q,dO*/ +
-                        2 * AT_TILE_BYTES /*dS^T*/ + AT_TILE * 128 /*dQ staging, half a tile*/ +
+                        4 * AT_TILE_BYTES /*dS^T, two buffers*/ + AT_TILE * 128 /*dQ staging, half a tile*/ +
                         2 * BA_QS * AT_TILE * 4 /*lse2, delta*/ + 256;
 
 struct BwdMaps {
@@ -157,8 +158,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   uint8_t* sV = sK + 2 * AT_TILE_BYTES;        // [2]
   uint8_t* sQ = sV + 2 * AT_TILE_BYTES;        // [BA_QS]
   uint8_t* sDO = sQ + BA_QS * AT_TILE_BYTES;   // [BA_QS]
-  uint8_t* sDS = sDO + BA_QS * AT_TILE_BYTES;  // dS^T: two 64-query blocks of [128 keys][64]
-  uint8_t* sDQ = sDS + 2 * AT_TILE_BYTES;      // dQ staging: one [128 q][32 fp32] swizzled half
+  uint8_t* sDS = sDO + BA_QS * AT_TILE_BYTES;  // dS^T [2 buffers]: two 64-query blocks of [128 keys][64]
+  uint8_t* sDQ = sDS + 4 * AT_TILE_BYTES;      // dQ staging: one [128 q][32 fp32] swizzled half
   float* sLse = reinterpret_cast<float*>(sDQ + AT_TILE * 128);  // [BA_QS][128]
   float* sDelta = sLse + BA_QS * AT_TILE;                           // [BA_QS][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + BA_QS * AT_TILE);
@@ -172,8 +173,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   uint64_t* dv_done = p_ready + 1;    // the dV MMA reading P^T has completed
   uint64_t* ds_ready = dv_done + 1;   // dP^T read, dS^T written to TMEM and smem (256 arrivals)
   uint64_t* dk_done = ds_ready + 1;   // the dK MMA reading dS^T from TMEM has completed
-  uint64_t* ds_free = dk_done + 1;    // the dQ MMA reading dS^T from smem has completed
-  uint64_t* dq_full = ds_free + 1;
+  uint64_t* ds_free = dk_done + 1;    // [2] the dQ MMA reading that dS^T buffer has completed
+  uint64_t* dq_full = ds_free + 2;
   uint64_t* dq_free = dq_full + 1;    // 128 arrivals
   uint64_t* dkdv_full = dq_free + 1;
   uint64_t* dkdv_free = dkdv_full + 1;  // 128 arrivals
@@ -198,7 +199,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
     mbar_init(dv_done, 1);
     mbar_init(ds_ready, 256);
     mbar_init(dk_done, 1);
-    mbar_init(ds_free, 1);
+    mbar_init(&ds_free[0], 1);
+    mbar_init(&ds_free[1], 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 128);
     mbar_init(dkdv_full, 1);
@@ -270,11 +272,14 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
         // (row = 64 output columns), built per use from the stage's base address
         auto kmaj = [](const uint8_t* t) { return smem_desc_sw128(smem_u32(t), 16, 1024); };
         auto mnmaj = [](const uint8_t* t) { return smem_desc_sw128(smem_u32(t), 8192, 1024); };
-        // The previous tile's dV, dK and dQ are issued after this tile's S^T, which goes to the tensor
-        // core as soon as the P/dS warps have read the previous S^T.
+        // The previous tile's dV and dK are issued after this tile's S^T, which goes to the tensor
+        // core as soon as the P/dS warps have read the previous S^T; then this tile's dP^T (it only
+        // waits for the dK MMA, which reads the dS^T columns dP^T overwrites), and the previous
+        // tile's dQ last: it reads its own dS buffer in shared memory, so the P/dS warps get dP^T
+        // early and can write the next dS into the other buffer meanwhile.
         int pn = -1, ps = 0, pks = 0, pu = 0;
         bool pfirst = false, plast = false;
-        auto finish_prev = [&]() -> bool {
+        auto finish_dvdk = [&]() -> bool {
           // dV += P^T dO   (the first tile of a key tile starts dV/dK afresh once they are drained)
           if (pfirst && !mbar_wait(dkdv_free, (pu & 1) ^ 1, p.err, 308)) return false;
           tc_fence_after();
@@ -285,21 +290,25 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           umma_commit(dv_done);
           if (!mbar_wait(ds_ready, pn & 1, p.err, 303)) return false;
           tc_fence_after();
-          const uint64_t q_mn = mnmaj(sQ + ps * AT_TILE_BYTES), k_mn = mnmaj(sK + pks * AT_TILE_BYTES);
-          const uint64_t ds_mn = smem_desc_sw128(smem_u32(sDS), 16384, 1024);  // two 64-query blocks
+          const uint64_t q_mn = mnmaj(sQ + ps * AT_TILE_BYTES);
   #pragma unroll
           for (int k = 0; k < AT_TILE / 16; ++k)  // dK += dS^T Q   (k over the 128 queries)
             umma_ts(tdK, tdP + (k >> 2) * 64 + (k & 3) * 8, desc_step(q_mn, k * 2048),
                     idesc_kv, (pfirst && k == 0) ? 0u : 1u);
           umma_commit(dk_done);
           umma_commit(&q_empty[ps]);  // dK was the last MMA to read Q (and dV the last for dO)
+          return true;
+        };
+        auto finish_dq = [&]() -> bool {
           if (!mbar_wait(dq_free, (pn & 1) ^ 1, p.err, 304)) return false;
           tc_fence_after();
+          const uint64_t k_mn = mnmaj(sK + pks * AT_TILE_BYTES);
+          const uint64_t ds_mn = smem_desc_sw128(smem_u32(sDS + (pn & 1) * 2 * AT_TILE_BYTES), 16384, 1024);
   #pragma unroll
           for (int k = 0; k < AT_TILE / 16; ++k)  // dQ = dS K   (k over the 128 keys)
             umma_ss(tdQ, desc_step(ds_mn, k * 2048), desc_step(k_mn, k * 2048), idesc_q, k > 0 ? 1u : 0u);
           umma_commit(dq_full);
-          umma_commit(ds_free);
+          umma_commit(&ds_free[pn & 1]);
           if (plast) {
             umma_commit(dkdv_full);
             umma_commit(&kv_empty[pks]);
@@ -324,7 +333,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
               for (int k = 0; k < AT_D / 16; ++k)
                 umma_ss(tS, desc_step(k_k, k * 32), desc_step(q_k, k * 32), idesc_sdp, k > 0 ? 1u : 0u);
               umma_commit(s_full);
-              if (pn >= 0 && !finish_prev()) { ok = false; break; }
+              if (pn >= 0 && !finish_dvdk()) { ok = false; break; }
               // dP^T = V dO^T over the previous dS^T: wait for the dK MMA that reads it
               if (!mbar_wait(dk_done, (n & 1) ^ 1, p.err, 307)) { ok = false; break; }
               tc_fence_after();
@@ -332,6 +341,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
               for (int k = 0; k < AT_D / 16; ++k)
                 umma_ss(tdP, desc_step(v_k, k * 32), desc_step(do_k, k * 32), idesc_sdp, k > 0 ? 1u : 0u);
               umma_commit(dp_full);
+              if (pn >= 0 && !finish_dq()) { ok = false; break; }
               pn = n;
               ps = s;
               pks = ks;
@@ -341,7 +351,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
             }
           }
         }
-        if (ok && pn >= 0 && mbar_wait(p_ready, pn & 1, p.err, 309)) finish_prev();
+        if (ok && pn >= 0 && mbar_wait(p_ready, pn & 1, p.err, 309) && finish_dvdk()) finish_dq();
       }
     }
   } else if (warp < 12) {
@@ -354,7 +364,6 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
     const uint32_t tS = tmem + BA_TM_S + lane_off + g * 64;
     const uint32_t tdP = tmem + BA_TM_DP + lane_off + g * 64;
     const uint32_t tP = tmem + BA_TM_P + lane_off + g * 32;
-    uint8_t* dsrow = sDS + g * AT_TILE_BYTES + r * 128;
     const float sl2 = p.scale_log2;
     int n = 0;
     bool ok = true;
@@ -405,7 +414,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           mbar_arrive(p_ready);
           // ---- dS^T = P^T (dP^T - delta)
           ok = __all_sync(0xffffffffu, mbar_wait(dp_full, n & 1, p.err, 313) &&
-                                           mbar_wait(ds_free, (n & 1) ^ 1, p.err, 314));
+                                           mbar_wait(&ds_free[n & 1], ((n >> 1) & 1) ^ 1, p.err, 314));
+          uint8_t* dsrow = sDS + (n & 1) * 2 * AT_TILE_BYTES + g * AT_TILE_BYTES + r * 128;
           if (!ok) break;
           tc_fence_after();
           {
