@@ -39,8 +39,8 @@
 
 namespace attn {
 
-// Four warpgroups: 0 = TMA for K/V (warp 0), MMA (warp 1), TMA for Q/dO (warp 2), one idle warp;
-// 1-2 = P/dS; 3 = drain.
+// Four warpgroups: 0 = TMA for K/V (warp 0), MMA (warp 1), TMA for Q and lse2 (warp 2), TMA for dO
+// and delta (warp 3); 1-2 = P/dS; 3 = drain.
 // Launched at 128 registers per thread (512 threads); warpgroup 0 gives registers back so the
 // P/dS warpgroups can hold more: per SM sub-partition (one warp of each warpgroup)
 // BA_REG_LOW + 2 * BA_REG_PDS + 128 <= 4 x 128.
@@ -52,10 +52,16 @@ static_assert(BA_REG_LOW + 2 * BA_REG_PDS + BA_LAUNCH_REGS <= 4 * BA_LAUNCH_REGS
 constexpr uint32_t BA_TMEM_COLS = 512;
 constexpr uint32_t BA_TM_S = 0, BA_TM_DP = 128, BA_TM_P = 256, BA_TM_DV = 320, BA_TM_DK = 384, BA_TM_DQ = 448;
 constexpr int BA_MAX_CTAS = 160;  // the dQ accumulator workspace is sized for this many CTAs
-constexpr int BA_QS = 2;  // Q / dO / lse2 / delta stages (two, to leave room for two dS buffers)
-constexpr int BA_SMEM = 1024 + 4 * AT_TILE_BYTES /*K,V x2*/ + 2 * BA_QS * AT_TILE_BYTES /*Q,dO*/ +
+// Q (+ lse2) has three stages: S^T(n+1) reads Q(n+1) while dK(n-1) may still read Q(n-1).  dO
+// (+ delta) has two: dP^T(n+1) comes late in tile n+1, after dV(n) and dK(n), the last readers of
+// the stage it reuses.  With two dS^T buffers that fills shared memory with no room for an
+// alignment pad; the kernel checks that the dynamic shared memory starts 1024-byte aligned.
+constexpr int BA_QS = 3, BA_OS = 2;
+constexpr int BA_SMEM = 4 * AT_TILE_BYTES /*K,V x2*/ + (BA_QS + BA_OS) * AT_TILE_BYTES /*Q, dO*/ +
                         4 * AT_TILE_BYTES /*dS^T, two buffers*/ + AT_TILE * 128 /*dQ staging, half a tile*/ +
-                        2 * BA_QS * AT_TILE * 4 /*lse2, delta*/ + 256;
+                        (BA_QS + BA_OS) * AT_TILE * 4 /*lse2, delta*/ + 256;
+static_assert(BA_SMEM <= 232448, "over the per-block shared memory limit");
+constexpr int BA_SITE_SMEM_ALIGN = 300;  // error site: dynamic shared memory not 1024-byte aligned
 
 struct BwdMaps {
   TileMap q, k, v, dout;
@@ -152,22 +158,28 @@ __device__ __forceinline__ void store_packed_row(__nv_bfloat16* dst, const uint3
 
 __global__ void __launch_bounds__(BA_THREADS, 1)
 attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {  // the swizzled tiles need it; uniform, so every thread leaves
+    if (threadIdx.x == 0) atomicCAS(p.err, 0, BA_SITE_SMEM_ALIGN);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sK = smem;                          // [2]
   uint8_t* sV = sK + 2 * AT_TILE_BYTES;        // [2]
   uint8_t* sQ = sV + 2 * AT_TILE_BYTES;        // [BA_QS]
-  uint8_t* sDO = sQ + BA_QS * AT_TILE_BYTES;   // [BA_QS]
-  uint8_t* sDS = sDO + BA_QS * AT_TILE_BYTES;  // dS^T [2 buffers]: two 64-query blocks of [128 keys][64]
+  uint8_t* sDO = sQ + BA_QS * AT_TILE_BYTES;   // [BA_OS]
+  uint8_t* sDS = sDO + BA_OS * AT_TILE_BYTES;  // dS^T [2 buffers]: two 64-query blocks of [128 keys][64]
   uint8_t* sDQ = sDS + 4 * AT_TILE_BYTES;      // dQ staging: one [128 q][32 fp32] swizzled half
   float* sLse = reinterpret_cast<float*>(sDQ + AT_TILE * 128);  // [BA_QS][128]
-  float* sDelta = sLse + BA_QS * AT_TILE;                           // [BA_QS][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + BA_QS * AT_TILE);
+  float* sDelta = sLse + BA_QS * AT_TILE;                           // [BA_OS][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + BA_OS * AT_TILE);
   uint64_t* kv_full = bars;           // [2] per key tile (unit)
   uint64_t* kv_empty = kv_full + 2;   // [2]
   uint64_t* q_full = kv_empty + 2;    // [BA_QS] per query tile
   uint64_t* q_empty = q_full + BA_QS; // [BA_QS]
-  uint64_t* s_full = q_empty + BA_QS; // S^T in TMEM
+  uint64_t* o_full = q_empty + BA_QS; // [BA_OS] per query tile: dO and delta
+  uint64_t* o_empty = o_full + BA_OS; // [BA_OS]
+  uint64_t* s_full = o_empty + BA_OS; // S^T in TMEM
   uint64_t* dp_full = s_full + 1;     // dP^T in TMEM
   uint64_t* p_ready = dp_full + 1;    // S^T read, P^T written (256 arrivals)
   uint64_t* dv_done = p_ready + 1;    // the dV MMA reading P^T has completed
@@ -193,6 +205,10 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
     }
+    for (int s = 0; s < BA_OS; ++s) {
+      mbar_init(&o_full[s], 1);
+      mbar_init(&o_empty[s], 1);
+    }
     mbar_init(s_full, 1);
     mbar_init(dp_full, 1);
     mbar_init(p_ready, 256);
@@ -217,7 +233,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 4) {  // TMA producers, MMA issuer, one idle warp
+  if (warp < 4) {  // TMA producers, MMA issuer
     reg_dealloc<BA_REG_LOW>();
     if (warp == 0) {
       // ---------------- TMA producer: K/V per key tile ----------------
@@ -237,25 +253,31 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           }
         }
       }
-    } else if (warp == 2) {
-      // ---------------- TMA producer: Q, dO, lse2, delta per query tile (runs ahead of K/V) ----------------
+    } else if (warp == 2 || warp == 3) {
+      // ---------------- TMA producers per query tile (run ahead of K/V): warp 2 Q and lse2 into the
+      // Q stages, warp 3 dO and delta into the dO stages ----------------
       if (lane == 0) {
-        tma_prefetch_desc(&maps.q.map);
-        tma_prefetch_desc(&maps.dout.map);
+        const bool isq = (warp == 2);
+        const TileMap& map = isq ? maps.q : maps.dout;
+        const float* vec = isq ? p.lse2 : p.delta;
+        uint8_t* tiles = isq ? sQ : sDO;
+        float* vecs = isq ? sLse : sDelta;
+        uint64_t* full = isq ? q_full : o_full;
+        uint64_t* empty = isq ? q_empty : o_empty;
+        const int nst = isq ? BA_QS : BA_OS;
+        tma_prefetch_desc(&map.map);
         int n = 0;
         bool ok = true;
         for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
           const int b = bh / p.NH, h = bh % p.NH;
           for (int jt = nq - 1; jt >= 0 && ok; --jt) {
             for (int i = jt; i < nq; ++i, ++n) {
-              const int s = n % BA_QS;
-              if (!mbar_wait(&q_empty[s], ((n / BA_QS) & 1) ^ 1, p.err, 302)) { ok = false; break; }
+              const int s = n % nst;
+              if (!mbar_wait(&empty[s], ((n / nst) & 1) ^ 1, p.err, isq ? 302 : 318)) { ok = false; break; }
               const int q0 = i * AT_TILE;
-              mbar_arrive_expect_tx(&q_full[s], 2 * AT_TILE_BYTES + 2 * AT_TILE * 4);
-              load_tile(sQ + s * AT_TILE_BYTES, maps.q, &q_full[s], b, h, q0);
-              load_tile(sDO + s * AT_TILE_BYTES, maps.dout, &q_full[s], b, h, q0);
-              bulk_load(sLse + s * AT_TILE, p.lse2 + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
-              bulk_load(sDelta + s * AT_TILE, p.delta + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &q_full[s]);
+              mbar_arrive_expect_tx(&full[s], AT_TILE_BYTES + AT_TILE * 4);
+              load_tile(tiles + s * AT_TILE_BYTES, map, &full[s], b, h, q0);
+              bulk_load(vecs + s * AT_TILE, vec + (int64_t)bh * p.Tp + q0, AT_TILE * 4, &full[s]);
             }
           }
         }
@@ -277,13 +299,13 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
         // waits for the dK MMA, which reads the dS^T columns dP^T overwrites), and the previous
         // tile's dQ last: it reads its own dS buffer in shared memory, so the P/dS warps get dP^T
         // early and can write the next dS into the other buffer meanwhile.
-        int pn = -1, ps = 0, pks = 0, pu = 0;
+        int pn = -1, ps = 0, pso = 0, pks = 0, pu = 0;
         bool pfirst = false, plast = false;
         auto finish_dvdk = [&]() -> bool {
           // dV += P^T dO   (the first tile of a key tile starts dV/dK afresh once they are drained)
           if (pfirst && !mbar_wait(dkdv_free, (pu & 1) ^ 1, p.err, 308)) return false;
           tc_fence_after();
-          const uint64_t do_mn = mnmaj(sDO + ps * AT_TILE_BYTES);
+          const uint64_t do_mn = mnmaj(sDO + pso * AT_TILE_BYTES);
   #pragma unroll
           for (int k = 0; k < AT_TILE / 16; ++k)
             umma_ts(tdV, tP + k * 8, desc_step(do_mn, k * 2048), idesc_kv, (pfirst && k == 0) ? 0u : 1u);
@@ -296,7 +318,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
             umma_ts(tdK, tdP + (k >> 2) * 64 + (k & 3) * 8, desc_step(q_mn, k * 2048),
                     idesc_kv, (pfirst && k == 0) ? 0u : 1u);
           umma_commit(dk_done);
-          umma_commit(&q_empty[ps]);  // dK was the last MMA to read Q (and dV the last for dO)
+          umma_commit(&q_empty[ps]);   // dK was the last MMA to read Q
+          umma_commit(&o_empty[pso]);  // dV the last for dO, and delta has been read before ds_ready
           return true;
         };
         auto finish_dq = [&]() -> bool {
@@ -323,12 +346,12 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
             if (!mbar_wait(&kv_full[ks], (u >> 1) & 1, p.err, 305)) { ok = false; break; }
             const uint64_t k_k = kmaj(sK + ks * AT_TILE_BYTES), v_k = kmaj(sV + ks * AT_TILE_BYTES);
             for (int i = jt; i < nq; ++i, ++n) {
-              const int s = n % BA_QS;
+              const int s = n % BA_QS, so = n % BA_OS;
               if (!mbar_wait(&q_full[s], (n / BA_QS) & 1, p.err, 306)) { ok = false; break; }
               // S^T = K Q^T once the P/dS warps have read the previous S^T (and written its P^T)
               if (pn >= 0 && !mbar_wait(p_ready, pn & 1, p.err, 309)) { ok = false; break; }
               tc_fence_after();
-              const uint64_t q_k = kmaj(sQ + s * AT_TILE_BYTES), do_k = kmaj(sDO + s * AT_TILE_BYTES);
+              const uint64_t q_k = kmaj(sQ + s * AT_TILE_BYTES), do_k = kmaj(sDO + so * AT_TILE_BYTES);
   #pragma unroll
               for (int k = 0; k < AT_D / 16; ++k)
                 umma_ss(tS, desc_step(k_k, k * 32), desc_step(q_k, k * 32), idesc_sdp, k > 0 ? 1u : 0u);
@@ -336,6 +359,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
               if (pn >= 0 && !finish_dvdk()) { ok = false; break; }
               // dP^T = V dO^T over the previous dS^T: wait for the dK MMA that reads it
               if (!mbar_wait(dk_done, (n & 1) ^ 1, p.err, 307)) { ok = false; break; }
+              if (!mbar_wait(&o_full[so], (n / BA_OS) & 1, p.err, 319)) { ok = false; break; }
               tc_fence_after();
   #pragma unroll
               for (int k = 0; k < AT_D / 16; ++k)
@@ -344,6 +368,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
               if (pn >= 0 && !finish_dq()) { ok = false; break; }
               pn = n;
               ps = s;
+              pso = so;
               pks = ks;
               pu = u;
               pfirst = (i == jt);
@@ -413,7 +438,9 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           tc_fence_before();
           mbar_arrive(p_ready);
           // ---- dS^T = P^T (dP^T - delta)
+          const int so = n % BA_OS;
           ok = __all_sync(0xffffffffu, mbar_wait(dp_full, n & 1, p.err, 313) &&
+                                           mbar_wait(&o_full[so], (n / BA_OS) & 1, p.err, 320) &&
                                            mbar_wait(&ds_free[n & 1], ((n >> 1) & 1) ^ 1, p.err, 314));
           uint8_t* dsrow = sDS + (n & 1) * 2 * AT_TILE_BYTES + g * AT_TILE_BYTES + r * 128;
           if (!ok) break;
@@ -423,7 +450,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
             tmem_ld32(tdP, a0);
             tmem_ld32(tdP + 32, a1);
             tmem_wait_ld();
-            const float4* d4 = reinterpret_cast<const float4*>(sDelta + s * AT_TILE + g * 64);
+            const float4* d4 = reinterpret_cast<const float4*>(sDelta + so * AT_TILE + g * 64);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
               uint32_t dk[16];
