@@ -544,7 +544,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           tc_fence_before();
           mbar_arrive(dq_free);
           const int qrow = i * AT_TILE + row;
-if (jt == 0) {
+          if (jt == 0) {
             // key tile 0 is this query tile's last contribution: finish dQ
             if (i > 0) {
               // the accumulator's last reduce-add for tile i came from key tile 1, whose later
