@@ -57,7 +57,10 @@ uint64_t attn_launch_count(void);
 /*
  * Status word of the tensor-core kernels on the current device: 0, or the code of a bounded
  * wait inside a kernel that gave up (the kernel then skipped its remaining work and returned
- * instead of hanging).  Synchronises with the device.  clear != 0 resets it to 0.
+ * instead of hanging).  Codes are grouped by kernel: 1xx the GEMM, 2xx the attention forward,
+ * 3xx the attention backward (300: its dynamic shared memory did not start 1024-byte aligned,
+ * checked before any work), 900 the self-test below.  Synchronises with the device.
+ * clear != 0 resets it to 0.
  */
 int attn_device_error(int clear);
 
