@@ -1,4 +1,5 @@
-// tcgen05 causal attention backward for head_dim 64 (bf16 operands, fp32 accumulation).
+// tcgen05 causal attention backward for head_dim a multiple of 8 up to 64 (64-wide tiles; TMA
+// zero-fills the columns of narrower heads), bf16 operands, fp32 accumulation.
 //
 // Replaces the NumPy backward of model/gpt.py:669-680 (and the unwired GPU kernels
 // softmax_fused_backward / matmul_grad_{q,k,v}, core/mha_kernels.py:195-236, 592-680):
@@ -12,6 +13,8 @@
 // 2. attn_bwd_tc_kernel, persistent: one CTA per SM walks the heads (b, h) assigned to it; for
 //    each head it visits the 128-key tiles jt = nq-1 .. 0, keeps K_jt, V_jt and the dK/dV
 //    accumulators resident and streams the query tiles i = jt .. nq-1 that can see those keys:
+//      TMA warps      K/V per key tile (two stages), Q and lse2 per query tile (three stages),
+//                     dO and delta per query tile (two stages)
 //      MMA thread     S^T = K Q_i^T and dP^T = V dO_i^T (128 x 128 each) into TMEM;
 //                     dV += P^T dO_i and dK += dS^T Q_i with P^T, dS^T read from TMEM;
 //                     dQ_i(partial) = dS K with dS read from shared memory

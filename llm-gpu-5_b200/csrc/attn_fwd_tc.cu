@@ -1,4 +1,5 @@
-// tcgen05 tensor-core causal attention forward for head_dim 64, bf16 operands, fp32 accumulation.
+// tcgen05 tensor-core causal attention forward for head_dim a multiple of 8 up to 64 (64-wide
+// tiles; TMA zero-fills the columns of narrower heads), bf16 operands, fp32 accumulation.
 //
 // Replaces fused_attention_forward_kernel (core/mha_kernels.py:404-521).  A persistent kernel:
 // one CTA per SM walks a static list of work units (below).  Inside a CTA two
