@@ -84,20 +84,19 @@ struct BwdParams {
 
 // Eight lanes per row: lane c of a row reads the row's 16-byte pieces c (O and dO), so a row's 128
 // bytes of each are read by one coalesced request; the partial dot products meet by shuffles.
+// Grid (BH, Tp / 32), 256 threads: a block covers 32 rows of one head, so no thread divides a
+// flat row index.
 __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o,
                                      const __nv_bfloat16* __restrict__ dout,
                                      const float* __restrict__ lse, float* __restrict__ lse2,
                                      float* __restrict__ delta, int NH, int T, int Tp, int D,
-                                     int64_t o_sb, int64_t o_st, int64_t o_sh, int64_t rows) {
-  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t idx = gid >> 3;  // the row (all 8 lanes of a group share it; rows is padded per group)
-  const int c = (int)(gid & 7);
-  const bool live = idx < rows;
-  const int64_t bh = live ? idx / Tp : 0;
-  const int t = live ? (int)(idx % Tp) : 0;
+                                     int64_t o_sb, int64_t o_st, int64_t o_sh) {
+  const int bh = blockIdx.x;
+  const int t = blockIdx.y * 32 + (threadIdx.x >> 3);  // < Tp
+  const int c = threadIdx.x & 7;
   float acc = 0.f;
-  if (live && t < T && c < D / 8) {
-    const int b = (int)(bh / NH), h = (int)(bh % NH);
+  if (t < T && c < D / 8) {
+    const int b = bh / NH, h = bh - b * NH;
     const int64_t off = b * o_sb + (int64_t)t * o_st + (int64_t)h * o_sh;
     const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + off) + c);
     const uint4 g = __ldg(reinterpret_cast<const uint4*>(dout + off) + c);
@@ -113,14 +112,15 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o,
   acc += __shfl_xor_sync(0xffffffffu, acc, 1);
   acc += __shfl_xor_sync(0xffffffffu, acc, 2);
   acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-  if (!live || c != 0) return;
+  if (c != 0) return;
+  const int64_t idx = (int64_t)bh * Tp + t;
   if (t >= T) {
     lse2[idx] = INFINITY;  // padding rows: P = 2^(s - inf) = 0
     delta[idx] = 0.f;
     return;
   }
   delta[idx] = acc;
-  lse2[idx] = lse[bh * T + t] * LOG2E;
+  lse2[idx] = lse[(int64_t)bh * T + t] * LOG2E;
 }
 
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -648,9 +648,12 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   float* lse2 = reinterpret_cast<float*>(w);
   float* delta = reinterpret_cast<float*>(w + align256((size_t)BH * Tp * 4));
   float* dq_acc = reinterpret_cast<float*>(w + 2 * align256((size_t)BH * Tp * 4));
-  const int64_t rows = (int64_t)BH * Tp;
-  attn_bwd_prep_kernel<<<(unsigned)((rows * 8 + 255) / 256), 256, 0, stream>>>(
-      (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, lse2, delta, NH, T, Tp, D, s[3], s[4], s[5], rows);
+  if (Tp / 32 > 65535) {
+    set_error("attn_bwd: T = %d exceeds the backward's limit of 2,097,120", T);
+    return ATTN_ERR_UNSUPPORTED;
+  }
+  attn_bwd_prep_kernel<<<dim3((unsigned)BH, (unsigned)(Tp / 32)), 256, 0, stream>>>(
+      (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, lse2, delta, NH, T, Tp, D, s[3], s[4], s[5]);
   count_launch();
   if (int rc = check_launch("attn_bwd_prep_kernel")) return rc;
 
