@@ -103,6 +103,7 @@ size_t attn_bwd_workspace_size(int B, int NH, int T, int D, int dtype);
  * softmax_fused_backward / matmul_grad_{q,k,v} (core/mha_kernels.py:195-236, 592-680).
  * q, k, v, dq, dk, dv use the input strides; o and dout use the output strides.
  * workspace: device buffer of at least attn_bwd_workspace_size() bytes.
+ * The tensor-core path takes T up to 2,096,896 and returns ATTN_ERR_UNSUPPORTED beyond.
  */
 int attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
              const float* lse, void* dq, void* dk, void* dv,

@@ -648,8 +648,8 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   float* lse2 = reinterpret_cast<float*>(w);
   float* delta = reinterpret_cast<float*>(w + align256((size_t)BH * Tp * 4));
   float* dq_acc = reinterpret_cast<float*>(w + 2 * align256((size_t)BH * Tp * 4));
-  if (Tp / 32 > 65535) {
-    set_error("attn_bwd: T = %d exceeds the backward's limit of 2,097,120", T);
+  if (Tp / 32 > 65535) {  // the prep kernel's grid.y
+    set_error("attn_bwd: T = %d exceeds the tensor-core backward's limit of 2,096,896", T);
     return ATTN_ERR_UNSUPPORTED;
   }
   attn_bwd_prep_kernel<<<dim3((unsigned)BH, (unsigned)(Tp / 32)), 256, 0, stream>>>(
