@@ -70,6 +70,10 @@ def test_bad_arguments_rejected_without_launch():
     rc = L.attn_decode(fake, fake, fake, fake, None, 1, 1, 8, 12, 12, 12, 96, 12, 12, 0.3, 1, fake,
                        1 << 20, None)
     assert rc == -1
+    # the bounded-wait self-test takes limits of 1 us .. 1 s only
+    for limit in (0, -5, 1000001):
+        rc = L.attn_wait_selftest(limit, None)
+        assert rc == -1 and "limit_us" in L.attn_last_error_string().decode()
     assert pkg.launch_count() == before
 
 
