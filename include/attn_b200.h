@@ -56,13 +56,24 @@ uint64_t attn_launch_count(void);
 
 /*
  * Status word of the tensor-core kernels on the current device: 0, or the code of a bounded
- * wait inside a kernel that gave up (the kernel then skipped its remaining work and returned
- * instead of hanging).  Codes are grouped by kernel: 1xx the GEMM, 2xx the attention forward,
- * 3xx the attention backward (300: its dynamic shared memory did not start 1024-byte aligned,
- * checked before any work), 900 the self-test below.  Synchronises with the device.
- * clear != 0 resets it to 0.
+ * wait inside a kernel that gave up (that launch then skipped its remaining work and returned
+ * instead of hanging, so its outputs are incomplete).  Codes are grouped by kernel: 1xx the GEMM,
+ * 2xx the attention forward, 3xx the attention backward (300: its dynamic shared memory did not
+ * start 1024-byte aligned, checked before any work), 900 the self-test below.  The word keeps the
+ * first code until it is cleared; a set word does not affect later launches (each launch only
+ * stops early for a wait of its own that gave up).  Synchronises with the device.
+ * clear != 0 resets it to 0.  Has no counterpart in the reference, whose kernels cannot give up.
+ * (Replaces the launch-failure exceptions PyCUDA raises, model/gpt.py:649-650 for the module.)
  */
 int attn_device_error(int clear);
+
+/*
+ * Enqueue on `stream` a copy of the status word into *host_dst (pinned host memory, so that the
+ * copy is asynchronous), without synchronising.  Once the stream has passed the copy, *host_dst
+ * holds the word as it stood after every kernel enqueued before it.  The Python modules use it to
+ * raise AttnError at their next call without a per-call synchronisation.
+ */
+int attn_device_error_async(int* host_dst, void* stream);
 
 /* The code attn_wait_selftest leaves in the device error word. */
 #define ATTN_SELFTEST_SITE 900
@@ -103,7 +114,8 @@ size_t attn_bwd_workspace_size(int B, int NH, int T, int D, int dtype);
  * softmax_fused_backward / matmul_grad_{q,k,v} (core/mha_kernels.py:195-236, 592-680).
  * q, k, v, dq, dk, dv use the input strides; o and dout use the output strides.
  * workspace: device buffer of at least attn_bwd_workspace_size() bytes.
- * The tensor-core path takes T up to 2,096,896 and returns ATTN_ERR_UNSUPPORTED beyond.
+ * The tensor-core path takes T up to 2,097,024; longer rows run the CUDA-core backward, whose
+ * workspace attn_bwd_workspace_size() then sizes.
  */
 int attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
              const float* lse, void* dq, void* dk, void* dv,
@@ -133,6 +145,8 @@ size_t attn_decode_workspace_size(int B, int NH, int L, int D);
  * GenerationSession.generate re-runs per token (generate.py:611-628).
  * q, o: element (b, h, d) at ptr[b*q_sb + h*q_sh + d].  K/V cache: element (b, l, h, d) at
  * ptr[b*kv_sb + l*kv_sl + h*kv_sh + d].  lse may be NULL.  Split over L, then combined.
+ * B*NH (one grid row per sequence and head) is at most 65535; beyond it the call returns
+ * ATTN_ERR_UNSUPPORTED without launching.
  */
 int attn_decode(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
                 int B, int NH, int L, int D,
@@ -151,10 +165,13 @@ int attn_decode(const void* q, const void* k_cache, const void* v_cache, void* o
  * B*NH*ceil(L/256)*(D+2) > 1,048,576 (e.g. B=64, NH=8, L=2048, D=64 needs 270,336), are rejected
  * with ATTN_ERR_UNSUPPORTED and a message; nothing is launched.
  * The first call on each device resolves the array's device address (cudaGetSymbolAddress, with
- * that device current); make that first call before any stream capture.  Every call shares the
- * array and it keeps the last call's contents (each call writes every partial state before reading
- * it, so nothing needs zeroing); calls that overlap on the GPU (concurrent streams or threads)
- * race on the array and must be serialised by the caller.  Arguments otherwise as attn_decode.
+ * that device current); make that first call before any stream capture.  The address is resolved
+ * again when the device's CUDA context changes (after a cudaDeviceReset the module reloads and the
+ * array may move); that call too must come before any capture.  B*NH is at most 65535, as for
+ * attn_decode.  Every call shares the array and it keeps the last call's contents (each call
+ * writes every partial state before reading it, so nothing needs zeroing); calls that overlap on
+ * the GPU (concurrent streams or threads) race on the array and must be serialised by the caller.
+ * Arguments otherwise as attn_decode.
  */
 int attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
                         int B, int NH, int L, int D,

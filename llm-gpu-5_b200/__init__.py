@@ -9,11 +9,11 @@ Import by name (the directory name is not an identifier):
 All compute runs in ``libattn_b200.so`` (C ABI: ``include/attn_b200.h``); importing fails if the
 library has not been built.
 """
-from ._lib import AttnError, LIB_PATH, launch_count, lib  # noqa: F401  (fails loudly if unbuilt)
+from ._lib import AttnError, DeviceWaitError, LIB_PATH, clear_device_error, launch_count, lib  # noqa: F401  (fails loudly if unbuilt)
 from . import dp, mha_ops  # noqa: F401
 from .mha import DeviceBuffer, GPTConfig, KVCache, MultiHeadAttention, Parameter  # noqa: F401
 from .ffn import FeedForward  # noqa: F401
 from .mha_ops import get_shared_mha_module, THREADS_PER_BLOCK, SOFTMAX_BLOCK_THREADS  # noqa: F401
 
-__all__ = ["MultiHeadAttention", "FeedForward", "GPTConfig", "Parameter", "DeviceBuffer", "KVCache", "mha_ops", "dp", "AttnError",
+__all__ = ["MultiHeadAttention", "FeedForward", "GPTConfig", "Parameter", "DeviceBuffer", "KVCache", "mha_ops", "dp", "AttnError", "DeviceWaitError", "clear_device_error",
            "get_shared_mha_module", "launch_count"]

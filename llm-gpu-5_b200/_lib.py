@@ -36,6 +36,7 @@ SIGNATURES = {
     "attn_last_error_string": (ctypes.c_char_p, []),
     "attn_launch_count": (ctypes.c_uint64, []),
     "attn_device_error": (_i, [_i]),
+    "attn_device_error_async": (_i, [_p, _p]),
     "attn_wait_selftest": (_i, [_i, _p]),
     "attn_fwd": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i, _p]),
     "attn_bwd_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
@@ -99,3 +100,61 @@ def call(name, *args):
 
 def launch_count() -> int:
     return int(lib.attn_launch_count())
+
+
+# ---------------------------------------------------------------- device status word
+# A bounded wait inside a tensor-core kernel that gives up leaves a site code in the library's
+# device status word (attn_device_error) and that launch's outputs incomplete.  The modules watch
+# the word without synchronising: after each call they enqueue a copy of it into pinned host
+# memory (attn_device_error_async), and at the start of the next call they read that memory and
+# raise DeviceWaitError if it is set.  The word keeps its code until clear_device_error().
+_watch = {}  # device index -> pinned int32 host tensor holding the last copy of the word
+
+
+class DeviceWaitError(AttnError):
+    """A bounded wait inside one of the library's kernels gave up: some call's outputs are
+    incomplete.  The reference raises on a failed launch (PyCUDA's LaunchError); this is its
+    counterpart for a kernel that gave up instead of hanging."""
+
+    def __init__(self, site):
+        RuntimeError.__init__(self, f"a bounded wait in a tensor-core kernel gave up (site {site}); the "
+                              "outputs of a recent call are incomplete.  clear_device_error() resets the status")
+        self.code = ATTN_ERR_CUDA
+        self.site = site
+
+
+def _slot():
+    import torch
+    dev = torch.cuda.current_device()
+    buf = _watch.get(dev)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        _watch[dev] = buf
+    return buf
+
+
+def watch_device_error():
+    """Enqueue, on the current stream, a copy of the device status word into pinned memory."""
+    import torch
+    call("attn_device_error_async", _slot().data_ptr(), torch.cuda.current_stream().cuda_stream)
+
+
+def check_device_error():
+    """Raise DeviceWaitError if the last copy of the status word that has landed shows a code."""
+    import torch
+    buf = _watch.get(torch.cuda.current_device())
+    if buf is not None:
+        site = int(buf[0])
+        if site:
+            raise DeviceWaitError(site)
+
+
+def clear_device_error() -> int:
+    """Wait for the device, read and clear its status word; returns the code it held."""
+    import torch
+    torch.cuda.synchronize()
+    site = lib.attn_device_error(1)
+    buf = _watch.get(torch.cuda.current_device())
+    if buf is not None:
+        buf.zero_()
+    return site

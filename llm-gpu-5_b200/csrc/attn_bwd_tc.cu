@@ -162,8 +162,9 @@ __device__ __forceinline__ void store_packed_row(__nv_bfloat16* dst, const uint3
 __global__ void __launch_bounds__(BA_THREADS, 1)
 attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const WaitErr werr = wait_err(p.err);
   if (smem_u32(smem_raw) & 1023u) {  // the swizzled tiles need it; uniform, so every thread leaves
-    if (threadIdx.x == 0) atomicCAS(p.err, 0, BA_SITE_SMEM_ALIGN);
+    if (threadIdx.x == 0) record_wait_error(werr, BA_SITE_SMEM_ALIGN);
     return;
   }
   uint8_t* smem = smem_raw;
@@ -249,7 +250,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           const int b = bh / p.NH, h = bh % p.NH;
           for (int jt = nq - 1; jt >= 0; --jt, ++u) {
             const int ks = u & 1;
-            if (!mbar_wait(&kv_empty[ks], ((u >> 1) & 1) ^ 1, p.err, 301)) { ok = false; break; }
+            if (!mbar_wait(&kv_empty[ks], ((u >> 1) & 1) ^ 1, werr, 301)) { ok = false; break; }
             mbar_arrive_expect_tx(&kv_full[ks], 2 * AT_TILE_BYTES);
             load_tile(sK + ks * AT_TILE_BYTES, maps.k, &kv_full[ks], b, h, jt * AT_TILE);
             load_tile(sV + ks * AT_TILE_BYTES, maps.v, &kv_full[ks], b, h, jt * AT_TILE);
@@ -276,7 +277,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           for (int jt = nq - 1; jt >= 0 && ok; --jt) {
             for (int i = jt; i < nq; ++i, ++n) {
               const int s = n % nst;
-              if (!mbar_wait(&empty[s], ((n / nst) & 1) ^ 1, p.err, isq ? 302 : 318)) { ok = false; break; }
+              if (!mbar_wait(&empty[s], ((n / nst) & 1) ^ 1, werr, isq ? 302 : 318)) { ok = false; break; }
               const int q0 = i * AT_TILE;
               mbar_arrive_expect_tx(&full[s], AT_TILE_BYTES + AT_TILE * 4);
               load_tile(tiles + s * AT_TILE_BYTES, map, &full[s], b, h, q0);
@@ -306,14 +307,14 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
         bool pfirst = false, plast = false;
         auto finish_dvdk = [&]() -> bool {
           // dV += P^T dO   (the first tile of a key tile starts dV/dK afresh once they are drained)
-          if (pfirst && !mbar_wait(dkdv_free, (pu & 1) ^ 1, p.err, 308)) return false;
+          if (pfirst && !mbar_wait(dkdv_free, (pu & 1) ^ 1, werr, 308)) return false;
           tc_fence_after();
           const uint64_t do_mn = mnmaj(sDO + pso * AT_TILE_BYTES);
   #pragma unroll
           for (int k = 0; k < AT_TILE / 16; ++k)
             umma_ts(tdV, tP + k * 8, desc_step(do_mn, k * 2048), idesc_kv, (pfirst && k == 0) ? 0u : 1u);
           umma_commit(dv_done);
-          if (!mbar_wait(ds_ready, pn & 1, p.err, 303)) return false;
+          if (!mbar_wait(ds_ready, pn & 1, werr, 303)) return false;
           tc_fence_after();
           const uint64_t q_mn = mnmaj(sQ + ps * AT_TILE_BYTES);
   #pragma unroll
@@ -326,7 +327,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           return true;
         };
         auto finish_dq = [&]() -> bool {
-          if (!mbar_wait(dq_free, (pn & 1) ^ 1, p.err, 304)) return false;
+          if (!mbar_wait(dq_free, (pn & 1) ^ 1, werr, 304)) return false;
           tc_fence_after();
           const uint64_t k_mn = mnmaj(sK + pks * AT_TILE_BYTES);
           const uint64_t ds_mn = smem_desc_sw128(smem_u32(sDS + (pn & 1) * 2 * AT_TILE_BYTES), 16384, 1024);
@@ -346,13 +347,13 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
         for (int bh = blockIdx.x; bh < p.BH && ok; bh += gridDim.x) {
           for (int jt = nq - 1; jt >= 0 && ok; --jt, ++u) {
             const int ks = u & 1;
-            if (!mbar_wait(&kv_full[ks], (u >> 1) & 1, p.err, 305)) { ok = false; break; }
+            if (!mbar_wait(&kv_full[ks], (u >> 1) & 1, werr, 305)) { ok = false; break; }
             const uint64_t k_k = kmaj(sK + ks * AT_TILE_BYTES), v_k = kmaj(sV + ks * AT_TILE_BYTES);
             for (int i = jt; i < nq; ++i, ++n) {
               const int s = n % BA_QS, so = n % BA_OS;
-              if (!mbar_wait(&q_full[s], (n / BA_QS) & 1, p.err, 306)) { ok = false; break; }
+              if (!mbar_wait(&q_full[s], (n / BA_QS) & 1, werr, 306)) { ok = false; break; }
               // S^T = K Q^T once the P/dS warps have read the previous S^T (and written its P^T)
-              if (pn >= 0 && !mbar_wait(p_ready, pn & 1, p.err, 309)) { ok = false; break; }
+              if (pn >= 0 && !mbar_wait(p_ready, pn & 1, werr, 309)) { ok = false; break; }
               tc_fence_after();
               const uint64_t q_k = kmaj(sQ + s * AT_TILE_BYTES), do_k = kmaj(sDO + so * AT_TILE_BYTES);
   #pragma unroll
@@ -361,8 +362,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
               umma_commit(s_full);
               if (pn >= 0 && !finish_dvdk()) { ok = false; break; }
               // dP^T = V dO^T over the previous dS^T: wait for the dK MMA that reads it
-              if (!mbar_wait(dk_done, (n & 1) ^ 1, p.err, 307)) { ok = false; break; }
-              if (!mbar_wait(&o_full[so], (n / BA_OS) & 1, p.err, 319)) { ok = false; break; }
+              if (!mbar_wait(dk_done, (n & 1) ^ 1, werr, 307)) { ok = false; break; }
+              if (!mbar_wait(&o_full[so], (n / BA_OS) & 1, werr, 319)) { ok = false; break; }
               tc_fence_after();
   #pragma unroll
               for (int k = 0; k < AT_D / 16; ++k)
@@ -379,7 +380,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
             }
           }
         }
-        if (ok && pn >= 0 && mbar_wait(p_ready, pn & 1, p.err, 309) && finish_dvdk()) finish_dq();
+        if (ok && pn >= 0 && mbar_wait(p_ready, pn & 1, werr, 309) && finish_dvdk()) finish_dq();
       }
     }
   } else if (warp < 12) {
@@ -399,8 +400,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
       for (int jt = nq - 1; jt >= 0 && ok; --jt) {
         for (int i = jt; i < nq; ++i, ++n) {
           const int s = n % BA_QS;
-          ok = __all_sync(0xffffffffu, mbar_wait(s_full, n & 1, p.err, 310) &&
-                                           mbar_wait(&q_full[s], (n / BA_QS) & 1, p.err, 311));
+          ok = __all_sync(0xffffffffu, mbar_wait(s_full, n & 1, werr, 310) &&
+                                           mbar_wait(&q_full[s], (n / BA_QS) & 1, werr, 311));
           if (!ok) break;
           tc_fence_after();
           const bool diag = (i == jt);  // key r is visible to query q iff r <= q
@@ -432,7 +433,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
             }
           }
           // the P^T columns are rewritten once the previous tile's dV MMA has read them
-          ok = __all_sync(0xffffffffu, mbar_wait(dv_done, (n & 1) ^ 1, p.err, 312));
+          ok = __all_sync(0xffffffffu, mbar_wait(dv_done, (n & 1) ^ 1, werr, 312));
           if (!ok) break;
           tc_fence_after();
           tmem_st16(tP, *reinterpret_cast<const uint32_t(*)[16]>(pw));
@@ -442,9 +443,9 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           mbar_arrive(p_ready);
           // ---- dS^T = P^T (dP^T - delta)
           const int so = n % BA_OS;
-          ok = __all_sync(0xffffffffu, mbar_wait(dp_full, n & 1, p.err, 313) &&
-                                           mbar_wait(&o_full[so], (n / BA_OS) & 1, p.err, 320) &&
-                                           mbar_wait(&ds_free[n & 1], ((n >> 1) & 1) ^ 1, p.err, 314));
+          ok = __all_sync(0xffffffffu, mbar_wait(dp_full, n & 1, werr, 313) &&
+                                           mbar_wait(&o_full[so], (n / BA_OS) & 1, werr, 320) &&
+                                           mbar_wait(&ds_free[n & 1], ((n >> 1) & 1) ^ 1, werr, 314));
           uint8_t* dsrow = sDS + (n & 1) * 2 * AT_TILE_BYTES + g * AT_TILE_BYTES + r * 128;
           if (!ok) break;
           tc_fence_after();
@@ -495,7 +496,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
     uint32_t sync_phase = 0;
     auto drain_sync = [&]() -> bool {
       mbar_arrive(drain_bar);
-      const bool w = mbar_wait(drain_bar, sync_phase & 1, p.err, 315);
+      const bool w = mbar_wait(drain_bar, sync_phase & 1, werr, 315);
       ++sync_phase;
       return __all_sync(0xffffffffu, w);
     };
@@ -508,7 +509,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
           if (i == nq - 1) {
             // key tile jt done: dV and scale * dK out first (committed together with this
             // tile's dQ), so the next key tile can start accumulating while dQ is drained
-            ok = __all_sync(0xffffffffu, mbar_wait(dkdv_full, u & 1, p.err, 317));
+            ok = __all_sync(0xffffffffu, mbar_wait(dkdv_full, u & 1, werr, 317));
             if (!ok) break;
             tc_fence_after();
             // dV packed to bf16 first, then dK, so at most 64 fp32 values are live
@@ -537,7 +538,7 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
               store_packed_row(p.dk + off, pkk, p.D);
             }
           }
-          ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, p.err, 316));
+          ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, werr, 316));
           if (!ok) break;
           tc_fence_after();
           uint32_t a0[32], a1[32];
@@ -617,7 +618,13 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
 // ==========================================================================================
 // host side
 // ==========================================================================================
-bool tc_bwd_supported(int D, int dtype) { return tc_head_dim_ok(D) && dtype == ATTN_BF16; }
+// The prep kernel's grid has T/32 rows in y (at most 65535), so the tensor-core backward takes T up
+// to 16383 tiles of 128 rows; attn_bwd sends longer rows to the CUDA-core backward.
+constexpr int kBwdTcMaxT = (65535 * 32 / AT_TILE) * AT_TILE;  // 2,097,024
+
+bool tc_bwd_supported(int D, int T, int dtype) {
+  return tc_head_dim_ok(D) && dtype == ATTN_BF16 && T <= kBwdTcMaxT;
+}
 
 static int bwd_grid(int BH) { return BH < BA_MAX_CTAS ? BH : BA_MAX_CTAS; }
 
@@ -648,8 +655,8 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   float* lse2 = reinterpret_cast<float*>(w);
   float* delta = reinterpret_cast<float*>(w + align256((size_t)BH * Tp * 4));
   float* dq_acc = reinterpret_cast<float*>(w + 2 * align256((size_t)BH * Tp * 4));
-  if (Tp / 32 > 65535) {  // the prep kernel's grid.y
-    set_error("attn_bwd: T = %d exceeds the tensor-core backward's limit of 2,096,896", T);
+  if (T > kBwdTcMaxT) {  // the prep kernel's grid.y; attn_bwd routes such rows elsewhere first
+    set_error("attn_bwd: T = %d exceeds the tensor-core backward's limit of %d", T, kBwdTcMaxT);
     return ATTN_ERR_UNSUPPORTED;
   }
   attn_bwd_prep_kernel<<<dim3((unsigned)BH, (unsigned)(Tp / 32)), 256, 0, stream>>>(
@@ -689,7 +696,7 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   p.sh = s[2];
   p.err = dev_error_ptr();
   if (!p.err) return ATTN_ERR_CUDA;
-  static uint64_t attr_done = 0;
+  static CtxOnce attr_done;
   if (!set_smem_limit_once(attn_bwd_tc_kernel, BA_SMEM, attr_done)) return ATTN_ERR_CUDA;
   static int launch_regs = 0;
   if (!launch_regs_match(attn_bwd_tc_kernel, BA_LAUNCH_REGS, launch_regs, "attn_bwd_tc_kernel")) return ATTN_ERR_CUDA;

@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   using TileWalk = attn::TileWalk<SINGLES>;
   extern __shared__ uint8_t smem_raw[];
+  const WaitErr werr = wait_err(p.err);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   StreamBars* sbars = reinterpret_cast<StreamBars*>(smem + 2 * FA_STREAM_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbars + 2);
@@ -164,7 +165,7 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
         }
         auto load_q = [&](const TileWalk& c, int it) -> bool {
           const int qs = it & 1;
-          if (!mbar_wait(&sb.q_empty[qs], ((it >> 1) & 1) ^ 1, p.err, 201)) return false;
+          if (!mbar_wait(&sb.q_empty[qs], ((it >> 1) & 1) ^ 1, werr, 201)) return false;
           mbar_arrive_expect_tx(&sb.q_full[qs], AT_TILE_BYTES);
           load_tile(sQ + qs * AT_TILE_BYTES, maps.q, &sb.q_full[qs], c.bh / p.NH, c.bh % p.NH, c.t * AT_TILE);
           return true;
@@ -179,10 +180,10 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
           const int b = cur.bh / p.NH, h = cur.bh % p.NH;
           for (int j = 0; j <= cur.t && ok; ++j, ++kg, ++vg) {
             const int ks = kg & 1, vs = vg & 1;
-            if (!mbar_wait(&sb.k_empty[ks], ((kg >> 1) & 1) ^ 1, p.err, 202)) { ok = false; break; }
+            if (!mbar_wait(&sb.k_empty[ks], ((kg >> 1) & 1) ^ 1, werr, 202)) { ok = false; break; }
             mbar_arrive_expect_tx(&sb.k_full[ks], AT_TILE_BYTES);
             load_tile(sK + ks * AT_TILE_BYTES, maps.k, &sb.k_full[ks], b, h, j * AT_TILE);
-            if (!mbar_wait(&sb.v_empty[vs], ((vg >> 1) & 1) ^ 1, p.err, 212)) { ok = false; break; }
+            if (!mbar_wait(&sb.v_empty[vs], ((vg >> 1) & 1) ^ 1, werr, 212)) { ok = false; break; }
             mbar_arrive_expect_tx(&sb.v_full[vs], AT_TILE_BYTES);
             load_tile(sV + vs * AT_TILE_BYTES, maps.v, &sb.v_full[vs], b, h, j * AT_TILE);
             // the next tile's Q, as soon as this tile's first block is on its way
@@ -206,14 +207,14 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
         TileWalk cur;
         for (cur.start(p, X); ok && cur.valid(p); cur.next(p, X), ++it) {
           const int qs = it & 1;
-          if (!mbar_wait(&sb.q_full[qs], (it >> 1) & 1, p.err, 203)) { ok = false; break; }
+          if (!mbar_wait(&sb.q_full[qs], (it >> 1) & 1, werr, 203)) { ok = false; break; }
           const uint64_t q_desc = smem_desc_sw128(smem_u32(sQ + qs * AT_TILE_BYTES), 16, 1024);
           for (int j = 0; j <= cur.t + 1 && ok; ++j) {
             if (j <= cur.t) {
               // S(j) = Q K_j^T once softmax has loaded S(j-1)
               const int ks = kg & 1;
-              if (!mbar_wait(&sb.k_full[ks], (kg >> 1) & 1, p.err, 204)) { ok = false; break; }
-              if (scnt > 0 && !mbar_wait(&sb.s_free, (scnt - 1) & 1, p.err, 206)) { ok = false; break; }
+              if (!mbar_wait(&sb.k_full[ks], (kg >> 1) & 1, werr, 204)) { ok = false; break; }
+              if (scnt > 0 && !mbar_wait(&sb.s_free, (scnt - 1) & 1, werr, 206)) { ok = false; break; }
               tc_fence_after();
               const uint64_t k_desc = smem_desc_sw128(smem_u32(sK + ks * AT_TILE_BYTES), 16, 1024);
 #pragma unroll
@@ -228,8 +229,8 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
             if (j > 0) {
               // O += P(j-1) V_{j-1} once softmax has written P(j-1) (and rescaled O)
               const int vs = vg & 1;
-              if (!mbar_wait(&sb.v_full[vs], (vg >> 1) & 1, p.err, 205)) { ok = false; break; }
-              if (!mbar_wait(&sb.p_ready, pcnt & 1, p.err, 211)) { ok = false; break; }
+              if (!mbar_wait(&sb.v_full[vs], (vg >> 1) & 1, werr, 205)) { ok = false; break; }
+              if (!mbar_wait(&sb.p_ready, pcnt & 1, werr, 211)) { ok = false; break; }
               tc_fence_after();
               const uint64_t v_desc = smem_desc_sw128(smem_u32(sV + vs * AT_TILE_BYTES), 8192, 1024);
 #pragma unroll
@@ -263,7 +264,7 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
     uint32_t wg_phase = 0;
     auto wg_sync = [&]() -> bool {  // bounded barrier over the 128 threads of the warpgroup
       mbar_arrive(&sb.wg_bar);
-      const bool w = mbar_wait(&sb.wg_bar, wg_phase & 1, p.err, 210);
+      const bool w = mbar_wait(&sb.wg_bar, wg_phase & 1, werr, 210);
       ++wg_phase;
       return __all_sync(0xffffffffu, w);
     };
@@ -273,7 +274,7 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j <= t; ++j, ++c) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&sb.s_full, c & 1, p.err, 207))) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(&sb.s_full, c & 1, werr, 207))) { ok = false; break; }
         tc_fence_after();
         uint32_t sr[128];
         tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(sr));
@@ -319,7 +320,7 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
           pk[i / 2 + 1] = pack_bf16x2(a2, a3);
         }
         // P and O are rewritten once the previous step's P V has completed
-        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&sb.pv_done, (c - 1) & 1, p.err, 208))) { ok = false; break; }
+        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&sb.pv_done, (c - 1) & 1, werr, 208))) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) tmem_st16(tP + cc * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * cc));
@@ -341,7 +342,7 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       }
       if (!ok) break;
       // epilogue: O / l -> bf16 rows, lse = (m + log2 l) * ln 2
-      if (!__all_sync(0xffffffffu, mbar_wait(&sb.pv_done, (c - 1) & 1, p.err, 209))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sb.pv_done, (c - 1) & 1, werr, 209))) break;
       tc_fence_after();
       uint32_t o[64];
       tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
@@ -425,7 +426,7 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   const bool singles = (int64_t)p.BH * p.npairs < (int64_t)8 * 2 * sms;
   const int64_t units = (int64_t)p.BH * (singles ? p.nq : p.npairs);
   const int grid = (int)((units + 1) / 2 < sms ? (units + 1) / 2 : sms);  // at least a unit per stream
-  static uint64_t attr_pairs = 0, attr_singles = 0;
+  static CtxOnce attr_pairs, attr_singles;
   static int regs_pairs = 0, regs_singles = 0;
   if (singles) {
     if (!set_smem_limit_once(attn_fwd_tc_kernel<true>, FA_SMEM, attr_singles) ||

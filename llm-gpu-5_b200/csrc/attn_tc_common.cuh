@@ -82,19 +82,26 @@ inline int current_device_sms() {
   return n;
 }
 
-// Raise a kernel's dynamic shared-memory limit once per device; `done` holds one bit per device.
+// Per-device record of the CUDA context in which a one-time set-up step was done: a function
+// attribute belongs to the module loaded in a context, so the step is redone in a new context
+// (after a cudaDeviceReset).
+struct CtxOnce {
+  void* ctx[64] = {};
+};
+
+// Raise a kernel's dynamic shared-memory limit once per device and context.
 template <typename Kernel>
-inline bool set_smem_limit_once(Kernel kernel, int bytes, uint64_t& done) {
+inline bool set_smem_limit_once(Kernel kernel, int bytes, CtxOnce& done) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  const uint64_t bit = 1ull << (dev & 63);
-  if (done & bit) return true;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  void* ctx = current_context();
+  if (ctx && done.ctx[dev] == ctx) return true;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) {
     set_error("cudaFuncSetAttribute(MaxDynamicSharedMemorySize=%d) failed: %s", bytes, cudaGetErrorString(e));
     return false;
   }
-  done |= bit;
+  done.ctx[dev] = current_context();
   return true;
 }
 

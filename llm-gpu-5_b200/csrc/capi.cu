@@ -8,6 +8,7 @@
 #include "tc_common.cuh"
 
 #include <atomic>
+#include <mutex>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -37,26 +38,55 @@ int check_launch(const char* what) {
   return ATTN_OK;
 }
 
-// ---- device error word of the tensor-core kernels' bounded waits ---------------------------
-static __device__ int g_dev_error;
-static int* g_dev_error_ptr[64];
+// ---- CUDA context of the calling thread (driver API through the runtime's entry point) --------
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 
-int* dev_error_ptr() {
+void* current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  CUcontext c = nullptr;
+  if (fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+static std::mutex g_symbol_mu;
+
+void* device_symbol_address(SymbolCache& cache, const void* symbol, const char* what) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    set_error("cudaGetDevice failed");
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("%s: cudaGetDevice failed: %s", what, cudaGetErrorString(e));
     return nullptr;
   }
-  if (!g_dev_error_ptr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_dev_error);
-    if (e != cudaSuccess) {
-      set_error("cudaGetSymbolAddress(error word) failed: %s", cudaGetErrorString(e));
-      return nullptr;
-    }
-    g_dev_error_ptr[dev] = static_cast<int*>(p);
+  std::lock_guard<std::mutex> lock(g_symbol_mu);
+  void* ctx = current_context();
+  if (cache.ptr[dev] && ctx && cache.ctx[dev] == ctx) return cache.ptr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, symbol);  // creates the primary context if there is none yet
+  if (e != cudaSuccess || p == nullptr) {
+    set_error("%s: cudaGetSymbolAddress failed on device %d: %s", what, dev, cudaGetErrorString(e));
+    return nullptr;
   }
-  return g_dev_error_ptr[dev];
+  cache.ctx[dev] = current_context();
+  cache.ptr[dev] = p;
+  return p;
+}
+
+// ---- device error word pair of the tensor-core kernels' bounded waits ------------------------
+// [0]: site code of the first wait that gave up since the last clear; [1]: give-ups, ever.
+static __device__ int g_dev_error[2];
+static SymbolCache g_dev_error_cache;
+
+int* dev_error_ptr() {
+  return static_cast<int*>(device_symbol_address(g_dev_error_cache, (const void*)&g_dev_error,
+                                                 "device error word"));
 }
 
 // ---- TMA tensor maps through the driver entry point (no libcuda link dependency) ----------
@@ -143,6 +173,7 @@ int cast_colsum(const float*, int64_t, int, int, void*, int64_t, float*, int, vo
 int attn_probs_launch(const void*, const void*, const float*, float*, int, int, int, int, int64_t,
                       int64_t, int64_t, float, int, cudaStream_t);
 size_t decode_ws(int, int, int, int);
+int decode_grid_check(int, int, const char*);
 int wait_selftest(int, cudaStream_t);
 int decode(const void*, const void*, const void*, void*, float*, int, int, int, int, int64_t,
            int64_t, int64_t, int64_t, int64_t, float, int, float*, cudaStream_t);
@@ -150,7 +181,7 @@ bool tc_fwd_supported(int D, int dtype);
 bool tc_attn_layout_ok(const void* const* ptrs, int n, const int64_t* s, int D);
 int attn_fwd_tc(const void*, const void*, const void*, void*, float*, int, int, int, int,
                 const int64_t*, float, cudaStream_t);
-bool tc_bwd_supported(int D, int dtype);
+bool tc_bwd_supported(int D, int T, int dtype);
 size_t attn_bwd_tc_ws(int B, int NH, int T, int D);
 int attn_bwd_tc(const void*, const void*, const void*, const void*, const void*, const float*,
                 void*, void*, void*, void*, int, int, int, int, const int64_t*, float,
@@ -192,15 +223,25 @@ const char* attn_last_error_string(void) { return g_last_error.c_str(); }
 uint64_t attn_launch_count(void) { return g_launches.load(); }
 
 int attn_device_error(int clear) {
+  clear_error();
   int* p = dev_error_ptr();
   if (!p) return ATTN_ERR_CUDA;
   int v = 0;
-  if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return ATTN_ERR_CUDA;
+  ATTN_CUDA_TRY(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
   if (clear && v) {
     const int z = 0;
-    cudaMemcpy(p, &z, sizeof(int), cudaMemcpyHostToDevice);
+    ATTN_CUDA_TRY(cudaMemcpy(p, &z, sizeof(int), cudaMemcpyHostToDevice));
   }
   return v;
+}
+
+int attn_device_error_async(int* host_dst, void* stream) {
+  clear_error();
+  ATTN_REQUIRE(host_dst, "attn_device_error_async: null destination");
+  int* p = dev_error_ptr();
+  if (!p) return ATTN_ERR_CUDA;
+  ATTN_CUDA_TRY(cudaMemcpyAsync(host_dst, p, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream)));
+  return ATTN_OK;
 }
 
 int attn_wait_selftest(int limit_us, void* stream) {
@@ -229,7 +270,7 @@ int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, i
 size_t attn_bwd_workspace_size(int B, int NH, int T, int D, int dtype) {
   if (B <= 0 || NH <= 0 || T <= 0 || D <= 0) return 0;
   size_t ws = (size_t)B * NH * T * sizeof(float);  // delta = rowsum(dO * O)
-  if (tc_bwd_supported(D, dtype)) ws = attn_bwd_tc_ws(B, NH, T, D);
+  if (tc_bwd_supported(D, T, dtype)) ws = attn_bwd_tc_ws(B, NH, T, D);
   return ws;
 }
 
@@ -255,7 +296,7 @@ int attn_bwd(const void* q, const void* k, const void* v, const void* o, const v
                "attn_bwd: tensors must be %zu-byte aligned", a);
   const void* tens[8] = {q, k, v, o, dout, dq, dk, dv};
   // the tensor-core workspace (attn_bwd_workspace_size) also covers the CUDA-core path
-  if (tc_bwd_supported(D, dtype) && tc_attn_layout_ok(tens, 8, st, D))
+  if (tc_bwd_supported(D, T, dtype) && tc_attn_layout_ok(tens, 8, st, D))
     return attn_bwd_tc(q, k, v, o, dout, lse, dq, dk, dv, workspace, B, NH, T, D, st, scale,
                        as_stream(stream));
   return attn_bwd_simt(q, k, v, o, dout, lse, dq, dk, dv, (float*)workspace, B, NH, T, D, st, scale,
@@ -294,6 +335,7 @@ int attn_decode(const void* q, const void* k_cache, const void* v_cache, void* o
     ATTN_REQUIRE(st[i] >= 0 && st[i] % vec == 0, "attn_decode: strides must be multiples of %d", vec);
   ATTN_REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(o, 4),
                "attn_decode: q/k/v must be 16-byte aligned");
+  if (int rc = decode_grid_check(B, NH, "attn_decode")) return rc;
   const size_t need = decode_ws(B, NH, L, D);
   if (!workspace || workspace_bytes < need) {
     set_error("attn_decode: workspace of %zu bytes required", need);

@@ -10,7 +10,7 @@
 // Lane layout: a key row of D elements is read by LPK = D / EPL lanes, each loading one 16-byte
 // vector (EPL = 8 bf16 or 4 fp32 elements); a warp therefore reads KPW = 32 / LPK keys per step,
 // each lane group keeps its own online-softmax state, and the states are merged at the end.
-#include "common.cuh"
+#include "tc_common.cuh"
 #include <math.h>
 
 namespace attn {
@@ -22,6 +22,16 @@ static int decode_splits(int L) { return (L + DEC_CHUNK - 1) / DEC_CHUNK; }
 
 size_t decode_ws(int B, int NH, int L, int D) {
   return (size_t)B * NH * decode_splits(L) * (D + 2) * sizeof(float);
+}
+
+// The partial kernel runs one grid row per (b, h): B*NH is its grid.y, at most 65535.
+int decode_grid_check(int B, int NH, const char* fn) {
+  if ((int64_t)B * NH > 65535) {
+    set_error("%s: B*NH = %lld (sequences x heads) exceeds the decode kernel's limit of 65535; split the "
+              "batch into several calls", fn, (long long)B * NH);
+    return ATTN_ERR_UNSUPPORTED;
+  }
+  return ATTN_OK;
 }
 
 template <typename T> struct Vec16;
@@ -200,38 +210,17 @@ int decode(const void* q, const void* k, const void* v, void* o, float* lse, int
 // FFI callers that hold only the q/K/V/o pointers.  For them the per-split partial softmax
 // states live in this file-scope array, sized once at load time; every GPU that loads the
 // library holds it until the process exits.
-#include <mutex>
-
 namespace attn {
 
 constexpr size_t kNoAllocDecodeFloats = size_t(1) << 20;  // 4 MiB
 static __device__ __align__(256) float g_decode_scratch[kNoAllocDecodeFloats];
+static SymbolCache g_decode_scratch_cache;
 
-static std::mutex g_decode_scratch_mu;
-static float* g_decode_scratch_dev[64];  // device address of the array, per device
-
-// Resolve the array's device address on the current device (first call per device only).
-// In host code `g_decode_scratch` names a host-side stand-in, not device memory, so the address
-// must come from cudaGetSymbolAddress with the device current.
+// The array's device address on the current device, resolved on the first call per device (and
+// again if the device's CUDA context changes, since the module then reloads).
 static float* decode_scratch_address() {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    set_error("attn_decode_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(e));
-    return nullptr;
-  }
-  std::lock_guard<std::mutex> lock(g_decode_scratch_mu);
-  if (!g_decode_scratch_dev[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      set_error("attn_decode_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-                cudaGetErrorString(e));
-      return nullptr;
-    }
-    g_decode_scratch_dev[dev] = static_cast<float*>(p);
-  }
-  return g_decode_scratch_dev[dev];
+  return static_cast<float*>(device_symbol_address(g_decode_scratch_cache, (const void*)&g_decode_scratch,
+                                                   "attn_decode_noalloc"));
 }
 
 }  // namespace attn
@@ -252,6 +241,7 @@ extern "C" int attn_decode_noalloc(const void* q, const void* k_cache, const voi
     ATTN_REQUIRE(st[i] >= 0 && st[i] % vec == 0, "attn_decode_noalloc: strides must be multiples of %d", vec);
   ATTN_REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(o, 4),
                "attn_decode_noalloc: q/k/v must be 16-byte aligned");
+  if (int rc = decode_grid_check(B, NH, "attn_decode_noalloc")) return rc;
   const size_t need = decode_ws(B, NH, L, D);
   if (need > sizeof(float) * kNoAllocDecodeFloats) {
     set_error("attn_decode_noalloc: this problem needs %zu bytes of scratch but the fixed array holds "

@@ -154,6 +154,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux,
                const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
+  const WaitErr werr = wait_err(p.err);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using E = Epi<EW>;
   uint8_t* epi = smem + GT_STAGES * GT_STAGE_BYTES;  // output staging buffers, two per epilogue group
@@ -198,7 +199,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         int tm, tn, kb0, kb1;
         unit_coords(p, unit, tm, tn, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[s], ph ^ 1, p.err, 101)) { ok = false; break; }
+          if (!mbar_wait(&empty[s], ph ^ 1, werr, 101)) { ok = false; break; }
           uint8_t* sa = smem + s * GT_STAGE_BYTES;
           uint8_t* sb = sa + GT_A_BYTES;
           mbar_arrive_expect_tx(&full[s], GT_STAGE_BYTES);
@@ -221,7 +222,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // tail: wait until the MMA thread has released every stage, so no asynchronous arrive is
       // still in flight to this CTA's shared memory when it exits
       for (int i = 0; i < GT_STAGES && ok; ++i) {
-        ok = mbar_wait(&empty[s], ph ^ 1, p.err, 105);
+        ok = mbar_wait(&empty[s], ph ^ 1, werr, 105);
         if (++s == GT_STAGES) { s = 0; ph ^= 1; }
       }
     }
@@ -237,11 +238,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         unit_coords(p, unit, tm, tn, kb0, kb1);
         const int acc = local & 1;
         const uint32_t acc_ph = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_ph ^ 1, p.err, 102)) break;
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1, werr, 102)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * GT_BN;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full[s], ph, p.err, 103)) { ok = false; break; }
+          if (!mbar_wait(&full[s], ph, werr, 103)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * GT_STAGE_BYTES);
           const uint32_t sb = sa + GT_A_BYTES;
@@ -319,7 +320,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       unit_coords(p, unit, tm, tn, kb0, kb1);
       const int acc = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, p.err, 104));
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_ph, werr, 104));
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * GT_BN + h * E::span;
@@ -557,7 +558,7 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   }
   if (p.atomic && !accumulate)
     ATTN_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s));
-  static uint64_t attr4 = 0, attr8 = 0;
+  static CtxOnce attr4, attr8;
   const int grid = p.units < sms ? p.units : sms;
   if (wide) {
     if (!set_smem_limit_once(gemm_tc_kernel<8>, GT_SMEM, attr8)) return ATTN_ERR_CUDA;

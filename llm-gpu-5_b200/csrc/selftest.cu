@@ -14,7 +14,7 @@ __global__ void __launch_bounds__(32, 1) wait_selftest_kernel(int* err, uint64_t
     fence_mbar_init();
   }
   __syncwarp();
-  const bool ok = mbar_wait(&bar, 0, err, ATTN_SELFTEST_SITE, limit_ns);
+  const bool ok = mbar_wait(&bar, 0, wait_err(err), ATTN_SELFTEST_SITE, limit_ns);
   (void)__all_sync(0xffffffffu, ok);
 }
 

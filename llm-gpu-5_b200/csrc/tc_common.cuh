@@ -27,8 +27,27 @@
 namespace attn {
 
 // ---- device error word: a bounded wait that gives up records where and returns --------------
-// Kernels receive a pointer to the library's error word (see dev_error_ptr()); 0 = no error,
-// otherwise a code identifying the wait site that gave up.
+// Kernels receive a pointer to the library's error word pair (see dev_error_ptr()):
+//   word[0]  0, or the site code of the first wait that gave up since the word was last cleared
+//            (a report for the host: attn_device_error);
+//   word[1]  the number of waits that have given up, ever (never cleared).
+// Each thread of a kernel notes word[1] when it starts (WaitErr::seen).  A wait that sees word[1]
+// move stops early: another wait of the same launch gave up, so this launch's work is lost
+// anyway.  A word left set by an earlier launch therefore never cuts a later launch short.
+struct WaitErr {
+  int* word;
+  int seen;
+};
+
+__device__ __forceinline__ WaitErr wait_err(int* word) {
+  return WaitErr{word, *(volatile int*)(word + 1)};
+}
+
+// Record that a wait (or a check standing in for one) at `site` gave up.
+__device__ __forceinline__ void record_wait_error(const WaitErr& e, int site) {
+  atomicCAS(e.word, 0, site);
+  atomicAdd(e.word + 1, 1);
+}
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -87,21 +106,21 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Wait until the phase with the given parity has completed.  Gives up after `limit_ns`
-// (default 2 s, far above any legitimate wait in these kernels), records `site` in g_tc_error
-// and returns false; callers then skip their remaining work and fall through to teardown.
+// (default 2 s, far above any legitimate wait in these kernels), records `site` in the error
+// word and returns false; callers then skip their remaining work and fall through to teardown.
 // Between checks of %globaltimer the warp is suspended in try_wait (at most 0.2 ms per try);
-// the error word in global memory (another wait having given up) is read once per try.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site,
+// the give-up count (another wait of this launch having given up) is read once per try.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitErr& err, int site,
                                           uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;
     if (globaltimer_ns() - t0 > limit_ns) {
-      atomicCAS(err, 0, site);
+      record_wait_error(err, site);
       return false;
     }
-    if (*(volatile int*)err != 0) return false;  // another wait gave up: stop early
+    if (*(volatile int*)(err.word + 1) != err.seen) return false;  // another wait gave up: stop early
   }
 }
 
@@ -308,7 +327,22 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t
 bool make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes = 128);
 
-// Device address of the library's error word on the current device (resolved once per device).
+// Device address of the library's error word pair on the current device (resolved once per
+// device and CUDA context).
 int* dev_error_ptr();
+
+// Device address of a file-scope __device__ variable on the current device.  In host code the
+// variable's name denotes a host-side stand-in, not device memory, so the address comes from
+// cudaGetSymbolAddress with the device current.  The result is cached per device and re-resolved
+// when the device's current CUDA context changes (the module is loaded again after a
+// cudaDeviceReset, and the variable may then sit at another address).
+struct SymbolCache {
+  void* ctx[64];
+  void* ptr[64];
+};
+void* device_symbol_address(SymbolCache& cache, const void* symbol, const char* what);
+
+// The calling thread's current CUDA context (nullptr before the runtime has created one).
+void* current_context();
 
 }  // namespace attn

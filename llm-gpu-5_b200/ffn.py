@@ -28,7 +28,8 @@ import torch
 
 from . import dp
 from . import mha_ops as ops
-from .mha import DeviceBuffer, GPTConfig, Parameter, _as_tensor, _NULL
+from ._lib import check_device_error
+from .mha import DeviceBuffer, GPTConfig, Parameter, _as_tensor, _NULL, device_checked
 
 
 class FeedForward:
@@ -72,6 +73,7 @@ class FeedForward:
         return torch.bfloat16 if self.precision == "bf16" else torch.float32
 
     # ---------------------------------------------------------------- forward
+    @device_checked
     def forward(self, gpu_input, B: int, T: int):
         """x [B*T, C] float32 (device) -> DeviceBuffer [B*T, C] float32 (caller frees)."""
         C = self.config.embedding_dim
@@ -87,6 +89,7 @@ class FeedForward:
         self._forward_core(x_op, B, T, out, accumulate=False)
         return DeviceBuffer(out)
 
+    @device_checked
     def forward_residual(self, gpu_x, B: int, T: int, ln_gamma, ln_beta, eps: float = 1e-5):
         """x += FFN(LayerNorm(x)) in place on the residual stream x [B*T, C] float32: the second
         half of TransformerBlock.forward (model/gpt.py:785-795: ln_2, mlp.forward, the residual add).
@@ -129,6 +132,7 @@ class FeedForward:
             self._cache = dict(B=B, T=T, x=x_op, pre=pre, act=act, w_fc=w_fc, w_proj=w_proj)
 
     # ---------------------------------------------------------------- backward
+    @device_checked
     def backward(self, gpu_dOut, B: int, T: int, accumulate=False):
         """dOut [B*T, C] float32 -> dIn DeviceBuffer [B*T, C]; the four gradients set or accumulated
         in place (model/gpt.py:367-456, the GPU-resident path :428-456)."""
@@ -179,6 +183,7 @@ class FeedForward:
                      M, C, H)
         return DeviceBuffer(dx)
 
+    @device_checked
     def backward_residual(self, gpu_dx, B: int, T: int, ln_gamma, ln_dgamma, ln_dbeta, accumulate=False):
         """Backward of forward_residual, in place: dx (dL/dx after the residual add) becomes
         dx + LN_bwd(ffn.backward(dx)), and the FFN's and the LayerNorm's gradients are set (or
@@ -197,9 +202,12 @@ class FeedForward:
         dln.free()
 
     def wait_grad_sync(self):
+        """Wait for the gradient all-reduce launched by the last backward (if any), and raise
+        DeviceWaitError if a kernel of a finished call gave up a bounded wait."""
         if self._grad_sync_work is not None:
             self._grad_sync_work.wait()
             self._grad_sync_work = None
+        check_device_error()
 
     def free_forward_caches(self):
         """Release the forward caches (model/gpt.py:458-470)."""

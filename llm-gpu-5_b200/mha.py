@@ -24,6 +24,7 @@ the reference (model/gpt.py:780-783, :819, :836-837).
 
 from __future__ import annotations
 
+import functools
 import math
 
 import numpy as np
@@ -31,45 +32,56 @@ import torch
 
 from . import dp
 from . import mha_ops as ops
+from ._lib import check_device_error, watch_device_error
 from .mha_ops import HeadView, ptr
 
 
+def device_checked(fn):
+    """Wrap a module entry point: raise DeviceWaitError first if a kernel of an earlier call gave
+    up a bounded wait, and after the call enqueue the copy of the device status word that the next
+    call reads.  Costs one 4-byte device-to-host copy per call and no synchronisation."""
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        check_device_error()
+        out = fn(*args, **kwargs)
+        watch_device_error()
+        return out
+    return wrapper
+
+
 class GPTConfig:
-    """The attention-relevant subset of llm-gpu-5's GPTConfig (model/gpt.py:53-87), with the same
-    argument names and validation, plus ``attention_precision`` ("fp32" or "bf16")."""
+    """The fields of llm-gpu-5's GPTConfig (model/gpt.py:53-87) that the attention path and its
+    callers read, under the same argument names, plus ``attention_precision`` ("fp32" or "bf16").
+
+    ``attention_impl`` is only carried for the checkpoint metadata (model/gpt.py:1114, :1196-1199);
+    the reference's older spellings of it (``attention_mode``, ``use_flash_attention`` /
+    ``flash_attention``) are accepted.  Other keyword arguments are ignored, as there."""
 
     def __init__(self, vocab_size: int, max_len: int = 8, embedding_dim: int = 16, num_heads: int = 2,
                  num_layers: int = 1, dropout_prob: float = 0.1, max_seq_len: int = None,
-                 batch_size: int = None, attention_impl: str = None, use_flash_attention: bool = None,
+                 attention_impl: str = None, use_flash_attention: bool = None,
                  attention_precision: str = "fp32", **kwargs):
-        self.vocab_size = vocab_size
-        if max_seq_len is not None:
-            max_len = max_seq_len
-        self.max_len = max_len
-        self.embedding_dim = embedding_dim
-        self.num_heads = num_heads
-        self.num_layers = num_layers
-        self.dropout_prob = dropout_prob
-        self.head_dim = embedding_dim // num_heads
-        requested = kwargs.pop("attention_mode", None)
-        flash = kwargs.pop("flash_attention", None)
-        if use_flash_attention is None and flash is not None:
-            use_flash_attention = flash
-        if attention_impl is None:
-            if requested is not None:
-                attention_impl = requested
-            elif use_flash_attention is not None:
-                attention_impl = "strided" if use_flash_attention else "identity"
-            else:
-                attention_impl = "identity"
-        self.attention_impl = str(attention_impl).strip().lower()
-        if self.attention_impl not in {"identity", "strided"}:
-            raise ValueError(f"Unsupported attention_impl: {attention_impl}")
-        self.use_flash_attention = self.attention_impl == "strided"
+        if embedding_dim % num_heads:
+            raise ValueError("embedding_dim must be divisible by num_heads")
         if attention_precision not in ("fp32", "bf16"):
             raise ValueError(f"attention_precision must be 'fp32' or 'bf16', got {attention_precision!r}")
+        self.vocab_size = vocab_size
+        self.max_len = max_seq_len if max_seq_len is not None else max_len
+        self.embedding_dim = embedding_dim
+        self.num_heads = num_heads
+        self.head_dim = embedding_dim // num_heads
+        self.num_layers = num_layers
+        self.dropout_prob = dropout_prob
         self.attention_precision = attention_precision
-        assert self.embedding_dim % self.num_heads == 0, "embedding_dim must be divisible by num_heads"
+        impl = attention_impl if attention_impl is not None else kwargs.get("attention_mode")
+        if impl is None:
+            flash = use_flash_attention if use_flash_attention is not None else kwargs.get("flash_attention")
+            impl = "strided" if flash else "identity"
+        self.attention_impl = str(impl).strip().lower()
+        if self.attention_impl not in ("identity", "strided"):
+            raise ValueError(f"Unsupported attention_impl: {impl}")
+        self.use_flash_attention = self.attention_impl == "strided"
 
 
 class DeviceBuffer:
@@ -229,6 +241,7 @@ class MultiHeadAttention:
         return C, NH, C // NH
 
     # ---------------------------------------------------------------- forward
+    @device_checked
     def forward(self, gpu_input, B: int, T: int, kv_cache: "KVCache | None" = None):
         """x [B*T, C] float32 (device) -> DeviceBuffer [B*T, C] float32 (caller frees).
 
@@ -250,6 +263,7 @@ class MultiHeadAttention:
         self._forward_core(x_op, B, T, out, accumulate=False, kv_cache=kv_cache)
         return DeviceBuffer(out)
 
+    @device_checked
     def forward_residual(self, gpu_x, B: int, T: int, ln_gamma, ln_beta, eps: float = 1e-5):
         """x += attn(LayerNorm(x)) in place on the residual stream x [B*T, C] float32.
 
@@ -274,6 +288,7 @@ class MultiHeadAttention:
         if self._cache is not None:
             self._cache.update(ln_input=ln_input, ln_eps=eps)
 
+    @device_checked
     def backward_residual(self, gpu_dx, B: int, T: int, ln_gamma, ln_dgamma, ln_dbeta, accumulate=False):
         """Backward of forward_residual, in place: dx (dL/dx after the residual add) becomes
         dL/dx before it, dx + LN_bwd(attn.backward(dx)), and the four attention gradients and the
@@ -330,6 +345,7 @@ class MultiHeadAttention:
             self._cache = dict(B=B, T=T, x=x_op, qkv=qkv, ctx=ctx, lse=lse, w_qkv=w_qkv, w_o=w_o)
 
     # ---------------------------------------------------------------- backward
+    @device_checked
     def backward(self, gpu_dOut, B: int, T: int, accumulate=False):
         """dY [B*T, C] float32 -> dX DeviceBuffer [B*T, C]; parameter grads set or accumulated."""
         c = self._cache
@@ -390,10 +406,12 @@ class MultiHeadAttention:
         return DeviceBuffer(dx)
 
     def wait_grad_sync(self):
-        """Wait for the gradient all-reduce launched by the last backward (if any)."""
+        """Wait for the gradient all-reduce launched by the last backward (if any), and raise
+        DeviceWaitError if a kernel of a finished call gave up a bounded wait."""
         if self._grad_sync_work is not None:
             self._grad_sync_work.wait()
             self._grad_sync_work = None
+        check_device_error()
 
     def free_forward_caches(self):
         """Release the forward caches (model/gpt.py:700-707)."""
@@ -431,6 +449,7 @@ class MultiHeadAttention:
         C, NH, D = self._shape()
         return KVCache(B, max_len, NH, D, self._dt)
 
+    @device_checked
     def forward_decode(self, gpu_input, B: int, kv_cache: "KVCache"):
         """One new token per sequence: x [B, C] float32 -> DeviceBuffer [B, C] float32.
 

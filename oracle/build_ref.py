@@ -1,6 +1,6 @@
 """Build ``oracle/_ref/libref_kernels.so`` from the reference's own CUDA kernel sources (checker only).
 
-    python oracle/build_ref.py /root/reference
+    python oracle/build_ref.py <reference checkout>      (or LLM_GPU5_REFERENCE=<checkout>)
 
 The reference's GPU kernels live as CUDA source in Python strings, compiled at run time by
 PyCUDA's ``SourceModule`` with ``-O3 --use_fast_math`` (core/ops.py:27-34, core/mha_ops.py:26-33).
@@ -198,6 +198,17 @@ def build(reference_root: str) -> str:
     return LIB
 
 
+def reference_root(argv=None):
+    """The reference checkout: the first argument, else $LLM_GPU5_REFERENCE; None if neither names
+    a directory holding the reference's ``core/`` sources."""
+    root = (argv[0] if argv else None) or os.environ.get("LLM_GPU5_REFERENCE")
+    if root and os.path.isdir(os.path.join(root, "core")):
+        return root
+    return None
+
+
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = reference_root(sys.argv[1:])
+    if root is None:
+        sys.exit("usage: python oracle/build_ref.py <reference checkout>  (or set LLM_GPU5_REFERENCE)")
     print(build(root))

@@ -2,7 +2,7 @@
 
 Usage (needs the reference checkout, which only the build container has):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference checkout>      (or LLM_GPU5_REFERENCE=<checkout>)
 
 The reference is PyCUDA code for a Kepler GPU.  Its attention *math* is plain NumPy and host
 Python, so this script installs a host-memory stand-in for ``pycuda.driver`` /
@@ -327,4 +327,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLM_GPU5_REFERENCE")
+    if not ref:
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout>  (or set LLM_GPU5_REFERENCE)")
+    main(ref)

@@ -128,3 +128,32 @@ def test_bad_arguments_of_the_block_entry_points():
     rc = L.attn_layernorm_bwd(fake, fake + 4096, fake, 8, 64, 1e-5, fake + 4096, 0, fake, fake, 0, None)
     assert rc == -1 and "alias" in L.attn_last_error_string().decode()
     assert pkg.launch_count() == before
+
+
+def test_decode_rejects_more_than_65535_sequence_heads_without_launch():
+    """B*NH is the decode kernel's grid.y: both decode entry points refuse B*NH > 65535 with a
+    message before launching (bf16, D = 8, L = 256 would fit the no-allocation array)."""
+    pkg = load_pkg()
+    L = pkg.lib
+    before = pkg.launch_count()
+    fake = 1 << 20
+    B, NH, Lk, D = 7000, 10, 256, 8
+    ws_bytes = L.attn_decode_workspace_size(B, NH, Lk, D)
+    assert ws_bytes <= 4 * (1 << 20)
+    rc = L.attn_decode(fake, fake, fake, fake, None, B, NH, Lk, D, NH * D, D, Lk * NH * D, NH * D, D,
+                       ctypes.c_float(0.35), 1, fake, ws_bytes, None)
+    assert rc == -2 and "65535" in L.attn_last_error_string().decode()
+    rc = L.attn_decode_noalloc(fake, fake, fake, fake, None, B, NH, Lk, D, NH * D, D, Lk * NH * D, NH * D, D,
+                               ctypes.c_float(0.35), 1, None)
+    assert rc == -2 and "65535" in L.attn_last_error_string().decode()
+    assert pkg.launch_count() == before
+
+
+def test_backward_beyond_the_tensor_core_row_limit_sizes_the_cuda_core_workspace():
+    """Rows longer than the tensor-core backward's limit (2,097,024) go to the CUDA-core backward;
+    its workspace (one float per row: delta) is what attn_bwd_workspace_size reports for them."""
+    L = load_pkg().lib
+    t_max = 2097024
+    B, NH, D = 1, 1, 64
+    assert L.attn_bwd_workspace_size(B, NH, t_max + 1, D, 1) == B * NH * (t_max + 1) * 4
+    assert L.attn_bwd_workspace_size(B, NH, t_max, D, 1) > B * NH * t_max * 4  # the tensor-core layout
