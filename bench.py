@@ -192,6 +192,55 @@ class EventProfiler:
         return out
 
 
+class _NoRange:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+class MarkProfiler:
+    """CUDA timing events around the named op ranges only (all ranges when ``names`` is None).
+    The events are created as external events, so a range captured into a CUDA graph becomes a
+    pair of event-record nodes that record again on every replay; ``last()`` then reads the
+    duration of each range in the graph's latest replay."""
+
+    def __init__(self, names=None):
+        self.names = None if names is None else set(names)
+        self.spans = []
+
+    class _Range:
+        def __init__(self, prof, name):
+            self.prof, self.name = prof, name
+
+        def __enter__(self):
+            import torch
+            self.s = torch.cuda.Event(enable_timing=True, external=True)
+            self.s.record()
+            return self
+
+        def __exit__(self, *exc):
+            import torch
+            e = torch.cuda.Event(enable_timing=True, external=True)
+            e.record()
+            self.prof.spans.append((self.name, self.s, e))
+            return False
+
+    def range(self, name):
+        if self.names is not None and name not in self.names:
+            return _NoRange()
+        return MarkProfiler._Range(self, name)
+
+    def last(self):
+        """{name: (total ms, ranges)} over the recorded ranges (after a synchronize)."""
+        out = {}
+        for name, s, e in self.spans:
+            t, n = out.get(name, (0.0, 0))
+            out[name] = (t + s.elapsed_time(e), n + 1)
+        return out
+
+
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons sampled while the timed region runs: NVML read
     every 10 ms from a thread (read-only queries), or nvidia-smi every 200 ms where NVML is not
@@ -323,6 +372,7 @@ def run_ours(args, cfg):
     _, B = pkg.dp.shard(GB, world, rank)  # this rank's sequences (an even split of the global batch)
     M = B * T
     steps, warmup = args.steps, max(args.warmup, 3)
+    use_graph = not args.eager
 
     np.random.seed(1000 + cfg)  # replicated weights: every rank draws the same N(0, 0.02)
     attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
@@ -353,36 +403,103 @@ def run_ours(args, cfg):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---------------- device-resident timing
     for _ in range(warmup):
         step(x, dy).free()
-    prof = EventProfiler()
+
+    # ---------------- per-op breakdown and launches of one step (untimed)
+    # every op range of the step bracketed by events; with graphs, inside a captured step's replay
+    # (no host gaps between the ops), otherwise in an eager step
+    l0 = pkg.launch_count()
+    prof = MarkProfiler()
     attn.profiler = prof
-    step(x, dy).free()  # one profiled step outside the timed region primes the event objects
-    prof.spans.clear()
-    clocks = ClockSampler(local)
+    if use_graph:
+        bd_graph = pkg.graphs.CapturedStep(lambda: step(x, dy))
+        attn.profiler = None
+        bd_graph.replay()
+        torch.cuda.synchronize()
+    else:
+        step(x, dy).free()
+        attn.profiler = None
+        torch.cuda.synchronize()
+    launches_per_step = pkg.launch_count() - l0
+    totals = prof.last()
+    if use_graph:
+        bd_graph.reset()
+    dom = max((k for k in totals if op_flops(k, B, T, C, NH)), key=lambda k: totals[k][0])
+
+    # ---------------- eager steps: device time and host enqueue time per step
     barrier()
-    clocks.start()
-    launches0 = pkg.launch_count()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
+    h0 = time.perf_counter()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
     for _ in range(steps):
         step(x, dy).free()
+    host_enqueue_ms = (time.perf_counter() - h0) * 1e3 / steps
+    eb.record()
+    barrier()
+    eager_ms = max_over_ranks(ea.elapsed_time(eb)) / steps
+    host_enqueue_ms = max_over_ranks(host_enqueue_ms)
+
+    # ---------------- the gradient all-reduce alone (per rank, CUDA events on the launching stream)
+    comm_ms = None
+    if dist is not None:
+        times = []
+        for _ in range(5):
+            barrier()
+            ca, cb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ca.record()
+            pkg.dp.allreduce_grads(attn.flat_grads, dist.group.WORLD)
+            cb.record()
+            cb.synchronize()
+            times.append(ca.elapsed_time(cb))
+        comm_ms = max_over_ranks(statistics.median(times))
+
+    # ---------------- timed region: captured steps replayed (or eager steps with --eager)
+    # The dominant op is bracketed by timing events in every step; with graphs, R captured copies
+    # of the step (sharing one memory pool) are replayed in turn, so the last R steps of the timed
+    # region each leave their own reading of it.
+    marks = MarkProfiler({dom})
+    attn.profiler = marks
+    graphs = []
+    if use_graph:
+        pool = torch.cuda.graph_pool_handle()
+        R = max(1, min(steps, 4))
+        graphs = [pkg.graphs.CapturedStep(lambda: step(x, dy), pool=pool) for _ in range(R)]
+        attn.profiler = None
+        for g in graphs:
+            g.replay()
+        run_step = lambda k: graphs[k % len(graphs)].replay()  # noqa: E731
+    else:
+        run_step = lambda k: step(x, dy).free()  # noqa: E731
+        for k in range(2):
+            run_step(k)
+    clocks = ClockSampler(local)
+    barrier()
+    if not use_graph:
+        marks.spans.clear()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    h1 = time.perf_counter()
+    t0.record()
+    for k in range(steps):
+        run_step(k)
+    host_replay_ms = (time.perf_counter() - h1) * 1e3 / steps
     t1.record()
     barrier()
     clk = clocks.stop()
-    launches = pkg.launch_count() - launches0
-    ms = max_over_ranks(t0.elapsed_time(t1)) / steps
     attn.profiler = None
-    totals = prof.totals()
+    ms = max_over_ranks(t0.elapsed_time(t1)) / steps
+    dom_t, dom_n = marks.last()[dom]
+    dom_ms = max_over_ranks(dom_t / dom_n)
     value = GB * T / (ms * 1e-3)
 
     # ---------------- end to end through the public API with host buffers
-    # Every step copies its x and dY in from pinned host memory and its dX and gradients out.
-    # The copies run on their own streams with double-buffered device slots, so step k's
-    # host->device copies overlap step k-1's compute and step k-1's device->host copies (what a
-    # training loop with a prefetching data loader does); each step still moves all its bytes.
+    # Every step copies its x and dY in from pinned host memory and its dX and gradients out.  The
+    # copies run on their own streams with two device slots, so step k's host->device copies overlap
+    # step k-1's compute and its device->host copies (what a training loop with a prefetching data
+    # loader does); each step still moves all its bytes.  With graphs each slot has its own captured
+    # step reading that slot's buffers.
     x_h = torch.empty((M, C), dtype=torch.float32, pin_memory=True)
     dy_h = torch.empty((M, C), dtype=torch.float32, pin_memory=True)
     x_h.copy_(x)
@@ -391,13 +508,16 @@ def run_ours(args, cfg):
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
     slots = []
     for _ in range(2):
-        slots.append(dict(
-            x=torch.empty_like(x), dy=torch.empty_like(dy),
-            g=torch.empty_like(attn.flat_grads),
-            dx_h=torch.empty((M, C), dtype=torch.float32, pin_memory=True),
-            g_h=torch.empty(attn.flat_grads.numel(), dtype=torch.float32, pin_memory=True),
-            ev_x=torch.cuda.Event(), ev_dy=torch.cuda.Event(), ev_done=torch.cuda.Event(),
-            ev_out=torch.cuda.Event(), used=False))
+        sl = dict(x=torch.empty_like(x), dy=torch.empty_like(dy), g=torch.empty_like(attn.flat_grads),
+                  dx_h=torch.empty((M, C), dtype=torch.float32, pin_memory=True),
+                  g_h=torch.empty(attn.flat_grads.numel(), dtype=torch.float32, pin_memory=True),
+                  ev_in=torch.cuda.Event(), ev_done=torch.cuda.Event(), ev_out=torch.cuda.Event(), used=False)
+        sl["x"].copy_(x)
+        sl["dy"].copy_(dy)
+        if use_graph:
+            sl["graph"] = pkg.graphs.CapturedStep(lambda sl=sl: step(sl["x"], sl["dy"]), pool=graphs[0].pool())
+        slots.append(sl)
+    torch.cuda.synchronize()
 
     def e2e_step(k):
         sl = slots[k % 2]
@@ -405,29 +525,30 @@ def run_ours(args, cfg):
             if sl["used"]:
                 s_in.wait_event(sl["ev_done"])  # the slot's previous step has read its inputs
             sl["x"].copy_(x_h, non_blocking=True)
-            sl["ev_x"].record(s_in)
             sl["dy"].copy_(dy_h, non_blocking=True)
-            sl["ev_dy"].record(s_in)
+            sl["ev_in"].record(s_in)
         if sl["used"]:
-            comp.wait_event(sl["ev_out"])  # the slot's previous gradient snapshot has been copied out
-        comp.wait_event(sl["ev_x"])
-        out = attn.forward(sl["x"], B, T)
-        comp.wait_event(sl["ev_dy"])
-        din = attn.backward(sl["dy"], B, T)
-        attn.wait_grad_sync()
+            comp.wait_event(sl["ev_out"])  # the slot's previous results have been copied out
+        comp.wait_event(sl["ev_in"])
+        if use_graph:
+            din = sl["graph"].replay()
+            dxt = din.tensor
+        else:
+            din = step(sl["x"], sl["dy"])
+            dxt = din.tensor
         sl["g"].copy_(attn.flat_grads)
         sl["ev_done"].record(comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(sl["ev_done"])
-            sl["dx_h"].copy_(din.tensor, non_blocking=True)
+            sl["dx_h"].copy_(dxt, non_blocking=True)
             sl["g_h"].copy_(sl["g"], non_blocking=True)
             sl["ev_out"].record(s_out)
-        din.tensor.record_stream(s_out)
+        if not use_graph:
+            dxt.record_stream(s_out)
+            din.free()
         sl["used"] = True
-        out.free()
-        din.free()
 
-    e2e_steps = max(2, min(steps, 6))
+    e2e_steps = max(2, min(steps, 12))
     for k in range(2):
         e2e_step(k)
     barrier()
@@ -444,6 +565,11 @@ def run_ours(args, cfg):
     h2d = 2 * M * C * 4
     d2h = M * C * 4 + attn.flat_grads.numel() * 4
 
+    # ---------------- plain pinned copies of the same bytes, all ranks at once (the host-link rate)
+    link = host_link_rate(x_h, slots[0]["x"], slots[0]["dx_h"], barrier, max_over_ranks)
+
+    for g in graphs + [sl["graph"] for sl in slots if "graph" in sl]:
+        g.reset()  # graphs holding NCCL calls go before the process group
     if dist is not None:
         attn.grad_sync_group = None
         dist.barrier()
@@ -452,13 +578,11 @@ def run_ours(args, cfg):
             dist.destroy_process_group()
         return 0
 
-    # ---------------- roofline of the dominant kernel
+    # ---------------- the line
     peaks, src = load_peaks()
-    per_op = {k: dict(ms_per_step=t / steps, launches_per_step=n / steps) for k, (t, n) in totals.items()}
-    dom = max((k for k in totals if op_flops(k, B, T, C, NH)), key=lambda k: totals[k][0])
-    dom_ms = totals[dom][0] / totals[dom][1]
+    per_op = {k: dict(ms_per_step=t, ranges_per_step=n) for k, (t, n) in totals.items()}
     achieved = op_flops(dom, B, T, C, NH) / (dom_ms * 1e-3) / 1e12
-    peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     traffic = None
     tf = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tf):
@@ -468,45 +592,200 @@ def run_ours(args, cfg):
         # a launch over this rank's B sequences moves B / global_batch of it
         if full is not None and not args.batch:
             traffic = full * B / GB
-    total_flops = sum(op_flops(k, B, T, C, NH) for k in totals if op_flops(k, B, T, C, NH))
-    # the attention core (QK^T, PV, dP, dV, dQ, dK: 12*D per causal pair, no credit for recomputing S)
-    # and the six projection GEMMs, each over its own event-timed kernels, and their sum
-    groups = {}
-    for k, (t, n) in totals.items():
-        f = op_flops(k, B, T, C, NH)
-        if f:
-            g = "attention_core" if k.startswith("attn_") else "projections"
-            fl, tm = groups.get(g, (0, 0.0))
-            groups[g] = (fl + f * n / steps, tm + t / steps)
-    tflops = {g: dict(tflop_per_step=fl / 1e12, ms_per_step=tm, tflops=fl / (tm * 1e-3) / 1e12)
-              for g, (fl, tm) in groups.items()}
-    if groups:
-        fl = sum(v[0] for v in groups.values())
-        tm = sum(v[1] for v in groups.values())
-        tflops["sum"] = dict(tflop_per_step=fl / 1e12, ms_per_step=tm, tflops=fl / (tm * 1e-3) / 1e12)
+    tflops = group_tflops(totals, lambda k: op_flops(k, B, T, C, NH))
+    copy_gbs = (h2d + d2h) * world / (e2e_ms * 1e-3) / 1e9
+    # the step's copies alone at the measured link rates: the slowest of each direction by itself
+    # and both directions together
+    link_ms = 1e3 * max(h2d * world / (link["h2d_gbs"] * 1e9), d2h * world / (link["d2h_gbs"] * 1e9),
+                        (h2d + d2h) * world / (link["duplex_gbs"] * 1e9))
     line = dict(
         metric="causal attention fwd+bwd tokens/sec", value=value, unit="tokens/s", n_gpus=world,
         steps=steps, warmup=warmup, ms_per_step=ms, higher_is_better=True, scaling="strong",
         vs_baseline=None, dtype="bf16" if w["prec"] == "bf16" else "f32", data="synthetic",
         config=dict(workload=w["name"], global_batch=GB, seq_len=T, d_model=C, heads=NH, head_dim=C // NH,
-                    per_gpu_batch=B, parallelism=f"dp{world}", l2="inputs larger than L2 (no flush)"),
+                    per_gpu_batch=B, parallelism=f"dp{world}", l2="inputs larger than L2 (no flush)",
+                    launch="CUDA graph: the step captured once, replayed" if use_graph else "eager"),
         roofline=dict(bound="tensor", kernel=dom, achieved=achieved, peak=peak, unit="TFLOP/s",
                       frac=achieved / peak, traffic=traffic,
-                      peak_source=f"{src} bf16_tflops_sustained"),
-        step_tflops=total_flops / (ms * 1e-3) / 1e12 if world == 1 else None,
+                      peak_source=f"{src} bf16_tflops (burst; the timed region is {ms * steps / 1e3:.2f} s)",
+                      frac_of_sustained=achieved / peaks.get("bf16_tflops_sustained",
+                                                             FALLBACK_PEAKS["bf16_tflops_sustained"])),
+        step_tflops=sum(op_flops(k, B, T, C, NH) or 0 for k in totals) * world / (ms * 1e-3) / 1e12,
         tflops=tflops,
         breakdown=per_op,
-        gpu_launches=launches,
+        timing=dict(eager_ms_per_step=eager_ms, host_enqueue_ms_eager=host_enqueue_ms,
+                    host_enqueue_ms_graph=host_replay_ms if use_graph else None, comm_ms=comm_ms,
+                    comm_bytes=attn.flat_grads.numel() * 4 if dist is not None else 0,
+                    note="eager: the same step launched op by op from Python; comm_ms: the gradient "
+                         "all-reduce alone, median of 5, max over ranks"),
+        gpu_launches=launches_per_step * steps,
         e2e=dict(value=GB * T / (e2e_ms * 1e-3), unit="tokens/s", h2d_bytes_per_step=h2d * world,
-                 d2h_bytes_per_step=d2h * world, ms_per_step=e2e_ms),
+                 d2h_bytes_per_step=d2h * world, ms_per_step=e2e_ms, copy_gbs=copy_gbs,
+                 host_link_gbs=link, link_bound_ms=link_ms, frac_of_link_bound=link_ms / e2e_ms),
         clocks=clk,
     )
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg)
+    if world == 1 and not args.no_configs and not args.batch:
+        line["configs"] = measure_other_configs(args, pkg, peaks, src)
     print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
     return 0
+
+
+def group_tflops(totals, flops_of):
+    """Attention core (QK^T, PV, dP, dV, dQ, dK: 12*D per causal pair, no credit for recomputing
+    S) and projection GEMMs, each over its own event-timed ranges, and their sum.  ``totals`` maps an
+    op to (ms in one step, ranges in one step); ``flops_of`` gives one range's FLOPs."""
+    groups = {}
+    for k, (t, n) in totals.items():
+        f = flops_of(k)
+        if f:
+            g = "attention_core" if k.startswith("attn_") else "projections"
+            fl, tm = groups.get(g, (0, 0.0))
+            groups[g] = (fl + f * n, tm + t)
+    out = {g: dict(tflop_per_step=fl / 1e12, ms_per_step=tm, tflops=fl / (tm * 1e-3) / 1e12)
+           for g, (fl, tm) in groups.items()}
+    if groups:
+        fl = sum(v[0] for v in groups.values())
+        tm = sum(v[1] for v in groups.values())
+        out["sum"] = dict(tflop_per_step=fl / 1e12, ms_per_step=tm, tflops=fl / (tm * 1e-3) / 1e12)
+    return out
+
+
+def host_link_rate(h_src, d_buf, h_dst, barrier, max_over_ranks, reps=3):
+    """Plain pinned copies of one step-sized buffer, every rank at once: host->device, device->host,
+    and both together on two streams.  GB/s summed over the ranks (all ranks' bytes / the slowest
+    rank's time), best of ``reps``."""
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    nb = h_src.numel() * h_src.element_size()
+    cur = torch.cuda.current_stream()
+    other = torch.cuda.Stream()
+    d2 = torch.empty_like(d_buf)
+    res = {}
+    for name in ("h2d", "d2h", "duplex"):
+        best = None
+        for _ in range(reps):
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(cur)
+            if name == "duplex":  # the device->host copy starts with the host->device one
+                other.wait_event(a)
+                with torch.cuda.stream(other):
+                    h_dst.copy_(d2, non_blocking=True)
+            if name in ("h2d", "duplex"):
+                d_buf.copy_(h_src, non_blocking=True)
+            if name == "d2h":
+                h_dst.copy_(d2, non_blocking=True)
+            if name == "duplex":
+                cur.wait_stream(other)
+            b.record(cur)
+            b.synchronize()
+            t = max_over_ranks(a.elapsed_time(b))
+            best = t if best is None else min(best, t)
+        moved = nb * (2 if name == "duplex" else 1) * world
+        res[f"{name}_gbs"] = moved / (best * 1e-3) / 1e9
+    res["bytes_per_rank"] = nb
+    return res
+
+
+# ------------------------------------------------------------------------------ the other configs
+def fp32_core_peak(peaks):
+    """FP32 CUDA-core peak of the GPU, derived (no measured FP32 figure exists): SMs x 128 FP32 lanes
+    x 2 FLOP per FMA x the measured maximum SM clock."""
+    import torch
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    mhz = peaks.get("sm_max_mhz", 1965.0)
+    return sms * 128 * 2 * mhz * 1e6 / 1e12, f"derived: {sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz"
+
+
+def measure_module_config(args, pkg, cfg, peaks, src):
+    """MultiHeadAttention forward + backward at one configuration's full size on one GPU: the step
+    captured as a CUDA graph, each replay timed with events after a 256 MB write that flushes L2,
+    every op range timed inside the replays."""
+    import numpy as np
+    import torch
+    w = WORKLOADS[cfg]
+    B, T, C, NH = w["global_batch"], w["T"], w["C"], w["NH"]
+    steps = max(args.steps, 3)
+    np.random.seed(1000 + cfg)
+    attn = pkg.MultiHeadAttention(pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T,
+                                                attention_precision=w["prec"]))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1000 + cfg)
+    x = torch.randn((B * T, C), generator=gen, device="cuda")
+    dy = torch.randn((B * T, C), generator=gen, device="cuda")
+
+    def step():
+        out = attn.forward(x, B, T)
+        din = attn.backward(dy, B, T)
+        attn.wait_grad_sync()
+        out.free()
+        return din
+
+    for _ in range(max(args.warmup, 3)):
+        step().free()
+    prof = MarkProfiler()
+    attn.profiler = prof
+    graph = pkg.graphs.CapturedStep(step)
+    attn.profiler = None
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB, twice the L2
+    times, optot = [], {}
+    for k in range(steps + 1):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        b.synchronize()
+        if k == 0:
+            continue  # the first replay uploads the graph
+        times.append(a.elapsed_time(b))
+        for name, (t, n) in prof.last().items():
+            s = optot.setdefault(name, [0.0, n])
+            s[0] += t
+    graph.reset()
+    ms = statistics.median(times)
+    totals = {name: (t / steps, n) for name, (t, n) in optot.items()}
+    flops_of = lambda k: op_flops(k, B, T, C, NH)  # noqa: E731
+    dom = max((k for k in totals if flops_of(k)), key=lambda k: totals[k][0])
+    dom_ach = flops_of(dom) / (totals[dom][0] / totals[dom][1] * 1e-3) / 1e12
+    if w["prec"] == "bf16":
+        peak, psrc = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), f"{src} bf16_tflops (burst)"
+    else:
+        peak, psrc = fp32_core_peak(peaks)
+    tflops = group_tflops(totals, flops_of)
+    for g in tflops.values():
+        g["frac"] = g["tflops"] / peak
+    res = dict(workload=w["name"], value=B * T / (ms * 1e-3), unit="tokens/s", ms_per_step=ms,
+               dtype="bf16" if w["prec"] == "bf16" else "f32", steps=steps, tflops=tflops,
+               roofline=dict(bound="tensor" if w["prec"] == "bf16" else "fp32 CUDA core", kernel=dom,
+                             achieved=dom_ach, peak=peak, unit="TFLOP/s", frac=dom_ach / peak, peak_source=psrc),
+               breakdown={k: dict(ms_per_step=t, ranges_per_step=n) for k, (t, n) in totals.items()},
+               l2="a 256 MB buffer written before every timed step (L2 flushed)",
+               launch="CUDA graph: the step captured once, replayed")
+    del attn, x, dy, flush
+    torch.cuda.empty_cache()
+    if not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(cfg, budget_s=6.0)
+    return res
+
+
+def measure_other_configs(args, pkg, peaks, src):
+    """Configurations 1-4 at full size on one GPU, each with its CPU baseline; a configuration that
+    fails reports its error instead of a number."""
+    out = {}
+    for cfg in (1, 2, 3, 4):
+        try:
+            if WORKLOADS[cfg].get("decode"):
+                out[f"cfg{cfg}"] = decode_line(args, cfg, pkg, world=1, rank=0)
+            else:
+                out[f"cfg{cfg}"] = measure_module_config(args, pkg, cfg, peaks, src)
+        except Exception as e:  # reported in the line; the headline number stands on its own
+            out[f"cfg{cfg}"] = dict(workload=WORKLOADS[cfg]["name"], error=f"{type(e).__name__}: {e}"[:300])
+    return out
 
 
 # ------------------------------------------------------------------------------ decode (cfg 4)
@@ -538,15 +817,24 @@ def cpu_decode_baseline(w, reps=5):
 
 
 def run_decode(args, cfg):
-    """One decode step = one attn_decode call for B sequences; inputs (q and two alternating
-    copies of the K/V cache, 268 MB each, so no call reads L2-resident data) are on the device."""
     import torch
     import importlib
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     pkg = importlib.import_module("llm-gpu-5_b200")
+    line = decode_line(args, cfg, pkg, world, rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def decode_line(args, cfg, pkg, world, rank):
+    """One decode step = one attn_decode call for B sequences; inputs (q and two alternating
+    copies of the K/V cache, 268 MB each, so no call reads L2-resident data) are on the device.
+    Returns the JSON line (replicas: each GPU runs its own batch, no collective)."""
+    import torch
+    local = torch.cuda.current_device()
     w = WORKLOADS[cfg]
     B, L, NH = args.batch or w["global_batch"], w["T"], w["NH"]
     D = w["C"] // NH
@@ -598,7 +886,7 @@ def run_decode(args, cfg):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / steps
     if rank != 0:
-        return 0
+        return None
     peaks, src = load_peaks()
     kv_bytes = 2 * B * L * NH * D * 2
     achieved = kv_bytes / (ms * 1e-3) / 1e9
@@ -620,8 +908,7 @@ def run_decode(args, cfg):
     )
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_decode_baseline(w)
-    print(json.dumps(line), flush=True)
-    return 0
+    return line
 
 
 # ------------------------------------------------------------------------------ fused half-block
@@ -879,6 +1166,10 @@ def main():
                     help="vendor: time cuDNN attention and cuBLAS GEMMs on the same workload (context only)")
     ap.add_argument("--config", type=int, default=5, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="leave out the 'configs' object (configurations 1-4 measured after the headline)")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch every step op by op from Python instead of replaying a captured CUDA graph")
     ap.add_argument("--residual", action="store_true",
                     help="time x += attn(ln_1(x)) fused (forward_residual) against the unfused block sequence")
     ap.add_argument("--ffn", action="store_true",

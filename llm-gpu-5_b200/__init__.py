@@ -10,10 +10,10 @@ All compute runs in ``libattn_b200.so`` (C ABI: ``include/attn_b200.h``); import
 library has not been built.
 """
 from ._lib import AttnError, DeviceWaitError, LIB_PATH, clear_device_error, launch_count, lib  # noqa: F401  (fails loudly if unbuilt)
-from . import dp, mha_ops  # noqa: F401
+from . import dp, graphs, mha_ops  # noqa: F401
 from .mha import DeviceBuffer, GPTConfig, KVCache, MultiHeadAttention, Parameter  # noqa: F401
 from .ffn import FeedForward  # noqa: F401
 from .mha_ops import get_shared_mha_module, THREADS_PER_BLOCK, SOFTMAX_BLOCK_THREADS  # noqa: F401
 
-__all__ = ["MultiHeadAttention", "FeedForward", "GPTConfig", "Parameter", "DeviceBuffer", "KVCache", "mha_ops", "dp", "AttnError", "DeviceWaitError", "clear_device_error",
+__all__ = ["MultiHeadAttention", "FeedForward", "GPTConfig", "Parameter", "DeviceBuffer", "KVCache", "mha_ops", "dp", "graphs", "AttnError", "DeviceWaitError", "clear_device_error",
            "get_shared_mha_module", "launch_count"]

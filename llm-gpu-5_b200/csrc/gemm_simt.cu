@@ -24,7 +24,24 @@ gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* _
   const int m0 = blockIdx.y * SG_BM, n0 = blockIdx.x * SG_BN;
   const int k_begin = blockIdx.z * k_chunk, k_end = min(K, k_begin + k_chunk);
   const bool split = gridDim.z > 1;
-  float acc[4][4] = {};
+  // Long reductions (the weight gradients sum over every token: K = 262,144 at batch 512, T = 512)
+  // lose float32 accuracy in one running sum.  Each 256-deep chunk of K is summed on its own in
+  // acc, and the chunk sums are added into tot with Kahan compensation (comp).  For K <= 256 the
+  // result is the plain running sum.
+  float acc[4][4] = {}, tot[4][4] = {}, comp[4][4] = {};
+  auto fold = [&]() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float y = acc[i][j] - comp[i][j];
+        const float t = tot[i][j] + y;
+        comp[i][j] = (t - tot[i][j]) - y;
+        tot[i][j] = t;
+        acc[i][j] = 0.f;
+      }
+  };
+  int tiles_in_chunk = 0;
 
   for (int k0 = k_begin; k0 < k_end; k0 += SG_BK) {
 #pragma unroll
@@ -57,7 +74,12 @@ gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* _
         for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
     __syncthreads();
+    if (++tiles_in_chunk == 256 / SG_BK) {
+      fold();
+      tiles_in_chunk = 0;
+    }
   }
+  fold();
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int gm = m0 + ty * 4 + i;
@@ -66,7 +88,7 @@ gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* _
     for (int j = 0; j < 4; ++j) {
       const int gn = n0 + tx * 4 + j;
       if (gn >= N) continue;
-      float val = acc[i][j];
+      float val = tot[i][j];
       if (bias && blockIdx.z == 0) val += bias[gn];
       if (act == ACT_GELU) {
         if (aux) {

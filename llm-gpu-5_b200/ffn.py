@@ -114,8 +114,8 @@ class FeedForward:
         dt = self._dt
         if dt == torch.bfloat16:
             with self._rng("cast"):
-                w_fc = ops.cast_bf16(self.c_fc_w.weights)
-                w_proj = ops.cast_bf16(self.c_proj_w.weights)
+                w_fc = self.c_fc_w.bf16_weights()
+                w_proj = self.c_proj_w.bf16_weights()
         else:
             w_fc, w_proj = self.c_fc_w.weights, self.c_proj_w.weights
         training = getattr(self, "training", True)

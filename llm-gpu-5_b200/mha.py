@@ -146,11 +146,29 @@ class Parameter:
         self.grads.zero_()
         self.m = torch.zeros(self.shape, dtype=torch.float32, device="cuda")
         self.v = torch.zeros(self.shape, dtype=torch.float32, device="cuda")
+        self._handed_out = 0  # times gpu_weights gave the weights' address to a caller
+        self._bf16 = None     # (key, bf16 copy of the weights)
 
     # PyCUDA-style handles (``int()`` gives the device address)
     @property
     def gpu_weights(self):
+        # whoever takes the address may write the weights behind torch's back (the reference's
+        # optimizer kernels do, core/ops.py:545-570): the bf16 copy is made again after this
+        self._handed_out += 1
         return DeviceBuffer(self.weights)
+
+    def bf16_weights(self) -> torch.Tensor:
+        """The weights rounded to bf16 for the tensor-core path, kept between calls while the
+        weights are unchanged: while the tensor is the same, torch's version counter of it has not
+        moved (no in-place torch op) and ``gpu_weights`` has not handed its address out.  While a
+        CUDA graph is being captured the cast is always recorded, so every replay casts the weights
+        as they are then."""
+        key = (self.weights.data_ptr(), self.weights._version, self._handed_out)
+        if torch.cuda.is_current_stream_capturing():
+            return ops.cast_bf16(self.weights)
+        if self._bf16 is None or self._bf16[0] != key:
+            self._bf16 = (key, ops.cast_bf16(self.weights))
+        return self._bf16[1]
 
     @property
     def gpu_grads(self):
@@ -316,8 +334,8 @@ class MultiHeadAttention:
         dt = self._dt
         if dt == torch.bfloat16:
             with self._rng("cast"):
-                w_qkv = ops.cast_bf16(self.c_attn_w.weights)
-                w_o = ops.cast_bf16(self.c_proj_w.weights)
+                w_qkv = self.c_attn_w.bf16_weights()
+                w_o = self.c_proj_w.bf16_weights()
         else:
             w_qkv, w_o = self.c_attn_w.weights, self.c_proj_w.weights
         ldx = x_op.shape[1]
@@ -467,8 +485,8 @@ class MultiHeadAttention:
         x = _as_tensor(gpu_input, B * C).view(B, C)
         if dt == torch.bfloat16:
             x_op = ops.cast_bf16(x)
-            w_qkv = ops.cast_bf16(self.c_attn_w.weights)
-            w_o = ops.cast_bf16(self.c_proj_w.weights)
+            w_qkv = self.c_attn_w.bf16_weights()
+            w_o = self.c_proj_w.bf16_weights()
         else:
             x_op, w_qkv, w_o = x, self.c_attn_w.weights, self.c_proj_w.weights
         qkv = torch.empty((B, 3 * C), dtype=dt, device="cuda")
