@@ -37,8 +37,8 @@ sys.path.insert(0, ROOT)
 WORKLOADS = {
     1: dict(name="small preset: causal MHA fwd+bwd, B=8 T=128 C=64 NH=4 D=16, fp32",
             global_batch=8, T=128, C=64, NH=4, prec="fp32", cpu_slice=8),
-    2: dict(name="training batch: causal MHA fwd+bwd, B=256 T=128 C=256 NH=8 D=32, fp32",
-            global_batch=256, T=128, C=256, NH=8, prec="fp32", cpu_slice=16),
+    2: dict(name="training batch: causal MHA fwd+bwd, B=256 T=128 C=256 NH=8 D=32, fp32 inputs, tf32 "
+                 "tensor-core products", global_batch=256, T=128, C=256, NH=8, prec="tf32", cpu_slice=16),
     3: dict(name="long context: causal MHA fwd+bwd, B=32 T=1024 C=512 NH=8 D=64, bf16",
             global_batch=32, T=1024, C=512, NH=8, prec="bf16", cpu_slice=1),
     4: dict(name="generation-shaped decode: one query row per (batch, head) over an L=2048 K/V prefix, "
@@ -701,13 +701,16 @@ def fp32_core_peak(peaks):
     return sms * 128 * 2 * mhz * 1e6 / 1e12, f"derived: {sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz"
 
 
-def measure_module_config(args, pkg, cfg, peaks, src):
+def measure_module_config(args, pkg, cfg, peaks, src, prec=None):
     """MultiHeadAttention forward + backward at one configuration's full size on one GPU: the step
     captured as a CUDA graph, each replay timed with events after a 256 MB write that flushes L2,
-    every op range timed inside the replays."""
+    every op range timed inside the replays.  ``prec`` overrides the configuration's precision."""
     import numpy as np
     import torch
-    w = WORKLOADS[cfg]
+    w = dict(WORKLOADS[cfg])
+    if prec is not None and prec != w["prec"]:
+        w["prec"] = prec
+        w["name"] = w["name"].split(", fp32 inputs")[0] + f", {prec}"
     B, T, C, NH = w["global_batch"], w["T"], w["C"], w["NH"]
     steps = max(args.steps, 3)
     np.random.seed(1000 + cfg)
@@ -754,14 +757,18 @@ def measure_module_config(args, pkg, cfg, peaks, src):
     dom_ach = flops_of(dom) / (totals[dom][0] / totals[dom][1] * 1e-3) / 1e12
     if w["prec"] == "bf16":
         peak, psrc = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), f"{src} bf16_tflops (burst)"
+    elif w["prec"] == "tf32":
+        # no measured tf32 figure: the dense tf32 rate is half the bf16 rate on this part
+        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2
+        psrc = f"derived: half of the {src} bf16_tflops (burst)"
     else:
         peak, psrc = fp32_core_peak(peaks)
     tflops = group_tflops(totals, flops_of)
     for g in tflops.values():
         g["frac"] = g["tflops"] / peak
     res = dict(workload=w["name"], value=B * T / (ms * 1e-3), unit="tokens/s", ms_per_step=ms,
-               dtype="bf16" if w["prec"] == "bf16" else "f32", steps=steps, tflops=tflops,
-               roofline=dict(bound="tensor" if w["prec"] == "bf16" else "fp32 CUDA core", kernel=dom,
+               dtype=dict(bf16="bf16", tf32="tf32", fp32="f32")[w["prec"]], steps=steps, tflops=tflops,
+               roofline=dict(bound="fp32 CUDA core" if w["prec"] == "fp32" else "tensor", kernel=dom,
                              achieved=dom_ach, peak=peak, unit="TFLOP/s", frac=dom_ach / peak, peak_source=psrc),
                breakdown={k: dict(ms_per_step=t, ranges_per_step=n) for k, (t, n) in totals.items()},
                l2="a 256 MB buffer written before every timed step (L2 flushed)",
@@ -777,14 +784,16 @@ def measure_other_configs(args, pkg, peaks, src):
     """Configurations 1-4 at full size on one GPU, each with its CPU baseline; a configuration that
     fails reports its error instead of a number."""
     out = {}
-    for cfg in (1, 2, 3, 4):
+    # configuration 2 in both float32 arithmetics: tf32 products (its line) and exact fp32
+    for key, cfg, prec in (("cfg1", 1, None), ("cfg2", 2, None), ("cfg2_fp32", 2, "fp32"), ("cfg3", 3, None),
+                           ("cfg4", 4, None)):
         try:
             if WORKLOADS[cfg].get("decode"):
-                out[f"cfg{cfg}"] = decode_line(args, cfg, pkg, world=1, rank=0)
+                out[key] = decode_line(args, cfg, pkg, world=1, rank=0)
             else:
-                out[f"cfg{cfg}"] = measure_module_config(args, pkg, cfg, peaks, src)
+                out[key] = measure_module_config(args, pkg, cfg, peaks, src, prec)
         except Exception as e:  # reported in the line; the headline number stands on its own
-            out[f"cfg{cfg}"] = dict(workload=WORKLOADS[cfg]["name"], error=f"{type(e).__name__}: {e}"[:300])
+            out[key] = dict(workload=WORKLOADS[cfg]["name"], error=f"{type(e).__name__}: {e}"[:300])
     return out
 
 

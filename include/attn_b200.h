@@ -39,6 +39,9 @@ extern "C" {
 
 #define ATTN_F32 0  /* float32                       */
 #define ATTN_BF16 1 /* bfloat16 (stored as uint16_t) */
+#define ATTN_TF32 2 /* float32 storage, multiplied on the tensor cores as tf32 (10-bit mantissa)
+                       with float32 accumulation; shapes the tensor-core kernels do not take run
+                       the exact float32 CUDA-core path */
 
 /* Epilogue activations of attn_gemm_act (the feed-forward block, model/gpt.py:327-456). */
 #define ATTN_ACT_NONE 0
@@ -185,9 +188,10 @@ int attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
  * model/gpt.py:666-689 (dWo = ctx^T dY, dCtx = dY Wo^T, dWqkv = x^T dQKV, dX = dQKV Wqkv^T).
  *   a_trans = 0: A stored row-major [M][lda] (K contiguous);  1: stored [K][lda] (A = X^T).
  *   b_trans = 0: B stored row-major [K][ldb] (N contiguous);  1: stored [N][ldb] (B = W^T).
- * a_dtype == b_dtype.  ATTN_BF16 operands run on tcgen05 tensor cores (fp32 accumulate);
- * ATTN_F32 operands on the CUDA-core fp32 path.  C is ATTN_F32 or ATTN_BF16; accumulate
- * requires ATTN_F32 C.  bias is float32 or NULL.
+ * a_dtype == b_dtype.  ATTN_BF16 operands run on tcgen05 tensor cores (kind::f16, fp32
+ * accumulate); ATTN_TF32 operands (float32 storage, 16-byte aligned rows) on tcgen05 as tf32
+ * (kind::tf32, fp32 accumulate); ATTN_F32 operands on the CUDA-core fp32 path.  C is ATTN_F32
+ * or ATTN_BF16; accumulate requires ATTN_F32 C.  bias is float32 or NULL.
  */
 int attn_gemm(const void* A, int64_t lda, int a_trans,
               const void* B, int64_t ldb, int b_trans, int ab_dtype,

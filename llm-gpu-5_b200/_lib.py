@@ -19,6 +19,7 @@ ATTN_ERR_CUDA = -3
 ATTN_ERR_WORKSPACE = -4
 ATTN_F32 = 0
 ATTN_BF16 = 1
+ATTN_TF32 = 2
 ATTN_ACT_NONE = 0
 ATTN_ACT_GELU = 1
 ATTN_ACT_GELU_BWD = 2

@@ -124,7 +124,9 @@ static bool make_tmap(CUtensorMap* map, CUtensorMapDataType dt, const void* base
   }
   CUresult r = fn(map, dt, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  swizzle_bytes == 64                    ? CU_TENSOR_MAP_SWIZZLE_64B
+                  : swizzle_bytes == SWIZZLE_128B_ATOM32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                         : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d): rank %d dims %llu x %llu", (int)r, rank,
@@ -187,14 +189,18 @@ int attn_bwd_tc(const void*, const void*, const void*, const void*, const void*,
                 void*, void*, void*, void*, int, int, int, int, const int64_t*, float,
                 cudaStream_t);
 bool tc_gemm_supported(int M, int N, int K, int64_t lda, int a_trans, int64_t ldb, int b_trans,
-                       const void* A, const void* B);
+                       const void* A, const void* B, int tf32);
 int gemm_tc(const void*, int64_t, int, const void*, int64_t, int, void*, int64_t, int,
             const float*, int, int, int, int, cudaStream_t, int act = ACT_NONE, const void* aux = nullptr,
-            int64_t ldaux = 0, int aux_dtype = ATTN_F32);
+            int64_t ldaux = 0, int aux_dtype = ATTN_F32, int tf32 = 0);
 bool tc_gemm_act_ok(const void* C, int64_t ldc, int c_dtype, int act, const void* aux, int64_t ldaux,
                     int aux_dtype);
 
-static size_t elem_size(int dtype) { return dtype == ATTN_F32 ? 4 : 2; }
+static size_t elem_size(int dtype) { return dtype == ATTN_BF16 ? 2 : 4; }
+
+// The attention kernels' arithmetic for a storage type: ATTN_TF32 operands are float32 storage, and
+// the attention kernels serve them with their float32 arithmetic.
+static int attn_arith(int dtype) { return dtype == ATTN_TF32 ? ATTN_F32 : dtype; }
 
 static int check_attn_args(const char* fn, int B, int NH, int T, int D, int dtype,
                            const int64_t* st) {
@@ -254,6 +260,7 @@ int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, i
              int D, int64_t in_sb, int64_t in_st, int64_t in_sh, int64_t out_sb, int64_t out_st,
              int64_t out_sh, float scale, int dtype, void* stream) {
   clear_error();
+  dtype = attn_arith(dtype);
   ATTN_REQUIRE(q && k && v && o && lse, "attn_fwd: null pointer argument");
   const int64_t st[6] = {in_sb, in_st, in_sh, out_sb, out_st, out_sh};
   if (int rc = check_attn_args("attn_fwd", B, NH, T, D, dtype, st)) return rc;
@@ -268,6 +275,7 @@ int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, i
 }
 
 size_t attn_bwd_workspace_size(int B, int NH, int T, int D, int dtype) {
+  dtype = attn_arith(dtype);
   if (B <= 0 || NH <= 0 || T <= 0 || D <= 0) return 0;
   size_t ws = (size_t)B * NH * T * sizeof(float);  // delta = rowsum(dO * O)
   if (tc_bwd_supported(D, T, dtype)) ws = attn_bwd_tc_ws(B, NH, T, D);
@@ -280,6 +288,7 @@ int attn_bwd(const void* q, const void* k, const void* v, const void* o, const v
              int64_t in_sh, int64_t out_sb, int64_t out_st, int64_t out_sh, float scale, int dtype,
              void* stream) {
   clear_error();
+  dtype = attn_arith(dtype);
   ATTN_REQUIRE(q && k && v && o && dout && lse && dq && dk && dv, "attn_bwd: null pointer argument");
   const int64_t st[6] = {in_sb, in_st, in_sh, out_sb, out_st, out_sh};
   if (int rc = check_attn_args("attn_bwd", B, NH, T, D, dtype, st)) return rc;
@@ -307,6 +316,7 @@ int attn_probs(const void* q, const void* k, const float* lse, float* probs, int
                int D, int64_t in_sb, int64_t in_st, int64_t in_sh, float scale, int dtype,
                void* stream) {
   clear_error();
+  dtype = attn_arith(dtype);
   ATTN_REQUIRE(q && k && lse && probs, "attn_probs: null pointer argument");
   ATTN_REQUIRE(dtype == ATTN_F32 || dtype == ATTN_BF16, "attn_probs: bad dtype");
   ATTN_REQUIRE(B > 0 && NH > 0 && T > 0 && D > 0, "attn_probs: sizes must be positive");
@@ -351,16 +361,20 @@ int attn_gemm(const void* A, int64_t lda, int a_trans, const void* B, int64_t ld
   clear_error();
   ATTN_REQUIRE(A && B && C, "attn_gemm: null pointer argument");
   ATTN_REQUIRE(M > 0 && N > 0 && K > 0, "attn_gemm: M, N, K must be positive");
-  ATTN_REQUIRE(ab_dtype == ATTN_F32 || ab_dtype == ATTN_BF16, "attn_gemm: bad operand dtype");
+  ATTN_REQUIRE(ab_dtype == ATTN_F32 || ab_dtype == ATTN_BF16 || ab_dtype == ATTN_TF32,
+               "attn_gemm: bad operand dtype");
   ATTN_REQUIRE(c_dtype == ATTN_F32 || c_dtype == ATTN_BF16, "attn_gemm: bad output dtype");
   ATTN_REQUIRE(!accumulate || c_dtype == ATTN_F32, "attn_gemm: accumulate requires a float32 C");
   ATTN_REQUIRE(lda >= (a_trans ? M : K) && ldb >= (b_trans ? K : N) && ldc >= N,
                "attn_gemm: leading dimensions too small");
-  if (ab_dtype == ATTN_BF16 && tc_gemm_supported(M, N, K, lda, a_trans, ldb, b_trans, A, B))
+  const int tf32 = ab_dtype == ATTN_TF32;
+  if (ab_dtype != ATTN_F32 && tc_gemm_supported(M, N, K, lda, a_trans, ldb, b_trans, A, B, tf32))
     return gemm_tc(A, lda, a_trans, B, ldb, b_trans, C, ldc, c_dtype, bias, M, N, K, accumulate,
-                   as_stream(stream));
-  return gemm_simt(A, lda, a_trans, B, ldb, b_trans, ab_dtype, C, ldc, c_dtype, bias, M, N, K,
-                   accumulate, as_stream(stream));
+                   as_stream(stream), ACT_NONE, nullptr, 0, ATTN_F32, tf32);
+  // shapes the tensor-core kernel does not take: tf32 operands are float32 storage, so the exact
+  // float32 CUDA-core GEMM serves them
+  return gemm_simt(A, lda, a_trans, B, ldb, b_trans, tf32 ? ATTN_F32 : ab_dtype, C, ldc, c_dtype, bias, M, N,
+                   K, accumulate, as_stream(stream));
 }
 
 int attn_gemm_act(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans,
@@ -369,7 +383,8 @@ int attn_gemm_act(const void* A, int64_t lda, int a_trans, const void* B, int64_
   clear_error();
   ATTN_REQUIRE(A && B && C, "attn_gemm_act: null pointer argument");
   ATTN_REQUIRE(M > 0 && N > 0 && K > 0, "attn_gemm_act: M, N, K must be positive");
-  ATTN_REQUIRE(ab_dtype == ATTN_F32 || ab_dtype == ATTN_BF16, "attn_gemm_act: bad operand dtype");
+  ATTN_REQUIRE(ab_dtype == ATTN_F32 || ab_dtype == ATTN_BF16 || ab_dtype == ATTN_TF32,
+               "attn_gemm_act: bad operand dtype");
   ATTN_REQUIRE(c_dtype == ATTN_F32 || c_dtype == ATTN_BF16, "attn_gemm_act: bad output dtype");
   ATTN_REQUIRE(aux_dtype == ATTN_F32 || aux_dtype == ATTN_BF16, "attn_gemm_act: bad aux dtype");
   ATTN_REQUIRE(act == ATTN_ACT_NONE || act == ATTN_ACT_GELU || act == ATTN_ACT_GELU_BWD,
@@ -380,12 +395,13 @@ int attn_gemm_act(const void* A, int64_t lda, int a_trans, const void* B, int64_
   ATTN_REQUIRE(lda >= (a_trans ? M : K) && ldb >= (b_trans ? K : N) && ldc >= N,
                "attn_gemm_act: leading dimensions too small");
   if (act == ATTN_ACT_NONE) aux = nullptr;
-  if (ab_dtype == ATTN_BF16 && tc_gemm_supported(M, N, K, lda, a_trans, ldb, b_trans, A, B) &&
+  const int tf32 = ab_dtype == ATTN_TF32;
+  if (ab_dtype != ATTN_F32 && tc_gemm_supported(M, N, K, lda, a_trans, ldb, b_trans, A, B, tf32) &&
       tc_gemm_act_ok(C, ldc, c_dtype, act, aux, ldaux, aux_dtype))
     return gemm_tc(A, lda, a_trans, B, ldb, b_trans, C, ldc, c_dtype, bias, M, N, K, 0, as_stream(stream), act,
-                   aux, ldaux, aux_dtype);
-  return gemm_simt(A, lda, a_trans, B, ldb, b_trans, ab_dtype, C, ldc, c_dtype, bias, M, N, K, 0,
-                   as_stream(stream), act, aux, ldaux, aux_dtype);
+                   aux, ldaux, aux_dtype, tf32);
+  return gemm_simt(A, lda, a_trans, B, ldb, b_trans, tf32 ? ATTN_F32 : ab_dtype, C, ldc, c_dtype, bias, M, N, K,
+                   0, as_stream(stream), act, aux, ldaux, aux_dtype);
 }
 
 size_t attn_colsum_workspace_size(int M, int N) {

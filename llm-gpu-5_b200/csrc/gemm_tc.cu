@@ -1,13 +1,15 @@
-// tcgen05 tensor-core GEMM for the attention projections (bf16 operands, fp32 accumulation).
+// tcgen05 tensor-core GEMM for the attention projections: bf16 operands (kind::f16) or float32
+// operands read as tf32 (kind::tf32), fp32 accumulation.
 //
 // C[M,N] (=|+=) op(A)[M,K] . op(B)[K,N] (+ bias[N]), C float32 or bf16.  Serves the QKV and
 // output projections of MultiHeadAttention.forward (model/gpt.py:558, :629; matmul_2d_kernel,
 // core/kernels.py:119-140) and the projection gradients of its backward (model/gpt.py:666-689).
 //
 // Persistent, warp-specialised kernel, one CTA per SM:
-//   warp 0      TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 4-stage ring
-//   warp 1      TMEM allocation and the single MMA-issuing thread: 4 x tcgen05.mma (128x256x16)
-//               per 64-deep K block, accumulating in TMEM
+//   warp 0      TMA producer: 128-row A and 256-row B tiles, 128 bytes of K per row (64 bf16 or
+//               32 tf32 elements; 128-byte swizzle), into a 4-stage ring
+//   warp 1      TMEM allocation and the single MMA-issuing thread: 4 x tcgen05.mma (128x256x16
+//               bf16 or 128x256x8 tf32) per K block, accumulating in TMEM
 //   warps 2..   epilogue, groups of four warps (one warp per TMEM lane quarter in each), each group
 //               owning a column span of the tile: tcgen05.ld of the fp32 accumulator (one row per
 //               thread), bias, activation, conversion, then column chunks staged in swizzled shared
@@ -35,9 +37,9 @@
 
 namespace attn {
 
-constexpr int GT_BM = 128, GT_BN = 256, GT_BK = 64, GT_STAGES = 4;
-constexpr int GT_A_BYTES = GT_BM * GT_BK * 2;  // 16 KB
-constexpr int GT_B_BYTES = GT_BN * GT_BK * 2;  // 32 KB
+constexpr int GT_BM = 128, GT_BN = 256, GT_STAGES = 4;
+constexpr int GT_A_BYTES = GT_BM * 128;  // 16 KB: 128 rows x 128 bytes of K (64 bf16 / 32 tf32)
+constexpr int GT_B_BYTES = GT_BN * 128;  // 32 KB
 constexpr int GT_STAGE_BYTES = GT_A_BYTES + GT_B_BYTES;
 constexpr int GT_EPI_STAGING = 32 * 1024;      // output staging: two buffers per epilogue group
 constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + GT_EPI_STAGING + GT_BN * 4 /*bias*/ + 1024 + 256;
@@ -148,7 +150,7 @@ __device__ __forceinline__ void store_chunk_direct(const GemmParams& p, int64_t 
   }
 }
 
-template <int EW>
+template <int EW, bool TF32>
 __global__ void __launch_bounds__(Epi<EW>::kthreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux,
@@ -157,6 +159,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const WaitErr werr = wait_err(p.err);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using E = Epi<EW>;
+  // A K block is 128 bytes of K per row: 64 bf16 or 32 tf32 elements.  MN-major operands arrive as
+  // boxes MNW elements (128 bytes) wide and one K block deep; one MMA-K step spans 16 bf16 / 8 tf32
+  // K rows of such a box.
+  constexpr int BKE = TF32 ? 32 : 64;
+  constexpr int MNW = TF32 ? 32 : 64;
+  constexpr uint32_t MN_BOX = 128u * BKE;        // bytes of one MN-major box
+  constexpr uint32_t MN_KSTEP = 128u * (BKE / 4); // bytes per MMA-K step in an MN-major box
+  // MN-major operands: bf16 in the 128-byte swizzle (8-row atoms), tf32 in the 128-byte swizzle with
+  // 32-byte atomicity (4-row atoms), the only MN-major layout the tf32 MMA reads
+  auto mn_desc = [&](uint32_t addr) {
+    return TF32 ? smem_desc_sw128_atom32(addr, MN_BOX, 512) : smem_desc_sw128(addr, MN_BOX, 1024);
+  };
   uint8_t* epi = smem + GT_STAGES * GT_STAGE_BYTES;  // output staging buffers, two per epilogue group
   float* s_bias = reinterpret_cast<float*>(epi + GT_EPI_STAGING);  // the tile's bias columns
   uint64_t* full = reinterpret_cast<uint64_t*>(s_bias + GT_BN);
@@ -203,18 +217,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           uint8_t* sa = smem + s * GT_STAGE_BYTES;
           uint8_t* sb = sa + GT_A_BYTES;
           mbar_arrive_expect_tx(&full[s], GT_STAGE_BYTES);
-          const int k0 = kb * GT_BK;
+          const int k0 = kb * BKE;
           if (!p.a_mn) {
             tma_load_2d(sa, &tmA, &full[s], k0, tm * GT_BM);
           } else {
-            tma_load_2d(sa, &tmA, &full[s], tm * GT_BM, k0);
-            tma_load_2d(sa + 8192, &tmA, &full[s], tm * GT_BM + 64, k0);
+#pragma unroll
+            for (int j = 0; j < GT_BM / MNW; ++j)
+              tma_load_2d(sa + j * MN_BOX, &tmA, &full[s], tm * GT_BM + MNW * j, k0);
           }
           if (!p.b_mn) {
             tma_load_2d(sb, &tmB, &full[s], k0, tn * GT_BN);
           } else {
 #pragma unroll
-            for (int j = 0; j < GT_BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full[s], tn * GT_BN + 64 * j, k0);
+            for (int j = 0; j < GT_BN / MNW; ++j)
+              tma_load_2d(sb + j * MN_BOX, &tmB, &full[s], tn * GT_BN + MNW * j, k0);
           }
           if (++s == GT_STAGES) { s = 0; ph ^= 1; }
         }
@@ -228,7 +244,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(GT_BM, GT_BN, p.a_mn, p.b_mn);
+      const uint32_t idesc = TF32 ? idesc_tf32_f32(GT_BM, GT_BN, p.a_mn, p.b_mn)
+                                  : idesc_bf16_f32(GT_BM, GT_BN, p.a_mn, p.b_mn);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -247,12 +264,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint32_t sa = smem_u32(smem + s * GT_STAGE_BYTES);
           const uint32_t sb = sa + GT_A_BYTES;
 #pragma unroll
-          for (int k = 0; k < GT_BK / 16; ++k) {
-            const uint64_t ad = p.a_mn ? smem_desc_sw128(sa + k * 2048, 8192, 1024)
-                                       : smem_desc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bd = p.b_mn ? smem_desc_sw128(sb + k * 2048, 8192, 1024)
-                                       : smem_desc_sw128(sb + k * 32, 16, 1024);
-            umma_ss(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {  // four MMA-K steps of 32 bytes per 128-byte K block
+            const uint64_t ad = p.a_mn ? mn_desc(sa + k * MN_KSTEP) : smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = p.b_mn ? mn_desc(sb + k * MN_KSTEP) : smem_desc_sw128(sb + k * 32, 16, 1024);
+            if constexpr (TF32)
+              umma_ss_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            else
+              umma_ss(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
           if (++s == GT_STAGES) { s = 0; ph ^= 1; }
@@ -440,10 +458,11 @@ static int num_sms() {
 }
 
 bool tc_gemm_supported(int M, int N, int K, int64_t lda, int a_trans, int64_t ldb, int b_trans,
-                       const void* A, const void* B) {
+                       const void* A, const void* B, int tf32) {
   (void)a_trans;
   (void)b_trans;
-  return aligned(A, 16) && aligned(B, 16) && lda % 8 == 0 && ldb % 8 == 0 && K >= 16 &&
+  const int64_t q = tf32 ? 4 : 8;  // elements per 16 bytes
+  return aligned(A, 16) && aligned(B, 16) && lda % q == 0 && ldb % q == 0 && K >= 16 &&
          (int64_t)M * N * K >= (int64_t)1 << 21;
 }
 
@@ -477,33 +496,42 @@ bool tc_gemm_act_ok(const void* C, int64_t ldc, int c_dtype, int act, const void
 
 int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans, void* C,
             int64_t ldc, int c_dtype, const float* bias, int M, int N, int K, int accumulate,
-            cudaStream_t s, int act, const void* aux, int64_t ldaux, int aux_dtype) {
+            cudaStream_t s, int act, const void* aux, int64_t ldaux, int aux_dtype, int tf32) {
   if (act != ACT_NONE && (accumulate || !tc_gemm_act_ok(C, ldc, c_dtype, act, aux, ldaux, aux_dtype))) {
     set_error("gemm_tc: activation epilogue unsupported for this output layout");
     return ATTN_ERR_UNSUPPORTED;
   }
+  // operand boxes are 128 bytes wide: 64 bf16 or 32 tf32 elements (one K block, or one MN-major
+  // block of a K block's rows)
+  const uint32_t w = tf32 ? 32 : 64;
+  const uint64_t esz = tf32 ? 4 : 2;
+  auto make_op_map = [&](CUtensorMap* m, const void* base, const uint64_t* dims, const uint64_t* strides,
+                         const uint32_t* box, bool mn_major) {
+    return tf32 ? make_tmap_f32(m, base, 2, dims, strides, box, mn_major ? SWIZZLE_128B_ATOM32 : 128)
+                : make_tmap_bf16(m, base, 2, dims, strides, box);
+  };
   CUtensorMap tmA, tmB;
   {
     uint64_t dims[2], strides[1];
     uint32_t box[2];
     if (!a_trans) {  // A stored [M][lda], K contiguous
-      dims[0] = K; dims[1] = M; box[0] = 64; box[1] = GT_BM;
+      dims[0] = K; dims[1] = M; box[0] = w; box[1] = GT_BM;
     } else {         // A stored [K][lda], M contiguous
-      dims[0] = M; dims[1] = K; box[0] = 64; box[1] = 64;
+      dims[0] = M; dims[1] = K; box[0] = w; box[1] = w;
     }
-    strides[0] = (uint64_t)lda * 2;
-    if (!make_tmap_bf16(&tmA, A, 2, dims, strides, box)) return ATTN_ERR_CUDA;
+    strides[0] = (uint64_t)lda * esz;
+    if (!make_op_map(&tmA, A, dims, strides, box, a_trans != 0)) return ATTN_ERR_CUDA;
   }
   {
     uint64_t dims[2], strides[1];
     uint32_t box[2];
     if (b_trans) {   // B stored [N][ldb], K contiguous
-      dims[0] = K; dims[1] = N; box[0] = 64; box[1] = GT_BN;
+      dims[0] = K; dims[1] = N; box[0] = w; box[1] = GT_BN;
     } else {         // B stored [K][ldb], N contiguous
-      dims[0] = N; dims[1] = K; box[0] = 64; box[1] = 64;
+      dims[0] = N; dims[1] = K; box[0] = w; box[1] = w;
     }
-    strides[0] = (uint64_t)ldb * 2;
-    if (!make_tmap_bf16(&tmB, B, 2, dims, strides, box)) return ATTN_ERR_CUDA;
+    strides[0] = (uint64_t)ldb * esz;
+    if (!make_op_map(&tmB, B, dims, strides, box, b_trans == 0)) return ATTN_ERR_CUDA;
   }
   GemmParams p{};
   p.M = M; p.N = N; p.K = K;
@@ -511,7 +539,7 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   p.b_mn = b_trans ? 0 : 1;
   p.tiles_m = (M + GT_BM - 1) / GT_BM;
   p.tiles_n = (N + GT_BN - 1) / GT_BN;
-  p.kb_total = (K + GT_BK - 1) / GT_BK;
+  p.kb_total = (K + (int)w - 1) / (int)w;
   const int sms = num_sms();
   const int tiles = p.tiles_m * p.tiles_n;
   int splits = c_dtype == ATTN_F32 && act == ACT_NONE ? choose_splits(tiles, p.kb_total, sms) : 1;
@@ -558,15 +586,22 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   }
   if (p.atomic && !accumulate)
     ATTN_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s));
-  static CtxOnce attr4, attr8;
+  static CtxOnce attr[4];
   const int grid = p.units < sms ? p.units : sms;
-  if (wide) {
-    if (!set_smem_limit_once(gemm_tc_kernel<8>, GT_SMEM, attr8)) return ATTN_ERR_CUDA;
-    gemm_tc_kernel<8><<<grid, Epi<8>::kthreads, GT_SMEM, s>>>(tmA, tmB, tmC, tmAux, p);
-  } else {
-    if (!set_smem_limit_once(gemm_tc_kernel<4>, GT_SMEM, attr4)) return ATTN_ERR_CUDA;
-    gemm_tc_kernel<4><<<grid, Epi<4>::kthreads, GT_SMEM, s>>>(tmA, tmB, tmC, tmAux, p);
-  }
+#define GT_LAUNCH(EW, TF, slot)                                                                    \
+  do {                                                                                             \
+    if (!set_smem_limit_once(gemm_tc_kernel<EW, TF>, GT_SMEM, attr[slot])) return ATTN_ERR_CUDA;   \
+    gemm_tc_kernel<EW, TF><<<grid, Epi<EW>::kthreads, GT_SMEM, s>>>(tmA, tmB, tmC, tmAux, p);      \
+  } while (0)
+  if (wide && tf32)
+    GT_LAUNCH(8, true, 3);
+  else if (wide)
+    GT_LAUNCH(8, false, 2);
+  else if (tf32)
+    GT_LAUNCH(4, true, 1);
+  else
+    GT_LAUNCH(4, false, 0);
+#undef GT_LAUNCH
   count_launch();
   return check_launch("gemm_tc_kernel");
 }

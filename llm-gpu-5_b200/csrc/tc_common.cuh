@@ -6,9 +6,9 @@
 //   smem descriptor (64 bit): [0,14) start address >> 4, [16,30) leading-dimension byte offset >> 4,
 //     [32,46) stride-dimension byte offset >> 4, [46,48) version = 1, [49,52) base offset,
 //     [52] LBO mode, [61,64) layout (2 = 128-byte swizzle).
-//   instruction descriptor for kind::f16 (32 bit): [4,6) D format (1 = f32), [7,10) A format
-//     (1 = bf16), [10,13) B format, [15] A major (0 = K, 1 = MN), [16] B major, [17,23) N >> 3,
-//     [24,29) M >> 4.
+//   instruction descriptor for kind::f16 / kind::tf32 (32 bit): [4,6) D format (1 = f32), [7,10)
+//     A format (1 = bf16; 2 = tf32 under kind::tf32), [10,13) B format, [15] A major (0 = K,
+//     1 = MN), [16] B major, [17,23) N >> 3, [24,29) M >> 4.
 // Operand tiles use the 128-byte-swizzle canonical layouts that TMA writes with
 // CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 bytes, 8-row (1024-byte) atoms.
 //   K-major (K contiguous): SBO = 1024 (next 8 rows of M/N); one MMA-K step of 16 bf16 advances
@@ -16,6 +16,10 @@
 //   MN-major (M/N contiguous, 64 elements per 128-byte row, K rows): SBO = 1024 (next 8 K rows),
 //     LBO = byte distance to the next 64-wide M/N block; one MMA-K step (16 K rows) advances the
 //     start address by 2048 bytes.
+//   tf32 operands (4-byte elements) use 128-byte rows holding 32 elements.  K-major: the same
+//   layout, one MMA-K step of 8 advances 32 bytes.  MN-major: the 128-byte swizzle with 32-byte
+//   atomicity (4-row atoms, SBO = 512), blocks 32 elements wide, one MMA-K step = 8 K rows (1024
+//   bytes).
 #pragma once
 
 #include <cuda.h>
@@ -246,6 +250,18 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem] with tf32 operands (float32 in shared memory; the MMA uses
+// their upper 19 bits), fp32 accumulation.  One instruction covers K = 8 (32 bytes per row).
+__device__ __forceinline__ void umma_ss_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]
 __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                         uint32_t idesc, uint32_t accumulate) {
@@ -302,6 +318,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
          ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// MN-major tf32 operands take the 128-byte swizzle with 32-byte atomicity (layout type 1): rows of
+// 128 bytes in 4-row (512-byte) atoms whose 32-byte pieces are permuted by the row within the atom;
+// TMA writes it with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.  SBO is the stride between 4-row atoms
+// along K, LBO the stride between 32-element (128-byte) blocks along M/N.
+__device__ __forceinline__ uint64_t smem_desc_sw128_atom32(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (1ull << 61);
+}
+
 // A descriptor advanced by `bytes` (a multiple of 16) along its start address: the address field
 // is the low 14 bits of the start >> 4 and never carries for shared-memory offsets < 256 KB, so
 // the step is a plain add of a compile-time constant when the caller's loop is unrolled.
@@ -312,12 +337,20 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, in
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor for kind::tf32 (A and B format 2 = TF32, D format 1 = F32).
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
 // ---- host: tensor maps ---------------------------------------------------------------------------
+// swizzle_bytes value selecting CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B (MN-major tf32 operands).
+constexpr int SWIZZLE_128B_ATOM32 = -128;
 // Encode a 2D/3D/4D bf16 tensor map with a 128-byte (or, with swizzle_bytes = 64, 64-byte) swizzle.
 // dims/strides innermost first; strides in bytes for dims 1..rank-1.  Returns false (with the error
 // set) on failure.

@@ -46,8 +46,8 @@ class FeedForward:
         C = config.embedding_dim
         self.hidden = C * 4  # the reference fixes the expansion at 4C whatever hidden_dim says
         self.precision = precision or getattr(config, "attention_precision", "fp32")
-        if self.precision not in ("fp32", "bf16"):
-            raise ValueError(f"precision must be 'fp32' or 'bf16', got {self.precision!r}")
+        if self.precision not in ("fp32", "tf32", "bf16"):
+            raise ValueError(f"precision must be 'fp32', 'tf32' or 'bf16', got {self.precision!r}")
         self.flat_grads = torch.zeros(dp.layout_size(dp.ffn_grad_layout(C)), dtype=torch.float32, device="cuda")
         views = {name: self.flat_grads[off:off + int(np.prod(shape))].view(shape)
                  for name, off, shape in dp.ffn_grad_layout(C)}
@@ -71,6 +71,12 @@ class FeedForward:
     @property
     def _dt(self):
         return torch.bfloat16 if self.precision == "bf16" else torch.float32
+
+    @property
+    def _mm(self):
+        """Operand type of the module's GEMM and attention calls: the storage dtype, or "tf32"
+        (float32 storage multiplied on the tensor cores as tf32)."""
+        return "tf32" if self.precision == "tf32" else self._dt
 
     # ---------------------------------------------------------------- forward
     @device_checked
@@ -112,6 +118,7 @@ class FeedForward:
         C, H = self.config.embedding_dim, self.hidden
         M = B * T
         dt = self._dt
+        mm = self._mm
         if dt == torch.bfloat16:
             with self._rng("cast"):
                 w_fc = self.c_fc_w.bf16_weights()
@@ -122,11 +129,11 @@ class FeedForward:
         act = torch.empty((M, H), dtype=dt, device="cuda")
         pre = torch.empty((M, H), dtype=dt, device="cuda") if training else None
         with self._rng("gemm_fc_gelu"):
-            ops.gemm_act(x_op.data_ptr(), x_op.shape[1], False, w_fc.data_ptr(), H, False, dt, act.data_ptr(), H, dt,
+            ops.gemm_act(x_op.data_ptr(), x_op.shape[1], False, w_fc.data_ptr(), H, False, mm, act.data_ptr(), H, dt,
                          M, H, C, ops.ATTN_ACT_GELU, aux=pre.data_ptr() if pre is not None else None, ldaux=H,
                          aux_dtype=dt, bias=self.c_fc_b.weights.data_ptr())
         with self._rng("gemm_proj"):
-            ops.gemm(act.data_ptr(), H, False, w_proj.data_ptr(), C, False, dt, out.data_ptr(), C, torch.float32,
+            ops.gemm(act.data_ptr(), H, False, w_proj.data_ptr(), C, False, mm, out.data_ptr(), C, torch.float32,
                      M, C, H, bias=self.c_proj_b.weights.data_ptr(), accumulate=accumulate)
         if training:
             self._cache = dict(B=B, T=T, x=x_op, pre=pre, act=act, w_fc=w_fc, w_proj=w_proj)
@@ -145,6 +152,7 @@ class FeedForward:
         C, H = self.config.embedding_dim, self.hidden
         M = B * T
         dt = self._dt
+        mm = self._mm
         dy = _as_tensor(gpu_dOut, M * C).view(M, C)
         # c_proj: dProjB = sum(dOut), dProjW = act^T dOut   (model/gpt.py:431-432)
         if dt == torch.bfloat16:
@@ -155,22 +163,22 @@ class FeedForward:
             with self._rng("colsum"):
                 ops.colsum(dy.data_ptr(), torch.float32, C, M, C, self.c_proj_b.grads, accumulate=accumulate)
         with self._rng("gemm_dwproj"):
-            ops.gemm(c["act"].data_ptr(), H, True, dy_op.data_ptr(), C, False, dt, self.c_proj_w.grads.data_ptr(), C,
+            ops.gemm(c["act"].data_ptr(), H, True, dy_op.data_ptr(), C, False, mm, self.c_proj_w.grads.data_ptr(), C,
                      torch.float32, H, C, M, accumulate=accumulate)
         # dPre = (dOut W_proj^T) * gelu'(pre)   (model/gpt.py:433-436)
         dpre = torch.empty((M, H), dtype=dt, device="cuda")
         with self._rng("gemm_dhidden_gelu"):
-            ops.gemm_act(dy_op.data_ptr(), C, False, c["w_proj"].data_ptr(), C, True, dt, dpre.data_ptr(), H, dt,
+            ops.gemm_act(dy_op.data_ptr(), C, False, c["w_proj"].data_ptr(), C, True, mm, dpre.data_ptr(), H, dt,
                          M, H, C, ops.ATTN_ACT_GELU_BWD, aux=c["pre"].data_ptr(), ldaux=H, aux_dtype=dt)
         # c_fc: dFcW = x^T dPre, dFcB = sum(dPre)   (model/gpt.py:441-442)
         x_op = c["x"]
         if x_op.shape[1] > C:  # ones column: the C + 1 output rows are [dFcW; dFcB], adjacent in flat_grads
             with self._rng("gemm_dwfc"):
-                ops.gemm(x_op.data_ptr(), x_op.shape[1], True, dpre.data_ptr(), H, False, dt,
+                ops.gemm(x_op.data_ptr(), x_op.shape[1], True, dpre.data_ptr(), H, False, mm,
                          self.c_fc_w.grads.data_ptr(), H, torch.float32, C + 1, H, M, accumulate=accumulate)
         else:
             with self._rng("gemm_dwfc"):
-                ops.gemm(x_op.data_ptr(), C, True, dpre.data_ptr(), H, False, dt, self.c_fc_w.grads.data_ptr(), H,
+                ops.gemm(x_op.data_ptr(), C, True, dpre.data_ptr(), H, False, mm, self.c_fc_w.grads.data_ptr(), H,
                          torch.float32, C, H, M, accumulate=accumulate)
             with self._rng("colsum"):
                 ops.colsum(dpre.data_ptr(), dt, H, M, H, self.c_fc_b.grads, accumulate=accumulate)
@@ -179,7 +187,7 @@ class FeedForward:
         # dIn = dPre W_fc^T   (model/gpt.py:443)
         dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_dx"):
-            ops.gemm(dpre.data_ptr(), H, False, c["w_fc"].data_ptr(), H, True, dt, dx.data_ptr(), C, torch.float32,
+            ops.gemm(dpre.data_ptr(), H, False, c["w_fc"].data_ptr(), H, True, mm, dx.data_ptr(), C, torch.float32,
                      M, C, H)
         return DeviceBuffer(dx)
 

@@ -52,7 +52,8 @@ def device_checked(fn):
 
 class GPTConfig:
     """The fields of llm-gpu-5's GPTConfig (model/gpt.py:53-87) that the attention path and its
-    callers read, under the same argument names, plus ``attention_precision`` ("fp32" or "bf16").
+    callers read, under the same argument names, plus ``attention_precision``: "fp32" (the
+    reference's float32 arithmetic), "tf32" (float32 storage, tf32 tensor-core products) or "bf16".
 
     ``attention_impl`` is only carried for the checkpoint metadata (model/gpt.py:1114, :1196-1199);
     the reference's older spellings of it (``attention_mode``, ``use_flash_attention`` /
@@ -64,8 +65,8 @@ class GPTConfig:
                  attention_precision: str = "fp32", **kwargs):
         if embedding_dim % num_heads:
             raise ValueError("embedding_dim must be divisible by num_heads")
-        if attention_precision not in ("fp32", "bf16"):
-            raise ValueError(f"attention_precision must be 'fp32' or 'bf16', got {attention_precision!r}")
+        if attention_precision not in ("fp32", "tf32", "bf16"):
+            raise ValueError(f"attention_precision must be 'fp32', 'tf32' or 'bf16', got {attention_precision!r}")
         self.vocab_size = vocab_size
         self.max_len = max_seq_len if max_seq_len is not None else max_len
         self.embedding_dim = embedding_dim
@@ -225,8 +226,8 @@ class MultiHeadAttention:
         self.config = config
         C = config.embedding_dim
         self.precision = precision or getattr(config, "attention_precision", "fp32")
-        if self.precision not in ("fp32", "bf16"):
-            raise ValueError(f"precision must be 'fp32' or 'bf16', got {self.precision!r}")
+        if self.precision not in ("fp32", "tf32", "bf16"):
+            raise ValueError(f"precision must be 'fp32', 'tf32' or 'bf16', got {self.precision!r}")
 
         # one flat fp32 gradient buffer [dWqkv | dbqkv | dWo | dbo] so data-parallel training
         # all-reduces the four gradients with a single collective
@@ -252,6 +253,12 @@ class MultiHeadAttention:
     @property
     def _dt(self):
         return torch.bfloat16 if self.precision == "bf16" else torch.float32
+
+    @property
+    def _mm(self):
+        """Operand type of the module's GEMM and attention calls: the storage dtype, or "tf32"
+        (float32 storage multiplied on the tensor cores as tf32)."""
+        return "tf32" if self.precision == "tf32" else self._dt
 
     def _shape(self):
         C = self.config.embedding_dim
@@ -332,6 +339,7 @@ class MultiHeadAttention:
         C, NH, D = self._shape()
         M = B * T
         dt = self._dt
+        mm = self._mm
         if dt == torch.bfloat16:
             with self._rng("cast"):
                 w_qkv = self.c_attn_w.bf16_weights()
@@ -341,7 +349,7 @@ class MultiHeadAttention:
         ldx = x_op.shape[1]
         qkv = torch.empty((M, 3 * C), dtype=dt, device="cuda")
         with self._rng("gemm_qkv"):
-            ops.gemm(x_op.data_ptr(), ldx, False, w_qkv.data_ptr(), 3 * C, False, dt, qkv.data_ptr(),
+            ops.gemm(x_op.data_ptr(), ldx, False, w_qkv.data_ptr(), 3 * C, False, mm, qkv.data_ptr(),
                      3 * C, dt, M, 3 * C, C, bias=self.c_attn_b.weights.data_ptr())
         if kv_cache is not None:
             kv_cache.store(qkv.view(B, T, 3 * C), 0)
@@ -355,9 +363,9 @@ class MultiHeadAttention:
         ov = HeadView.tokens(ctx.data_ptr(), T, C, D)
         scale = 1.0 / math.sqrt(D)
         with self._rng("attn_fwd"):
-            ops.attention_forward(qv, kv, vv, ov, lse, B, NH, T, D, scale, dt)
+            ops.attention_forward(qv, kv, vv, ov, lse, B, NH, T, D, scale, mm)
         with self._rng("gemm_out"):
-            ops.gemm(ctx.data_ptr(), C, False, w_o.data_ptr(), C, False, dt, out.data_ptr(), C,
+            ops.gemm(ctx.data_ptr(), C, False, w_o.data_ptr(), C, False, mm, out.data_ptr(), C,
                      torch.float32, M, C, C, bias=self.c_proj_b.weights.data_ptr(), accumulate=accumulate)
         if getattr(self, "training", True):
             self._cache = dict(B=B, T=T, x=x_op, qkv=qkv, ctx=ctx, lse=lse, w_qkv=w_qkv, w_o=w_o)
@@ -372,6 +380,7 @@ class MultiHeadAttention:
         C, NH, D = self._shape()
         M = B * T
         dt = self._dt
+        mm = self._mm
         dy = _as_tensor(gpu_dOut, M * C)
         # output projection: dbo = sum(dY), dWo = ctx^T dY, dCtx = dY Wo^T   (gpt.py:666-670)
         if dt == torch.bfloat16:
@@ -382,11 +391,11 @@ class MultiHeadAttention:
             with self._rng("colsum"):
                 ops.colsum(dy.data_ptr(), torch.float32, C, M, C, self.c_proj_b.grads, accumulate=accumulate)
         with self._rng("gemm_dwo"):
-            ops.gemm(c["ctx"].data_ptr(), C, True, dy_op.data_ptr(), C, False, dt,
+            ops.gemm(c["ctx"].data_ptr(), C, True, dy_op.data_ptr(), C, False, mm,
                      self.c_proj_w.grads.data_ptr(), C, torch.float32, C, C, M, accumulate=accumulate)
         dctx = torch.empty((M, C), dtype=dt, device="cuda")
         with self._rng("gemm_dctx"):
-            ops.gemm(dy_op.data_ptr(), C, False, c["w_o"].data_ptr(), C, True, dt, dctx.data_ptr(), C,
+            ops.gemm(dy_op.data_ptr(), C, False, c["w_o"].data_ptr(), C, True, mm, dctx.data_ptr(), C,
                      dt, M, C, C)
         # attention: softmax VJP + dQ/dK/dV written straight into the [B*T, 3C] layout (gpt.py:672-685)
         dqkv = torch.empty((M, 3 * C), dtype=dt, device="cuda")
@@ -398,19 +407,19 @@ class MultiHeadAttention:
         with self._rng("attn_bwd"):
             ops.attention_backward(tv(qb), tv(qb + C * es), tv(qb + 2 * C * es), ov, dov, c["lse"],
                                    tv(gb), tv(gb + C * es), tv(gb + 2 * C * es), B, NH, T, D,
-                                   1.0 / math.sqrt(D), dt)
+                                   1.0 / math.sqrt(D), mm)
         # input projection: dWqkv = x^T dQKV, dbqkv = sum(dQKV), dX = dQKV Wqkv^T  (gpt.py:687-689)
         x_op = c["x"]
         if x_op.shape[1] > C:
             # x carries a ones column: the C + 1 output rows are [dWqkv; dbqkv], and dbqkv follows
             # dWqkv in the flat gradient buffer, so one GEMM writes both
             with self._rng("gemm_dwqkv"):
-                ops.gemm(x_op.data_ptr(), x_op.shape[1], True, gb, 3 * C, False, dt,
+                ops.gemm(x_op.data_ptr(), x_op.shape[1], True, gb, 3 * C, False, mm,
                          self.c_attn_w.grads.data_ptr(), 3 * C, torch.float32, C + 1, 3 * C, M,
                          accumulate=accumulate)
         else:
             with self._rng("gemm_dwqkv"):
-                ops.gemm(x_op.data_ptr(), C, True, gb, 3 * C, False, dt, self.c_attn_w.grads.data_ptr(),
+                ops.gemm(x_op.data_ptr(), C, True, gb, 3 * C, False, mm, self.c_attn_w.grads.data_ptr(),
                          3 * C, torch.float32, C, 3 * C, M, accumulate=accumulate)
             with self._rng("colsum"):
                 ops.colsum(gb, dt, 3 * C, M, 3 * C, self.c_attn_b.grads, accumulate=accumulate)
@@ -419,7 +428,7 @@ class MultiHeadAttention:
             self._grad_sync_work = dp.allreduce_grads(self.flat_grads, self.grad_sync_group, async_op=True)
         dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_dx"):
-            ops.gemm(gb, 3 * C, False, c["w_qkv"].data_ptr(), 3 * C, True, dt, dx.data_ptr(), C,
+            ops.gemm(gb, 3 * C, False, c["w_qkv"].data_ptr(), 3 * C, True, mm, dx.data_ptr(), C,
                      torch.float32, M, C, 3 * C)
         return DeviceBuffer(dx)
 
@@ -478,6 +487,7 @@ class MultiHeadAttention:
         No backward (inference only; the training caches are left untouched)."""
         C, NH, D = self._shape()
         dt = self._dt
+        mm = self._mm
         L = kv_cache.length
         if kv_cache.B != B or L >= kv_cache.max_len:
             raise RuntimeError(f"forward_decode: cache holds {kv_cache.B} sequences, {L} of "
@@ -490,13 +500,13 @@ class MultiHeadAttention:
         else:
             x_op, w_qkv, w_o = x, self.c_attn_w.weights, self.c_proj_w.weights
         qkv = torch.empty((B, 3 * C), dtype=dt, device="cuda")
-        ops.gemm(x_op.data_ptr(), C, False, w_qkv.data_ptr(), 3 * C, False, dt, qkv.data_ptr(), 3 * C, dt,
+        ops.gemm(x_op.data_ptr(), C, False, w_qkv.data_ptr(), 3 * C, False, mm, qkv.data_ptr(), 3 * C, dt,
                  B, 3 * C, C, bias=self.c_attn_b.weights.data_ptr())
         kv_cache.store(qkv.view(B, 1, 3 * C), L)
         q = qkv[:, :C].contiguous().view(B, NH, D)  # q and the output share one layout
         ctx = ops.decode(q, kv_cache.k[:, :L + 1], kv_cache.v[:, :L + 1], 1.0 / math.sqrt(D))
         out = torch.empty((B, C), dtype=torch.float32, device="cuda")
-        ops.gemm(ctx.data_ptr(), C, False, w_o.data_ptr(), C, False, dt, out.data_ptr(), C, torch.float32,
+        ops.gemm(ctx.data_ptr(), C, False, w_o.data_ptr(), C, False, mm, out.data_ptr(), C, torch.float32,
                  B, C, C, bias=self.c_proj_b.weights.data_ptr())
         return DeviceBuffer(out)
 
@@ -530,7 +540,7 @@ class MultiHeadAttention:
         base = c["qkv"].data_ptr()
         p = ops.attention_probs(HeadView.tokens(base, T, 3 * C, D),
                                 HeadView.tokens(base + C * es, T, 3 * C, D), c["lse"], B, NH, T, D,
-                                1.0 / math.sqrt(D), self._dt)
+                                1.0 / math.sqrt(D), self._mm)
         return p.cpu().numpy()
 
 

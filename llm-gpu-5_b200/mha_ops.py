@@ -13,7 +13,7 @@ import math
 
 import torch
 
-from ._lib import ATTN_ACT_GELU, ATTN_ACT_GELU_BWD, ATTN_ACT_NONE, ATTN_BF16, ATTN_F32, call, lib  # noqa: F401
+from ._lib import ATTN_ACT_GELU, ATTN_ACT_GELU_BWD, ATTN_ACT_NONE, ATTN_BF16, ATTN_F32, ATTN_TF32, call, lib  # noqa: F401
 
 THREADS_PER_BLOCK = 256
 SOFTMAX_BLOCK_THREADS = 64
@@ -21,11 +21,15 @@ SOFTMAX_BLOCK_THREADS = 64
 _DT = {torch.float32: ATTN_F32, torch.bfloat16: ATTN_BF16}
 
 
-def dtype_code(t: torch.dtype) -> int:
+def dtype_code(t) -> int:
+    """Library code of an operand type: torch.float32, torch.bfloat16, or "tf32" (float32 storage
+    multiplied on the tensor cores as tf32)."""
+    if isinstance(t, str) and t == "tf32":
+        return ATTN_TF32
     try:
         return _DT[t]
     except KeyError:
-        raise TypeError(f"unsupported dtype {t}; expected float32 or bfloat16") from None
+        raise TypeError(f"unsupported dtype {t}; expected float32, bfloat16 or 'tf32'") from None
 
 
 def _stream():

@@ -12,8 +12,9 @@ softmax for the forward) on the device with torch, chunk by chunk over the seque
 * the output and dX on sampled sequences (the first, the last and two in between).
 
 The checker computes in float64 for the float32 path (tolerance 1e-5, max|diff| / max|ref|) and in
-float32 with TF32 disabled for the bf16 path (tolerance 2e-2).  Inputs are seeded synthetic data with
-the workloads' distributions: x, dY ~ N(0, 1), weights ~ N(0, 0.02), biases 0.1 * N(0, 1).
+float32 with TF32 disabled for the bf16 and tf32 paths (tolerance 2e-2).  Inputs are seeded
+synthetic data with the workloads' distributions: x, dY ~ N(0, 1), weights ~ N(0, 0.02), biases
+0.1 * N(0, 1).
 """
 import math
 
@@ -119,6 +120,8 @@ def test_long_context_full_batch_32(pkg, cuda_dev):
     _run_and_check(pkg, 32, 1024, 512, 8, "bf16", 2e-2, seed=1003, chunk=8)
 
 
-def test_training_batch_full_256_fp32(pkg, cuda_dev):
-    """Training-batch configuration at full size: B=256, T=128, C=256, NH=8 (head_dim 32), fp32."""
-    _run_and_check(pkg, 256, 128, 256, 8, "fp32", 1e-5, seed=1002, chunk=64)
+@pytest.mark.parametrize("prec,tol", [("fp32", 1e-5), ("tf32", 2e-2)])
+def test_training_batch_full_256(pkg, cuda_dev, prec, tol):
+    """Training-batch configuration at full size: B=256, T=128, C=256, NH=8 (head_dim 32), float32
+    inputs, with float32 arithmetic and with tf32 tensor-core products."""
+    _run_and_check(pkg, 256, 128, 256, 8, prec, tol, seed=1002, chunk=64)

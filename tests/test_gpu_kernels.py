@@ -194,7 +194,7 @@ def test_decode_matches_oracle(pkg, cuda_dev, dtype, B, NH, L, D):
     assert O.rel_err(lse.cpu().numpy(), ref_l) < tol
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype", ["f32", "tf32", "bf16"])
 @pytest.mark.parametrize("M,N,K,at,bt", [(100, 72, 40, 0, 0), (256, 768, 256, 0, 0), (64, 96, 300, 1, 0),
                                          (130, 64, 96, 0, 1), (384, 256, 128, 1, 1), (1024, 2304, 768, 0, 0),
                                          (768, 2304, 4096, 1, 0), (4096, 768, 2304, 0, 1), (512, 512, 8192, 1, 0),
@@ -206,22 +206,24 @@ def test_gemm_matches_numpy(pkg, cuda_dev, dtype, M, N, K, at, bt):
     Bm = rng.standard_normal((N, K) if bt else (K, N)).astype(np.float32)
     bias = rng.standard_normal(N).astype(np.float32)
     C0 = rng.standard_normal((M, N)).astype(np.float32)
-    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32  # storage
+    code = "tf32" if dtype == "tf32" else tdt                    # operand type of the call
     if dtype == "bf16":
         A, Bm = _bf16_round(A), _bf16_round(Bm)
     tA, tB, tbias = _dev(A, tdt), _dev(Bm, tdt), _dev(bias)
     ref = (A.T if at else A).astype(np.float64) @ (Bm.T if bt else Bm).astype(np.float64)
+    # bf16 operands are exact (fp32 accumulation); tf32 keeps 10 mantissa bits of each operand
+    tol = dict(f32=F32_TOL, bf16=1e-3, tf32=5e-3)[dtype]
     for acc in (False, True):
         tC = _dev(C0.copy())
-        pkg.mha_ops.gemm(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, tdt,
+        pkg.mha_ops.gemm(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, code,
                          tC.data_ptr(), N, torch.float32, M, N, K, bias=tbias.data_ptr(), accumulate=acc)
         torch.cuda.synchronize()
         want = ref + bias + (C0 if acc else 0)
-        tol = F32_TOL if dtype == "f32" else 1e-3  # bf16 operands are exact; fp32 accumulation
         assert O.rel_err(tC.cpu().numpy(), want) < tol, (acc, O.rel_err(tC.cpu().numpy(), want))
     # bf16 output
     tCb = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
-    pkg.mha_ops.gemm(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, tdt, tCb.data_ptr(), N,
+    pkg.mha_ops.gemm(tA.data_ptr(), A.shape[1], at, tB.data_ptr(), Bm.shape[1], bt, code, tCb.data_ptr(), N,
                      torch.bfloat16, M, N, K)
     torch.cuda.synchronize()
     assert O.rel_err(tCb.float().cpu().numpy(), ref) < 1e-2

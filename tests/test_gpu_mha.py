@@ -93,6 +93,9 @@ def test_mha_fp32_matches_reference_fixture(pkg, cuda_dev, path):
     (1, 8, 128, 64, 4, "fp32", 1e-5),      # the 'small' preset, full size
     (2, 16, 128, 256, 8, "fp32", 1e-5),    # training-batch shape, batch slice
     (2, 16, 128, 256, 8, "bf16", 2e-2),    # the same on the tensor cores (head_dim 32)
+    (2, 16, 128, 256, 8, "tf32", 2e-2),    # float32 storage, tf32 tensor-core products
+    (5, 2, 512, 768, 12, "tf32", 2e-2),    # data-parallel step shape in tf32, batch slice
+    (1, 4, 100, 128, 2, "tf32", 2e-2),     # ragged T in tf32
     (3, 2, 1024, 512, 8, "bf16", 2e-2),    # long context, batch slice
     (5, 2, 512, 768, 12, "bf16", 2e-2),    # data-parallel step shape, batch slice
     (1, 4, 100, 128, 2, "bf16", 2e-2),     # ragged T on the tensor-core path
