@@ -13,7 +13,7 @@ from ._lib import AttnError, DeviceWaitError, LIB_PATH, clear_device_error, laun
 from . import dp, graphs, mha_ops  # noqa: F401
 from .mha import DeviceBuffer, GPTConfig, KVCache, MultiHeadAttention, Parameter  # noqa: F401
 from .ffn import FeedForward  # noqa: F401
-from .mha_ops import get_shared_mha_module, THREADS_PER_BLOCK, SOFTMAX_BLOCK_THREADS  # noqa: F401
+from .mha_ops import MHAController, get_shared_mha_module, THREADS_PER_BLOCK, SOFTMAX_BLOCK_THREADS  # noqa: F401
 
 __all__ = ["MultiHeadAttention", "FeedForward", "GPTConfig", "Parameter", "DeviceBuffer", "KVCache", "mha_ops", "dp", "graphs", "AttnError", "DeviceWaitError", "clear_device_error",
-           "get_shared_mha_module", "launch_count"]
+           "get_shared_mha_module", "MHAController", "launch_count"]

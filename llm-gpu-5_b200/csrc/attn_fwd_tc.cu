@@ -108,7 +108,7 @@ struct StreamBars {
 };
 static_assert(2 * sizeof(StreamBars) + 16 <= FA_BAR_BYTES, "barrier area too small");
 
-template <bool SINGLES>
+template <bool SINGLES, bool TF32>
 __global__ void __launch_bounds__(FA_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   using TileWalk = attn::TileWalk<SINGLES>;
@@ -195,7 +195,59 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       }
     } else {
       // ---------------- MMA issuer of stream X ----------------
-      if (lane == 0) {
+      if (lane == 0 && TF32) {
+        // tf32: P(j) is written over S(j)'s TMEM columns (as float32 it needs all 128), so S(j+1)
+        // waits until P(j) V(j) has read them; per stream the tensor core alternates P V and S
+        // while the other stream's softmax runs.  Q and K K-major (128-byte swizzle), V MN-major
+        // in the 128-byte swizzle with 32-byte atomicity (the tf32 MMA's only MN-major layout).
+        const uint32_t idesc_s = idesc_tf32_f32(128, 128, 0, 0);
+        const uint32_t idesc_o = idesc_tf32_f32(128, AT_D / 2, 0, 1);
+        const uint32_t tS = tmem + X * FA_TM_STREAM + FA_TM_S;
+        const uint32_t tO = tmem + X * FA_TM_STREAM + FA_TM_O;
+        int pcnt = 0;  // P V MMAs issued
+        int it = 0, kg = 0, vg = 0;
+        bool ok = true;
+        TileWalk cur;
+        for (cur.start(p, X); ok && cur.valid(p); cur.next(p, X), ++it) {
+          const int qs = it & 1;
+          if (!mbar_wait(&sb.q_full[qs], (it >> 1) & 1, werr, 203)) { ok = false; break; }
+          const uint64_t q_desc = smem_desc_sw128(smem_u32(sQ + qs * AT_TILE_BYTES), 16, 1024);
+          for (int j = 0; j <= cur.t + 1 && ok; ++j) {
+            if (j > 0) {
+              // O += P(j-1) V_{j-1} once softmax has written P(j-1) (and rescaled O)
+              const int vs = vg & 1;
+              if (!mbar_wait(&sb.v_full[vs], (vg >> 1) & 1, werr, 205)) { ok = false; break; }
+              if (!mbar_wait(&sb.p_ready, pcnt & 1, werr, 211)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t v_addr = smem_u32(sV + vs * AT_TILE_BYTES);
+#pragma unroll
+              for (int k = 0; k < AT_TILE / 8; ++k)
+                umma_ts_tf32(tO, tS + k * 8, smem_desc_sw128_atom32(v_addr + k * 1024, AT_TILE_BYTES, 512),
+                             idesc_o, (j == 1 && k == 0) ? 0u : 1u);
+              umma_commit(&sb.pv_done);
+              umma_commit(&sb.v_empty[vs]);
+              ++pcnt;
+              ++vg;
+            }
+            if (j <= cur.t) {
+              // S(j) = Q K_j^T over the columns of P(j-1) (or of the previous tile's last P) once
+              // that P V has completed
+              const int ks = kg & 1;
+              if (!mbar_wait(&sb.k_full[ks], (kg >> 1) & 1, werr, 204)) { ok = false; break; }
+              if (pcnt > 0 && !mbar_wait(&sb.pv_done, (pcnt - 1) & 1, werr, 213)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t k_desc = smem_desc_sw128(smem_u32(sK + ks * AT_TILE_BYTES), 16, 1024);
+#pragma unroll
+              for (int k = 0; k < AT_D / 16; ++k)
+                umma_ss_tf32(tS, desc_step(q_desc, k * 32), desc_step(k_desc, k * 32), idesc_s, k > 0 ? 1u : 0u);
+              umma_commit(&sb.s_full);
+              umma_commit(&sb.k_empty[ks]);
+              if (j == cur.t) umma_commit(&sb.q_empty[qs]);  // the tile's last S read Q
+              ++kg;
+            }
+          }
+        }
+      } else if (lane == 0) {
         const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);  // Q K-major, K K-major
         const uint32_t idesc_o = idesc_bf16_f32(128, 64, 0, 1);   // P from TMEM, V MN-major
         const uint32_t tS = tmem + X * FA_TM_STREAM + FA_TM_S;
@@ -283,7 +335,7 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
         tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&sb.s_free);  // S is in registers: the next S may be computed
+        if constexpr (!TF32) mbar_arrive(&sb.s_free);  // S is in registers: the next S may be computed
         if (j == t) {  // diagonal block: key column k is visible to query row r iff k <= r
 #pragma unroll
           for (int i = 0; i < 128; ++i)
@@ -303,9 +355,10 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
         const bool rescale = j > 0 && __any_sync(0xffffffffu, grow_m);
         const float alpha = (j > 0 && grow_m) ? ex2_approx(m - m_cand) : 1.f;
         if (grow_m) m = m_cand;
-        // P = 2^(s*scale*log2e - m) packed to bf16 in registers, the row sum in fp32
+        // P = 2^(s*scale*log2e - m), the row sum in fp32; bf16: packed in registers for the P V MMA;
+        // tf32: float32 in place of S (the MMA reads its upper 19 bits)
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        uint32_t pk[64];
+        uint32_t pk[TF32 ? 1 : 64];
 #pragma unroll
         for (int i = 0; i < 128; i += 4) {
           const float a0 = ex2_approx(fmaf(__uint_as_float(sr[i]), sl2, -m));
@@ -316,23 +369,37 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
           s1 += a1;
           s2 += a2;
           s3 += a3;
-          pk[i / 2] = pack_bf16x2(a0, a1);
-          pk[i / 2 + 1] = pack_bf16x2(a2, a3);
+          if constexpr (TF32) {
+            sr[i] = __float_as_uint(a0);
+            sr[i + 1] = __float_as_uint(a1);
+            sr[i + 2] = __float_as_uint(a2);
+            sr[i + 3] = __float_as_uint(a3);
+          } else {
+            pk[i / 2] = pack_bf16x2(a0, a1);
+            pk[i / 2 + 1] = pack_bf16x2(a2, a3);
+          }
         }
-        // P and O are rewritten once the previous step's P V has completed
+        // P and O are rewritten once the previous step's P V has completed (tf32: already implied,
+        // this step's S was computed after it)
         if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&sb.pv_done, (c - 1) & 1, werr, 208))) { ok = false; break; }
         tc_fence_after();
+        constexpr int OC = TF32 ? AT_D / 2 : AT_D;  // O columns
+        if constexpr (TF32) {
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) tmem_st16(tP + cc * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * cc));
+          for (int cc = 0; cc < 8; ++cc) tmem_st16(tS + cc * 16, *reinterpret_cast<const uint32_t(*)[16]>(sr + 16 * cc));
+        } else {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) tmem_st16(tP + cc * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * cc));
+        }
         if (rescale) {  // O *= 2^(m_old - m_new) on the rows whose max moved (before this P V)
-          uint32_t o[64];
-          tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
-          tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+          uint32_t o[OC];
+#pragma unroll
+          for (int q = 0; q < OC / 32; ++q) tmem_ld32(tO + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(o + 32 * q));
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 64; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          for (int i = 0; i < OC; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) tmem_st16(tO + 16 * q4, *reinterpret_cast<const uint32_t(*)[16]>(o + 16 * q4));
+          for (int q4 = 0; q4 < OC / 16; ++q4) tmem_st16(tO + 16 * q4, *reinterpret_cast<const uint32_t(*)[16]>(o + 16 * q4));
         }
         l *= alpha;
         l += (s0 + s1) + (s2 + s3);
@@ -344,9 +411,10 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       // epilogue: O / l -> bf16 rows, lse = (m + log2 l) * ln 2
       if (!__all_sync(0xffffffffu, mbar_wait(&sb.pv_done, (c - 1) & 1, werr, 209))) break;
       tc_fence_after();
-      uint32_t o[64];
-      tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
-      tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+      constexpr int OC = TF32 ? AT_D / 2 : AT_D;  // O columns: 128 bytes of output per row either way
+      uint32_t o[OC];
+#pragma unroll
+      for (int q = 0; q < OC / 32; ++q) tmem_ld32(tO + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(o + 32 * q));
       tmem_wait_ld();
       tc_fence_before();
       // O rows -> swizzled staging tile -> one TMA store (rows past T are clipped)
@@ -355,12 +423,18 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
       if (!wg_sync()) break;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const uint32_t* src = o + 8 * k;
         uint4 u;
-        u.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
-        u.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-        u.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
-        u.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+        if constexpr (TF32) {
+          const uint32_t* src = o + 4 * k;
+          u = make_uint4(__float_as_uint(__uint_as_float(src[0]) * inv), __float_as_uint(__uint_as_float(src[1]) * inv),
+                         __float_as_uint(__uint_as_float(src[2]) * inv), __float_as_uint(__uint_as_float(src[3]) * inv));
+        } else {
+          const uint32_t* src = o + 8 * k;
+          u.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+          u.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+          u.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+          u.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+        }
         *reinterpret_cast<uint4*>(stg + row * 128 + ((k ^ (row & 7)) << 4)) = u;
       }
       fence_proxy_async_smem();
@@ -387,31 +461,43 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
 // ==========================================================================================
 // host side
 // ==========================================================================================
-bool tc_fwd_supported(int D, int dtype) { return tc_head_dim_ok(D) && dtype == ATTN_BF16; }
+bool tc_fwd_supported(int D, int dtype) {
+  return dtype == ATTN_BF16 ? tc_head_dim_ok(D) : dtype == ATTN_TF32 ? tc_head_dim_ok_tf32(D) : false;
+}
 
 // Whether n tensors with the element strides s[0..5] (input b/t/h, output b/t/h) can go through
 // the TMA maps of the tensor-core kernels: 16-byte aligned bases, strides in 16-byte steps.
-bool tc_attn_layout_ok(const void* const* ptrs, int n, const int64_t* s, int D) {
-  if (!head_strides_ok(s[0], s[1], s[2], D) || !head_strides_ok(s[3], s[4], s[5], D)) return false;
+bool tc_attn_layout_ok(const void* const* ptrs, int n, const int64_t* s, int D, int esz) {
+  auto ok = [&](int64_t sb, int64_t st, int64_t sh) {
+    return esz == 4 ? head_strides_ok_f32(sb, st, sh, D) : head_strides_ok(sb, st, sh, D);
+  };
+  if (!ok(s[0], s[1], s[2]) || !ok(s[3], s[4], s[5])) return false;
   for (int i = 0; i < n; ++i)
     if (!aligned(ptrs[i], 16)) return false;
   return true;
 }
 
+// tf32 != 0: float32 q/k/v/o (head_dim <= 32) multiplied as tf32; otherwise bf16 (head_dim <= 64).
 int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse, int B, int NH, int T,
-                int D, const int64_t* s, float scale, cudaStream_t stream) {
-  if (!head_strides_ok(s[0], s[1], s[2], D) || !head_strides_ok(s[3], s[4], s[5], D) || !aligned(q, 16) || !aligned(k, 16) ||
-      !aligned(v, 16) || !aligned(o, 16)) {
-    set_error("attn_fwd: the tensor-core path needs 16-byte aligned bf16 tensors with strides that are "
-              "multiples of 8 elements");
+                int D, const int64_t* s, float scale, cudaStream_t stream, int tf32) {
+  const void* tens[4] = {q, k, v, o};
+  if (!tc_attn_layout_ok(tens, 4, s, D, tf32 ? 4 : 2)) {
+    set_error("attn_fwd: the tensor-core path needs 16-byte aligned tensors with strides in 16-byte steps");
     return ATTN_ERR_ARG;
   }
   FwdMaps maps;
-  if (!make_head_map(&maps.q, q, B, NH, T, D, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.k, k, B, NH, T, D, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.v, v, B, NH, T, D, s[0], s[1], s[2]) ||
-      !make_head_map(&maps.o, o, B, NH, T, D, s[3], s[4], s[5]))
+  if (tf32) {
+    if (!make_head_map_f32(&maps.q, q, B, NH, T, D, s[0], s[1], s[2], 128) ||
+        !make_head_map_f32(&maps.k, k, B, NH, T, D, s[0], s[1], s[2], 128) ||
+        !make_head_map_f32(&maps.v, v, B, NH, T, D, s[0], s[1], s[2], SWIZZLE_128B_ATOM32) ||
+        !make_head_map_f32(&maps.o, o, B, NH, T, D, s[3], s[4], s[5], 128))
+      return ATTN_ERR_CUDA;
+  } else if (!make_head_map(&maps.q, q, B, NH, T, D, s[0], s[1], s[2]) ||
+             !make_head_map(&maps.k, k, B, NH, T, D, s[0], s[1], s[2]) ||
+             !make_head_map(&maps.v, v, B, NH, T, D, s[0], s[1], s[2]) ||
+             !make_head_map(&maps.o, o, B, NH, T, D, s[3], s[4], s[5])) {
     return ATTN_ERR_CUDA;
+  }
   FwdParams p;
   p.NH = NH;
   p.T = T;
@@ -426,19 +512,24 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   const bool singles = (int64_t)p.BH * p.npairs < (int64_t)8 * 2 * sms;
   const int64_t units = (int64_t)p.BH * (singles ? p.nq : p.npairs);
   const int grid = (int)((units + 1) / 2 < sms ? (units + 1) / 2 : sms);  // at least a unit per stream
-  static CtxOnce attr_pairs, attr_singles;
-  static int regs_pairs = 0, regs_singles = 0;
-  if (singles) {
-    if (!set_smem_limit_once(attn_fwd_tc_kernel<true>, FA_SMEM, attr_singles) ||
-        !launch_regs_match(attn_fwd_tc_kernel<true>, FA_LAUNCH_REGS, regs_singles, "attn_fwd_tc_kernel"))
-      return ATTN_ERR_CUDA;
-    attn_fwd_tc_kernel<true><<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);
-  } else {
-    if (!set_smem_limit_once(attn_fwd_tc_kernel<false>, FA_SMEM, attr_pairs) ||
-        !launch_regs_match(attn_fwd_tc_kernel<false>, FA_LAUNCH_REGS, regs_pairs, "attn_fwd_tc_kernel"))
-      return ATTN_ERR_CUDA;
-    attn_fwd_tc_kernel<false><<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);
-  }
+  static CtxOnce attr[4];
+  static int regs[4] = {0, 0, 0, 0};
+#define FA_LAUNCH(SG, TF, slot)                                                                          \
+  do {                                                                                                   \
+    if (!set_smem_limit_once(attn_fwd_tc_kernel<SG, TF>, FA_SMEM, attr[slot]) ||                         \
+        !launch_regs_match(attn_fwd_tc_kernel<SG, TF>, FA_LAUNCH_REGS, regs[slot], "attn_fwd_tc_kernel")) \
+      return ATTN_ERR_CUDA;                                                                              \
+    attn_fwd_tc_kernel<SG, TF><<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);                          \
+  } while (0)
+  if (singles && tf32)
+    FA_LAUNCH(true, true, 3);
+  else if (singles)
+    FA_LAUNCH(true, false, 1);
+  else if (tf32)
+    FA_LAUNCH(false, true, 2);
+  else
+    FA_LAUNCH(false, false, 0);
+#undef FA_LAUNCH
   count_launch();
   return check_launch("attn_fwd_tc_kernel");
 }

@@ -34,6 +34,20 @@ __device__ __forceinline__ void axpy4(float4& acc, float s, float4 x) {
 }
 __device__ __forceinline__ void scale4(float4& a, float s) { a.x *= s; a.y *= s; a.z *= s; a.w *= s; }
 
+// x as the tf32 tensor cores read it (the 13 low mantissa bits ignored), when TF32S; else x.
+// The backward after a tf32 forward recomputes its scores from these values, so that
+// P = exp(scale*q.k - lse) matches the probabilities the forward's lse was computed from.
+template <bool TF32S>
+__device__ __forceinline__ float4 score_operand(float4 x) {
+  if constexpr (TF32S) {
+    const uint32_t m = 0xffffe000u;
+    return make_float4(__uint_as_float(__float_as_uint(x.x) & m), __uint_as_float(__float_as_uint(x.y) & m),
+                       __uint_as_float(__float_as_uint(x.z) & m), __uint_as_float(__float_as_uint(x.w) & m));
+  } else {
+    return x;
+  }
+}
+
 template <int TPR> __device__ __forceinline__ float row_reduce(float v) {
 #pragma unroll
   for (int off = TPR / 2; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -165,7 +179,7 @@ attn_bwd_delta_kernel(const T* __restrict__ o, const T* __restrict__ dout, float
 // ------------------------------------------------------------------------------------------
 constexpr int KV_BN = 64, KV_BQ = 32;
 
-template <typename T, int D>
+template <typename T, int D, bool TF32S = false>
 __global__ void __launch_bounds__(KV_BN * RowSplit<D>::TPR)
 attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                      const T* __restrict__ dout, const float* __restrict__ lse,
@@ -188,7 +202,7 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int64_t e = in_off + key * st.in_st + (i * TPR + part) * 4;
-    kr[i] = key < T_ ? load4(k + e) : make_float4(0, 0, 0, 0);
+    kr[i] = key < T_ ? score_operand<TF32S>(load4(k + e)) : make_float4(0, 0, 0, 0);  // scores only
     vr[i] = key < T_ ? load4(v + e) : make_float4(0, 0, 0, 0);
     dkr[i] = make_float4(0, 0, 0, 0);
     dvr[i] = make_float4(0, 0, 0, 0);
@@ -219,7 +233,7 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
       float s = 0.f, dp = 0.f;
 #pragma unroll
       for (int c = 0; c < NV; ++c) {
-        s += dot4(Qs[i][c * TPR + part], kr[c]);
+        s += dot4(score_operand<TF32S>(Qs[i][c * TPR + part]), kr[c]);
         dp += dot4(Gs[i][c * TPR + part], vr[c]);
       }
       s = row_reduce<TPR>(s);
@@ -249,7 +263,7 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
 // ------------------------------------------------------------------------------------------
 constexpr int DQ_BM = 64, DQ_BN = 32;
 
-template <typename T, int D>
+template <typename T, int D, bool TF32S = false>
 __global__ void __launch_bounds__(DQ_BM * RowSplit<D>::TPR)
 attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                    const T* __restrict__ dout, const float* __restrict__ lse,
@@ -270,7 +284,8 @@ attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
   float4 qr[NV], gr[NV], dqr[NV];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    qr[i] = row < T_ ? load4(q + in_off + row * st.in_st + (i * TPR + part) * 4) : make_float4(0, 0, 0, 0);
+    qr[i] = row < T_ ? score_operand<TF32S>(load4(q + in_off + row * st.in_st + (i * TPR + part) * 4))
+                     : make_float4(0, 0, 0, 0);  // scores only
     gr[i] = row < T_ ? load4(dout + out_off + row * st.out_st + (i * TPR + part) * 4) : make_float4(0, 0, 0, 0);
     dqr[i] = make_float4(0, 0, 0, 0);
   }
@@ -299,7 +314,7 @@ attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
       float s = 0.f, dp = 0.f;
 #pragma unroll
       for (int c = 0; c < NV; ++c) {
-        s += dot4(qr[c], Ks[j][c * TPR + part]);
+        s += dot4(qr[c], score_operand<TF32S>(Ks[j][c * TPR + part]));
         dp += dot4(gr[c], Vs[j][c * TPR + part]);
       }
       s = row_reduce<TPR>(s);
@@ -330,7 +345,7 @@ static int fwd_simt_d(const void* q, const void* k, const void* v, void* o, floa
   return check_launch("attn_fwd_simt_kernel");
 }
 
-template <typename T, int D>
+template <typename T, int D, bool TF32S = false>
 static int bwd_simt_d(const void* q, const void* k, const void* v, const void* o, const void* dout,
                       const float* lse, void* dq, void* dk, void* dv, float* delta, int B, int NH,
                       int T_, AttnStrides st, float scale, cudaStream_t s) {
@@ -343,14 +358,14 @@ static int bwd_simt_d(const void* q, const void* k, const void* v, const void* o
   int rc = check_launch("attn_bwd_delta_kernel");
   if (rc) return rc;
   dim3 g1((T_ + KV_BN - 1) / KV_BN, B * NH);
-  attn_bwd_dkdv_kernel<T, D><<<g1, KV_BN * RowSplit<D>::TPR, 0, s>>>(
+  attn_bwd_dkdv_kernel<T, D, TF32S><<<g1, KV_BN * RowSplit<D>::TPR, 0, s>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, delta, (T*)dk, (T*)dv, NH, T_,
       st, scale);
   count_launch();
   rc = check_launch("attn_bwd_dkdv_kernel");
   if (rc) return rc;
   dim3 g2((T_ + DQ_BM - 1) / DQ_BM, B * NH);
-  attn_bwd_dq_kernel<T, D><<<g2, DQ_BM * RowSplit<D>::TPR, 0, s>>>(
+  attn_bwd_dq_kernel<T, D, TF32S><<<g2, DQ_BM * RowSplit<D>::TPR, 0, s>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, delta, (T*)dq, NH, T_, st,
       scale);
   count_launch();
@@ -386,6 +401,12 @@ static int bwd_f32(const void* q, const void* k, const void* v, const void* o, c
   return bwd_simt_d<float, D>(q, k, v, o, dout, lse, dq, dk, dv, delta, B, NH, T_, st, scale, s);
 }
 template <int D>
+static int bwd_tf32(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                    const float* lse, void* dq, void* dk, void* dv, float* delta, int B, int NH,
+                    int T_, AttnStrides st, float scale, cudaStream_t s) {
+  return bwd_simt_d<float, D, true>(q, k, v, o, dout, lse, dq, dk, dv, delta, B, NH, T_, st, scale, s);
+}
+template <int D>
 static int bwd_bf16(const void* q, const void* k, const void* v, const void* o, const void* dout,
                     const float* lse, void* dq, void* dk, void* dv, float* delta, int B, int NH,
                     int T_, AttnStrides st, float scale, cudaStream_t s) {
@@ -408,6 +429,9 @@ int attn_bwd_simt(const void* q, const void* k, const void* v, const void* o, co
   AttnStrides st{strides[0], strides[1], strides[2], strides[3], strides[4], strides[5]};
   if (dtype == ATTN_F32) {
     ATTN_DISPATCH_D(D, bwd_f32, q, k, v, o, dout, lse, dq, dk, dv, delta, B, NH, T_, st, scale, s);
+  }
+  if (dtype == ATTN_TF32) {  // float32 storage after a tf32 forward: scores from tf32 q and k
+    ATTN_DISPATCH_D(D, bwd_tf32, q, k, v, o, dout, lse, dq, dk, dv, delta, B, NH, T_, st, scale, s);
   }
   ATTN_DISPATCH_D(D, bwd_bf16, q, k, v, o, dout, lse, dq, dk, dv, delta, B, NH, T_, st, scale, s);
 }

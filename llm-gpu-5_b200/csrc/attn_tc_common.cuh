@@ -68,6 +68,36 @@ inline bool make_head_map(TileMap* tm, const void* base, int B, int NH, int T, i
   return make_tmap_bf16(&tm->map, base, 4, dims, strides, box);
 }
 
+// The same map over a float32 tensor (the tf32 path, head_dim <= 32): 128-byte rows of 32 elements,
+// columns D..31 read as zeros.  swizzle_bytes selects the shared-memory layout (128, or
+// SWIZZLE_128B_ATOM32 for operands the tf32 MMA reads MN-major).
+inline bool make_head_map_f32(TileMap* tm, const void* base, int B, int NH, int T, int D, int64_t sb,
+                              int64_t st, int64_t sh, int swizzle_bytes) {
+  uint64_t dims[4], strides[3];
+  uint32_t box[4];
+  tm->h_first = sh <= st ? 1 : 0;
+  dims[0] = D;
+  box[0] = AT_D / 2;
+  if (tm->h_first) {
+    dims[1] = NH; dims[2] = T; dims[3] = B;
+    strides[0] = sh * 4; strides[1] = st * 4; strides[2] = sb * 4;
+    box[1] = 1; box[2] = AT_TILE; box[3] = 1;
+  } else {
+    dims[1] = T; dims[2] = NH; dims[3] = B;
+    strides[0] = st * 4; strides[1] = sh * 4; strides[2] = sb * 4;
+    box[1] = AT_TILE; box[2] = 1; box[3] = 1;
+  }
+  return make_tmap_f32(&tm->map, base, 4, dims, strides, box, swizzle_bytes);
+}
+
+// head_dim values of the tf32 tensor-core forward: multiples of 4 (16-byte rows) up to 32.
+inline bool tc_head_dim_ok_tf32(int D) { return D >= 4 && D <= AT_D / 2 && D % 4 == 0; }
+
+// Element strides usable by TMA for float32 tensors: 16-byte multiples.
+inline bool head_strides_ok_f32(int64_t sb, int64_t st, int64_t sh, int D) {
+  return sb % 4 == 0 && st % 4 == 0 && sh % 4 == 0 && st >= D;
+}
+
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Streaming multiprocessors of the current device (cached per device).

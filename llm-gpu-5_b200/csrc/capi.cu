@@ -180,9 +180,9 @@ int wait_selftest(int, cudaStream_t);
 int decode(const void*, const void*, const void*, void*, float*, int, int, int, int, int64_t,
            int64_t, int64_t, int64_t, int64_t, float, int, float*, cudaStream_t);
 bool tc_fwd_supported(int D, int dtype);
-bool tc_attn_layout_ok(const void* const* ptrs, int n, const int64_t* s, int D);
+bool tc_attn_layout_ok(const void* const* ptrs, int n, const int64_t* s, int D, int esz);
 int attn_fwd_tc(const void*, const void*, const void*, void*, float*, int, int, int, int,
-                const int64_t*, float, cudaStream_t);
+                const int64_t*, float, cudaStream_t, int tf32);
 bool tc_bwd_supported(int D, int T, int dtype);
 size_t attn_bwd_tc_ws(int B, int NH, int T, int D);
 int attn_bwd_tc(const void*, const void*, const void*, const void*, const void*, const float*,
@@ -260,6 +260,7 @@ int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, i
              int D, int64_t in_sb, int64_t in_st, int64_t in_sh, int64_t out_sb, int64_t out_st,
              int64_t out_sh, float scale, int dtype, void* stream) {
   clear_error();
+  const int requested = dtype;  // ATTN_TF32 selects the tf32 tensor-core forward where it applies
   dtype = attn_arith(dtype);
   ATTN_REQUIRE(q && k && v && o && lse, "attn_fwd: null pointer argument");
   const int64_t st[6] = {in_sb, in_st, in_sh, out_sb, out_st, out_sh};
@@ -269,8 +270,8 @@ int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, i
                "attn_fwd: q/k/v/o must be %zu-byte aligned", a);
   const void* tens[4] = {q, k, v, o};
   // tensor-core path for bf16 head_dim <= 64 whenever the layout suits TMA; CUDA cores otherwise
-  if (tc_fwd_supported(D, dtype) && tc_attn_layout_ok(tens, 4, st, D))
-    return attn_fwd_tc(q, k, v, o, lse, B, NH, T, D, st, scale, as_stream(stream));
+  if (tc_fwd_supported(D, requested) && tc_attn_layout_ok(tens, 4, st, D, (int)elem_size(dtype)))
+    return attn_fwd_tc(q, k, v, o, lse, B, NH, T, D, st, scale, as_stream(stream), requested == ATTN_TF32);
   return attn_fwd_simt(q, k, v, o, lse, B, NH, T, D, st, scale, dtype, as_stream(stream));
 }
 
@@ -288,6 +289,7 @@ int attn_bwd(const void* q, const void* k, const void* v, const void* o, const v
              int64_t in_sh, int64_t out_sb, int64_t out_st, int64_t out_sh, float scale, int dtype,
              void* stream) {
   clear_error();
+  const int requested = dtype;  // ATTN_TF32: scores recomputed from tf32 q and k (see attn_bwd_simt)
   dtype = attn_arith(dtype);
   ATTN_REQUIRE(q && k && v && o && dout && lse && dq && dk && dv, "attn_bwd: null pointer argument");
   const int64_t st[6] = {in_sb, in_st, in_sh, out_sb, out_st, out_sh};
@@ -305,11 +307,11 @@ int attn_bwd(const void* q, const void* k, const void* v, const void* o, const v
                "attn_bwd: tensors must be %zu-byte aligned", a);
   const void* tens[8] = {q, k, v, o, dout, dq, dk, dv};
   // the tensor-core workspace (attn_bwd_workspace_size) also covers the CUDA-core path
-  if (tc_bwd_supported(D, T, dtype) && tc_attn_layout_ok(tens, 8, st, D))
+  if (tc_bwd_supported(D, T, dtype) && tc_attn_layout_ok(tens, 8, st, D, 2))
     return attn_bwd_tc(q, k, v, o, dout, lse, dq, dk, dv, workspace, B, NH, T, D, st, scale,
                        as_stream(stream));
   return attn_bwd_simt(q, k, v, o, dout, lse, dq, dk, dv, (float*)workspace, B, NH, T, D, st, scale,
-                       dtype, as_stream(stream));
+                       requested, as_stream(stream));
 }
 
 int attn_probs(const void* q, const void* k, const float* lse, float* probs, int B, int NH, int T,

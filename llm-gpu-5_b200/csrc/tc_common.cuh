@@ -262,6 +262,18 @@ __device__ __forceinline__ void umma_ss_tf32(uint32_t d_tmem, uint64_t a_desc, u
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem] with tf32 operands (A: one float32 per TMEM column, 8 columns per
+// instruction; B float32 in shared memory), fp32 accumulation.
+__device__ __forceinline__ void umma_ts_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]
 __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                         uint32_t idesc, uint32_t accumulate) {

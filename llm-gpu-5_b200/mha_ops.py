@@ -254,3 +254,58 @@ _SHARED = _SharedModule()
 
 def get_shared_mha_module():
     return _SHARED
+
+
+class MHAController:
+    """The reference's sandbox attention controller (core/mha_ops.py:55-138) on this library.
+
+    ``forward(X[H, M, Din], W_qkv[Din, 3D])`` runs the fused-QKV causal attention pass on host
+    float32 arrays and returns ``(out[H, M, D], probs[H, M, M])`` as the reference's does: the
+    fused projection ``X W_qkv`` (matmul_qkv_fused, core/mha_kernels.py:689-720) is one float32
+    GEMM; the reference's split into contiguous Q/K/V (split_qkv_kernel, :722-) is folded into the
+    attention's strides (it reads Q, K and V straight out of the fused [H*M, 3D] buffer); the causal
+    attention (fused_attention_forward_kernel) runs on the float32 kernels and writes the row
+    log-sum-exp, from which ``probs`` is rebuilt on the device.  Inputs are copied to the device
+    and the results back, as in the reference.  ``H, M, D`` fix the attention shape; ``module`` is
+    accepted for signature compatibility.
+    """
+
+    def __init__(self, H: int, M: int, D: int, module=None):
+        self.H, self.M, self.D = int(H), int(M), int(D)
+        self.scale = 1.0 / math.sqrt(D)
+        self.module = module if module is not None else get_shared_mha_module()
+
+    def _fused(self, gX, gW, Din: int) -> torch.Tensor:
+        H, M, D = self.H, self.M, self.D
+        fused = torch.empty((H * M, 3 * D), dtype=torch.float32, device="cuda")
+        gemm(gX.data_ptr(), Din, False, gW.data_ptr(), 3 * D, False, torch.float32, fused.data_ptr(), 3 * D,
+             torch.float32, H * M, 3 * D, Din)
+        return fused
+
+    def matmul_qkv_fused(self, gpu_X, gpu_W, gpu_fused, Din: int, block=None, grid=None):
+        """Fused[H, M, 3D] = X[H, M, Din] @ W_qkv[Din, 3D] on device buffers (the launch
+        configuration arguments of the reference are accepted and unused)."""
+        H, M, D = self.H, self.M, self.D
+        gemm(ptr(gpu_X), Din, False, ptr(gpu_W), 3 * D, False, torch.float32, ptr(gpu_fused), 3 * D,
+             torch.float32, H * M, 3 * D, int(Din))
+
+    def forward(self, X, W_qkv):
+        import numpy as np
+        H, M, D = self.H, self.M, self.D
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        W_qkv = np.ascontiguousarray(W_qkv, dtype=np.float32)
+        if X.shape[:2] != (H, M) or W_qkv.shape != (X.shape[-1], 3 * D):
+            raise ValueError(f"MHAController({H}, {M}, {D}): X {X.shape} / W_qkv {W_qkv.shape} do not match")
+        Din = X.shape[-1]
+        gX = torch.from_numpy(X).cuda().view(H * M, Din)
+        gW = torch.from_numpy(W_qkv).cuda()
+        fused = self._fused(gX, gW, Din)
+        base, es = fused.data_ptr(), fused.element_size()
+        # heads as batch entries of one head each: element (h, m, d) of Q/K/V at h*M*3D + m*3D + d
+        qv, kv, vv = (HeadView(base + i * D * es, M * 3 * D, 3 * D, D) for i in range(3))
+        out = torch.empty((H, M, D), dtype=torch.float32, device="cuda")
+        lse = torch.empty((H, 1, M), dtype=torch.float32, device="cuda")
+        attention_forward(qv, kv, vv, HeadView(out.data_ptr(), M * D, D, D), lse, H, 1, M, D, self.scale,
+                          torch.float32)
+        probs = attention_probs(qv, kv, lse, H, 1, M, D, self.scale, torch.float32)
+        return out.cpu().numpy(), probs.view(H, M, M).cpu().numpy()

@@ -1,7 +1,8 @@
 """GPU parity of the attention kernels against the oracle, through the C ABI.
 
 Tolerances (max|Δ|/max|ref| per tensor, ``rel_err``): float32 path 1e-5; bf16 tensor-core path
-2e-2, with the oracle evaluated on the same bf16-rounded inputs.  The reference's own
+2e-2, with the oracle evaluated on the same bf16-rounded inputs; tf32 tensor-core path (float32
+inputs) 2e-2.  The reference's own
 assert_allclose tolerance (rtol=1e-4, atol=1e-5, test_mha_golden_model.py:45) is also applied to
 the float32 path on its golden fixture.
 """
@@ -41,7 +42,8 @@ def _run_attention(pkg, q, k, v, do, dtype, layout):
     torch = _torch()
     ops = pkg.mha_ops
     B, NH, T, D = q.shape
-    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32  # storage (tf32: float32)
+    code = "tf32" if dtype == "tf32" else tdt                    # operand type of the calls
     if layout == "heads":
         def put(a):
             return _dev(a.astype(np.float32), tdt).contiguous()
@@ -73,8 +75,8 @@ def _run_attention(pkg, q, k, v, do, dtype, layout):
             return tg[:, i * C:(i + 1) * C].float().cpu().numpy().reshape(B, T, NH, D).transpose(0, 2, 1, 3)
     lse = torch.empty((B, NH, T), dtype=torch.float32, device="cuda")
     scale = 1.0 / math.sqrt(D)
-    ops.attention_forward(qv, kv, vv, ov, lse, B, NH, T, D, scale, tdt)
-    ops.attention_backward(qv, kv, vv, ov, dov, lse, dqv, dkv, dvv, B, NH, T, D, scale, tdt)
+    ops.attention_forward(qv, kv, vv, ov, lse, B, NH, T, D, scale, code)
+    ops.attention_backward(qv, kv, vv, ov, dov, lse, dqv, dkv, dvv, B, NH, T, D, scale, code)
     torch.cuda.synchronize()
     if layout == "heads":
         res = (get(to), lse.cpu().numpy(), get(tdq), get(tdk), get(tdv))
@@ -123,7 +125,23 @@ def test_attention_bf16_matches_oracle(pkg, cuda_dev, B, NH, T, D, layout):
         assert O.rel_err(g, r) < BF16_TOL, (name, O.rel_err(g, r))
 
 
-@pytest.mark.parametrize("dtype,D", [("bf16", 64), ("bf16", 32), ("f32", 64)])
+@pytest.mark.parametrize("B,NH,T,D", [(1, 2, 128, 32), (2, 2, 200, 32), (1, 2, 384, 32), (2, 3, 130, 16),
+                                      (2, 4, 128, 8), (1, 3, 257, 16), (1, 2, 77, 4), (2, 2, 1024, 32),
+                                      (40, 4, 200, 32), (256, 8, 128, 32)])
+@pytest.mark.parametrize("layout", ["heads", "tokens"])
+def test_attention_tf32_matches_oracle(pkg, cuda_dev, B, NH, T, D, layout):
+    """float32 inputs with the forward on the tf32 tensor cores (head_dim <= 32; the backward runs
+    the float32 CUDA-core kernels on the tf32 forward's O and lse), against the oracle on the same
+    float32 inputs at 2e-2."""
+    q, k, v, do = _inputs(B, NH, T, D, seed=11 + T + D)
+    got = _run_attention(pkg, q, k, v, do, "tf32", layout)
+    ref = _oracle(q, k, v, do)
+    for name, g, r in zip(("o", "lse", "dq", "dk", "dv"), got, ref):
+        assert O.rel_err(g, r) < BF16_TOL, (name, O.rel_err(g, r))
+    assert pkg.lib.attn_device_error(1) == 0
+
+
+@pytest.mark.parametrize("dtype,D", [("bf16", 64), ("bf16", 32), ("f32", 64), ("tf32", 32)])
 def test_attention_long_rows(pkg, cuda_dev, dtype, D):
     """T = 2048 (16 key tiles per row) with large scores whose row maximum keeps growing along the
     keys: the forward's lazy rescaling (the running max moves only when it grows by more than 2^8)
@@ -140,7 +158,7 @@ def test_attention_long_rows(pkg, cuda_dev, dtype, D):
         q, k, v, do = (_bf16_round(a) for a in (q, k, v, do))
     got = _run_attention(pkg, q, k, v, do, dtype, "tokens")
     ref = _oracle(q, k, v, do)
-    tol = BF16_TOL if dtype == "bf16" else F32_TOL
+    tol = F32_TOL if dtype == "f32" else BF16_TOL
     for name, g, r in zip(("o", "lse", "dq", "dk", "dv"), got, ref):
         assert O.rel_err(g, r) < tol, (name, O.rel_err(g, r))
     assert pkg.lib.attn_device_error(1) == 0
@@ -192,6 +210,22 @@ def test_decode_matches_oracle(pkg, cuda_dev, dtype, B, NH, L, D):
     tol = F32_TOL if dtype == "f32" else BF16_TOL
     assert O.rel_err(out.float().cpu().numpy(), ref_o) < tol
     assert O.rel_err(lse.cpu().numpy(), ref_l) < tol
+
+
+def test_tf32_operands_drop_their_low_mantissa_bits(pkg, cuda_dev):
+    """The tf32 tensor cores read a float32 operand's upper 19 bits (the low 13 mantissa bits are
+    dropped, not rounded): A = 1 + 0.75 * 2^-10 (between the tf32 values 1 and 1 + 2^-10) times the
+    identity gives exactly 1.  The CUDA-core backward after a tf32 forward relies on this: it
+    recomputes the scores from q and k truncated the same way."""
+    torch = _torch()
+    n = 256
+    a = torch.full((n, n), 1.0 + 0.75 * 2.0 ** -10, dtype=torch.float32, device="cuda")
+    eye = torch.eye(n, dtype=torch.float32, device="cuda")
+    c = torch.empty((n, n), dtype=torch.float32, device="cuda")
+    for at, bt in ((False, False), (True, True)):  # K-major and MN-major operands
+        pkg.mha_ops.gemm(a.data_ptr(), n, at, eye.data_ptr(), n, bt, "tf32", c.data_ptr(), n, torch.float32, n, n, n)
+        torch.cuda.synchronize()
+        assert torch.equal(c, torch.ones_like(c)), (at, bt, c[0, :4].tolist())
 
 
 @pytest.mark.parametrize("dtype", ["f32", "tf32", "bf16"])

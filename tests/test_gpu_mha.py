@@ -254,3 +254,30 @@ def test_backward_residual_matches_block_sequence(pkg, cuda_dev, prec, tol, B, T
                   d_attn_w=(attn.c_attn_w.grads, daw), d_proj_b=(attn.c_proj_b.grads, dpb))
     for k, (got, want) in checks.items():
         assert O.rel_err(got.cpu().numpy(), want) < tol, (k, O.rel_err(got.cpu().numpy(), want))
+
+
+@pytest.mark.parametrize("H,M,D,Din,seed", [(3, 17, 8, 6, 1337), (4, 200, 32, 48, 7)])
+def test_mha_controller_matches_oracle(pkg, cuda_dev, H, M, D, Din, seed):
+    """MHAController.forward (core/mha_ops.py:84-138) as the reference's golden test drives it in
+    its Layer 3 (test_mha_golden_model.py:285-308, 511-517: seed 1337, H=3, M=17, D=8, Din=6,
+    X ~ N(0, 1), W_qkv ~ N(0, 1/sqrt(Din))), and at a larger shape: out and probs against the
+    oracle's fused projection + causal attention, at the reference's tolerance and 1e-5 relative."""
+    torch = _torch()
+    np.random.seed(seed)
+    X = np.random.normal(0.0, 1.0, size=(H, M, Din)).astype(np.float32)
+    W = np.random.normal(0.0, 1.0 / np.sqrt(Din), size=(Din, 3 * D)).astype(np.float32)
+    ctl = pkg.MHAController(H, M, D)
+    out, probs = ctl.forward(X, W)
+    assert out.shape == (H, M, D) and probs.shape == (H, M, M)
+    fused = X.astype(np.float64) @ W.astype(np.float64)  # matmul_qkv_fused, split_qkv_kernel
+    q, k, v = fused[..., :D], fused[..., D:2 * D], fused[..., 2 * D:]
+    ref_out, _, ref_probs = O.causal_attention_forward(q, k, v, 1.0 / np.sqrt(D))
+    np.testing.assert_allclose(out, ref_out, **TOL)
+    np.testing.assert_allclose(probs, ref_probs, **TOL)
+    assert O.rel_err(out, ref_out) < 1e-5 and O.rel_err(probs, ref_probs) < 1e-5
+    # the pass-through of the fused projection on device buffers
+    gX, gW = torch.from_numpy(X).cuda(), torch.from_numpy(W).cuda()
+    gF = torch.empty((H, M, 3 * D), dtype=torch.float32, device="cuda")
+    ctl.matmul_qkv_fused(gX, gW, gF, Din, block=(256, 1, 1), grid=(1, 1))
+    torch.cuda.synchronize()
+    assert O.rel_err(gF.cpu().numpy(), fused) < 1e-5
