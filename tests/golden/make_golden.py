@@ -3,6 +3,7 @@
 Usage (needs the reference checkout, which only the build container has):
 
     python tests/golden/make_golden.py <reference checkout>      (or LLM_GPU5_REFERENCE=<checkout>)
+    python tests/golden/make_golden.py <reference checkout> --only=checkpoint   (that archive alone)
 
 The reference is PyCUDA code for a Kepler GPU.  Its attention *math* is plain NumPy and host
 Python, so this script installs a host-memory stand-in for ``pycuda.driver`` /
@@ -22,6 +23,9 @@ Python, so this script installs a host-memory stand-in for ``pycuda.driver`` /
   index arithmetic, and ``fused_attention_forward_kernel`` by the reference's own golden forward
   ``numpy_causal_attention_forward``.  The capture scenario of capture_mha_oracle.py:23-73
   (seed 4242, B=2, T=5, C=8, NH=2), whose ``.npz`` the reference does not ship, is rebuilt this way.
+* ``model.gpt.GPTModel.save_checkpoint`` (model/gpt.py:1103-1176) writes ``ckpt_gpt_c16_nh2_l2.npz``
+  for a small seeded model (2 layers, C=16, 2 heads, non-zero attention biases): the reference's
+  own checkpoint archive, which the drop-in modules must read and write back unchanged.
 
 Nothing here is imported by the tests; they only read the ``.npz`` files it writes.
 """
@@ -289,7 +293,23 @@ def _run_reference_ffn(gpt, cuda, C, M, seed, dout_seed=None, bias_scale=0.0):
                 d_proj_w=dl(ffn.c_proj_w, "gpu_grads"), d_proj_b=dl(ffn.c_proj_b, "gpu_grads"), C=C, M=M)
 
 
-def main(ref_root):
+def _run_reference_checkpoint(gpt, cuda, path, seed):
+    """The reference's own GPTModel.save_checkpoint (model/gpt.py:1103-1176) on a small seeded
+    model (vocab 20, max_len 8, C=16, 2 heads, 2 layers) whose attention biases are set to
+    non-zero draws first (the reference initialises them to 0), so every attention key of the
+    archive carries values.  The archive it writes is the checkpoint format the drop-in modules
+    must read and write back unchanged."""
+    np.random.seed(seed)
+    cfg = gpt.GPTConfig(vocab_size=20, max_len=8, embedding_dim=16, num_heads=2, num_layers=2)
+    model = gpt.GPTModel(cfg)
+    rng = np.random.default_rng(seed + 1)
+    for block in model.blocks:
+        for p in (block.attn.c_attn_b, block.attn.c_proj_b):
+            cuda.memcpy_htod(p.gpu_weights, (0.1 * rng.standard_normal(p.shape)).astype(np.float32))
+    model.save_checkpoint(path)
+
+
+def main(ref_root, only=None):
     ref_root = os.path.abspath(ref_root)
     state = {}
     _install_fake_pycuda(_make_kernels(lambda: state["golden"]))
@@ -302,6 +322,9 @@ def main(ref_root):
         import pycuda.driver as cuda  # noqa: E402  (the stand-in)
         from model import gpt  # noqa: E402
         state["golden"] = golden
+        if only == "checkpoint":
+            _run_reference_checkpoint(gpt, cuda, os.path.join(HERE, "ckpt_gpt_c16_nh2_l2.npz"), 2026)
+            return
         saved_M = golden.M
         _kernel_level(golden)
         golden.M = saved_M
@@ -321,13 +344,19 @@ def main(ref_root):
         np.savez(os.path.join(HERE, "ffn_c16_m6.npz"), **_run_reference_ffn(gpt, cuda, 16, 6, 1337))
         np.savez_compressed(os.path.join(HERE, "ffn_c64_m40.npz"),
                             **_run_reference_ffn(gpt, cuda, 64, 40, 2024, dout_seed=2025, bias_scale=0.5))
+
+        # a checkpoint archive written by the reference's GPTModel.save_checkpoint
+        _run_reference_checkpoint(gpt, cuda, os.path.join(HERE, "ckpt_gpt_c16_nh2_l2.npz"), 2026)
     finally:
         os.chdir(cwd)
     print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLM_GPU5_REFERENCE")
+    args = [a for a in sys.argv[1:] if not a.startswith("--only=")]
+    only = next((a.split("=", 1)[1] for a in sys.argv[1:] if a.startswith("--only=")), None)
+    ref = args[0] if args else os.environ.get("LLM_GPU5_REFERENCE")
     if not ref:
-        sys.exit("usage: python tests/golden/make_golden.py <reference checkout>  (or set LLM_GPU5_REFERENCE)")
-    main(ref)
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout> [--only=checkpoint]  "
+                 "(or set LLM_GPU5_REFERENCE)")
+    main(ref, only)
