@@ -463,12 +463,13 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
                 const float4 dv = d4[c * 8 + j];
                 const uint32_t* src = (c == 0 ? a0 : a1) + 4 * j;
                 const uint32_t w0 = pw[c * 16 + 2 * j], w1 = pw[c * 16 + 2 * j + 1];
-                const float d0 = __uint_as_float(w0 << 16) * (__uint_as_float(src[0]) - dv.x);
-                const float d1 = __uint_as_float(w0 & 0xffff0000u) * (__uint_as_float(src[1]) - dv.y);
-                const float d2 = __uint_as_float(w1 << 16) * (__uint_as_float(src[2]) - dv.z);
-                const float d3 = __uint_as_float(w1 & 0xffff0000u) * (__uint_as_float(src[3]) - dv.w);
-                dk[2 * j] = pack_bf16x2(d0, d1);
-                dk[2 * j + 1] = pack_bf16x2(d2, d3);
+                // dS^T = P^T (dP^T - delta) as packed bf16x2 products: the differences in fp32,
+                // rounded to bf16 pairs, times the packed P^T pairs (4 instructions per pair of
+                // elements instead of 7 with unpacking and fp32 products)
+                const uint32_t g0 = pack_bf16x2(__uint_as_float(src[0]) - dv.x, __uint_as_float(src[1]) - dv.y);
+                const uint32_t g1 = pack_bf16x2(__uint_as_float(src[2]) - dv.z, __uint_as_float(src[3]) - dv.w);
+                dk[2 * j] = mul_bf16x2(w0, g0);
+                dk[2 * j + 1] = mul_bf16x2(w1, g1);
               }
               tmem_st16(tdP + c * 16, dk);  // dS^T over dP^T columns already read
 #pragma unroll

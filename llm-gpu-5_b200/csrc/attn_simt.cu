@@ -3,7 +3,9 @@
 // This is the exact path used for float32 problems (the reference's own precision) and the
 // generic path for bf16 head dims the tensor-core kernels do not cover.  Math follows the
 // reference: scores = scale * q.k over keys j <= i (core/mha_kernels.py:429-445), a softmax with
-// accurate expf (core/mha_kernels.py:466-470), O = P.V (core/mha_kernels.py:501-520); backward is
+// expf (core/mha_kernels.py:466-470; the reference compiles with --use_fast_math, so its expf is the
+// hardware exponential) computed here as 2^x on log2-scaled scores with the ex2.approx instruction,
+// O = P.V (core/mha_kernels.py:501-520); backward is
 // the VJP of model/gpt.py:672-680 with the scale applied to dS (model/gpt.py:677).
 //
 // Instead of materialising P[T,T] the forward keeps an online softmax per row and writes the
@@ -25,6 +27,15 @@ template <int D> struct RowSplit {
   static constexpr int NV = DPT / 4;               // float4 groups per thread
   static_assert(D % 4 == 0 && DPT % 4 == 0, "head_dim must be a multiple of 4");
 };
+
+constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+
+// 2^x by the special-function unit (ex2.approx.ftz.f32); the softmax works in log2 units.
+__device__ __forceinline__ float exp2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ float dot4(float4 a, float4 b) {
   return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
@@ -69,6 +80,7 @@ attn_fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
                      T* __restrict__ o, float* __restrict__ lse, int NH, int T_, AttnStrides st,
                      float scale) {
   using RS = RowSplit<D>;
+  const float scale_log2 = scale * kLog2e;
   constexpr int TPR = RS::TPR, NV = RS::NV, D4 = D / 4;
   __shared__ float4 Ks[FWD_BN][D4];
   __shared__ float4 Vs[FWD_BN][D4];
@@ -113,20 +125,20 @@ attn_fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
       float p = 0.f;
 #pragma unroll
       for (int i = 0; i < NV; ++i) p += dot4(qr[i], Ks[j][i * TPR + part]);
-      p = row_reduce<TPR>(p) * scale;
+      p = row_reduce<TPR>(p) * scale_log2;  // log2 units
       const int key = k0 + j;
       s[j] = (key <= row && key < T_) ? p : -INFINITY;
       tile_max = fmaxf(tile_max, s[j]);
     }
     // key 0 is in tile 0 and visible to every row, so m_new is finite from the first tile on
     const float m_new = fmaxf(m, tile_max);
-    const float corr = expf(m - m_new);
+    const float corr = exp2_fast(m - m_new);
     l *= corr;
 #pragma unroll
     for (int i = 0; i < NV; ++i) scale4(acc[i], corr);
 #pragma unroll
     for (int j = 0; j < FWD_BN; ++j) {
-      const float p = expf(s[j] - m_new);
+      const float p = exp2_fast(s[j] - m_new);
       l += p;
 #pragma unroll
       for (int i = 0; i < NV; ++i) axpy4(acc[i], p, Vs[j][i * TPR + part]);
@@ -143,7 +155,7 @@ attn_fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
       scale4(a, inv);
       store4(ob + (i * TPR + part) * 4, a);
     }
-    if (part == 0) lse[(int64_t)bh * T_ + row] = m + logf(l);
+    if (part == 0) lse[(int64_t)bh * T_ + row] = (m + __log2f(l)) * kLn2;  // natural-log units
   }
 }
 
@@ -186,6 +198,7 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
                      const float* __restrict__ delta, T* __restrict__ dk, T* __restrict__ dv,
                      int NH, int T_, AttnStrides st, float scale) {
   using RS = RowSplit<D>;
+  const float scale_log2 = scale * kLog2e;
   constexpr int TPR = RS::TPR, NV = RS::NV, D4 = D / 4;
   __shared__ float4 Qs[KV_BQ][D4];
   __shared__ float4 Gs[KV_BQ][D4];
@@ -223,7 +236,7 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
     }
     for (int i = tid; i < KV_BQ; i += blockDim.x) {
       const int qi = q0 + i;
-      Ls[i] = qi < T_ ? lse[(int64_t)bh * T_ + qi] : 0.f;
+      Ls[i] = qi < T_ ? lse[(int64_t)bh * T_ + qi] * kLog2e : 0.f;  // log2 units
       Ds[i] = qi < T_ ? delta[(int64_t)bh * T_ + qi] : 0.f;
     }
     __syncthreads();
@@ -239,7 +252,7 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
       s = row_reduce<TPR>(s);
       dp = row_reduce<TPR>(dp);
       const bool valid = key <= qi && qi < T_ && key < T_;
-      const float p = valid ? expf(s * scale - Ls[i]) : 0.f;
+      const float p = valid ? exp2_fast(s * scale_log2 - Ls[i]) : 0.f;
       const float ds = p * (dp - Ds[i]) * scale;
 #pragma unroll
       for (int c = 0; c < NV; ++c) {
@@ -270,6 +283,7 @@ attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
                    const float* __restrict__ delta, T* __restrict__ dq, int NH, int T_,
                    AttnStrides st, float scale) {
   using RS = RowSplit<D>;
+  const float scale_log2 = scale * kLog2e;
   constexpr int TPR = RS::TPR, NV = RS::NV, D4 = D / 4;
   __shared__ float4 Ks[DQ_BN][D4];
   __shared__ float4 Vs[DQ_BN][D4];
@@ -289,7 +303,7 @@ attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
     gr[i] = row < T_ ? load4(dout + out_off + row * st.out_st + (i * TPR + part) * 4) : make_float4(0, 0, 0, 0);
     dqr[i] = make_float4(0, 0, 0, 0);
   }
-  const float L = row < T_ ? lse[(int64_t)bh * T_ + row] : 0.f;
+  const float L = row < T_ ? lse[(int64_t)bh * T_ + row] * kLog2e : 0.f;  // log2 units
   const float Dl = row < T_ ? delta[(int64_t)bh * T_ + row] : 0.f;
   const int last_row = min(T_ - 1, qtile * DQ_BM + DQ_BM - 1);
   const int nkt = last_row / DQ_BN + 1;
@@ -320,7 +334,7 @@ attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
       s = row_reduce<TPR>(s);
       dp = row_reduce<TPR>(dp);
       const bool valid = key <= row && key < T_ && row < T_;
-      const float p = valid ? expf(s * scale - L) : 0.f;
+      const float p = valid ? exp2_fast(s * scale_log2 - L) : 0.f;
       const float ds = p * (dp - Dl) * scale;
 #pragma unroll
       for (int c = 0; c < NV; ++c) axpy4(dqr[c], ds, Ks[j][c * TPR + part]);
