@@ -582,7 +582,7 @@ def run_ours(args, cfg):
     peaks, src = load_peaks()
     per_op = {k: dict(ms_per_step=t, ranges_per_step=n) for k, (t, n) in totals.items()}
     achieved = op_flops(dom, B, T, C, NH) / (dom_ms * 1e-3) / 1e12
-    peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    peak, peak_src, bound = precision_peak(w["prec"], peaks, src)
     traffic = None
     tf = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tf):
@@ -601,15 +601,16 @@ def run_ours(args, cfg):
     line = dict(
         metric="causal attention fwd+bwd tokens/sec", value=value, unit="tokens/s", n_gpus=world,
         steps=steps, warmup=warmup, ms_per_step=ms, higher_is_better=True, scaling="strong",
-        vs_baseline=None, dtype="bf16" if w["prec"] == "bf16" else "f32", data="synthetic",
+        vs_baseline=None, dtype=DTYPE_NAME[w["prec"]], data="synthetic",
         config=dict(workload=w["name"], global_batch=GB, seq_len=T, d_model=C, heads=NH, head_dim=C // NH,
                     per_gpu_batch=B, parallelism=f"dp{world}", l2="inputs larger than L2 (no flush)",
                     launch="CUDA graph: the step captured once, replayed" if use_graph else "eager"),
-        roofline=dict(bound="tensor", kernel=dom, achieved=achieved, peak=peak, unit="TFLOP/s",
+        roofline=dict(bound=bound, kernel=dom, achieved=achieved, peak=peak, unit="TFLOP/s",
                       frac=achieved / peak, traffic=traffic,
-                      peak_source=f"{src} bf16_tflops (burst; the timed region is {ms * steps / 1e3:.2f} s)",
-                      frac_of_sustained=achieved / peaks.get("bf16_tflops_sustained",
-                                                             FALLBACK_PEAKS["bf16_tflops_sustained"])),
+                      peak_source=f"{peak_src}; the timed region is {ms * steps / 1e3:.2f} s",
+                      frac_of_sustained=(achieved / peaks.get("bf16_tflops_sustained",
+                                                              FALLBACK_PEAKS["bf16_tflops_sustained"])
+                                         if w["prec"] == "bf16" else None)),
         step_tflops=sum(op_flops(k, B, T, C, NH) or 0 for k in totals) * world / (ms * 1e-3) / 1e12,
         tflops=tflops,
         breakdown=per_op,
@@ -701,6 +702,22 @@ def fp32_core_peak(peaks):
     return sms * 128 * 2 * mhz * 1e6 / 1e12, f"derived: {sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz"
 
 
+DTYPE_NAME = dict(bf16="bf16", tf32="tf32", fp32="f32")
+
+
+def precision_peak(prec, peaks, src):
+    """(peak TFLOP/s, where it comes from, bound) for a step computed in ``prec``: bf16 the measured
+    burst bf16 figure; tf32 half of it (the dense tf32 rate is half the bf16 rate on this part; no
+    tf32 figure is measured); fp32 the CUDA-core peak."""
+    if prec == "bf16":
+        return peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), f"{src} bf16_tflops (burst)", "tensor"
+    if prec == "tf32":
+        return (peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2,
+                f"derived: half of the {src} bf16_tflops (burst)", "tensor")
+    peak, psrc = fp32_core_peak(peaks)
+    return peak, psrc, "fp32 CUDA core"
+
+
 def measure_module_config(args, pkg, cfg, peaks, src, prec=None):
     """MultiHeadAttention forward + backward at one configuration's full size on one GPU: the step
     captured as a CUDA graph, each replay timed with events after a 256 MB write that flushes L2,
@@ -755,20 +772,13 @@ def measure_module_config(args, pkg, cfg, peaks, src, prec=None):
     flops_of = lambda k: op_flops(k, B, T, C, NH)  # noqa: E731
     dom = max((k for k in totals if flops_of(k)), key=lambda k: totals[k][0])
     dom_ach = flops_of(dom) / (totals[dom][0] / totals[dom][1] * 1e-3) / 1e12
-    if w["prec"] == "bf16":
-        peak, psrc = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), f"{src} bf16_tflops (burst)"
-    elif w["prec"] == "tf32":
-        # no measured tf32 figure: the dense tf32 rate is half the bf16 rate on this part
-        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2
-        psrc = f"derived: half of the {src} bf16_tflops (burst)"
-    else:
-        peak, psrc = fp32_core_peak(peaks)
+    peak, psrc, bound = precision_peak(w["prec"], peaks, src)
     tflops = group_tflops(totals, flops_of)
     for g in tflops.values():
         g["frac"] = g["tflops"] / peak
     res = dict(workload=w["name"], value=B * T / (ms * 1e-3), unit="tokens/s", ms_per_step=ms,
-               dtype=dict(bf16="bf16", tf32="tf32", fp32="f32")[w["prec"]], steps=steps, tflops=tflops,
-               roofline=dict(bound="fp32 CUDA core" if w["prec"] == "fp32" else "tensor", kernel=dom,
+               dtype=DTYPE_NAME[w["prec"]], steps=steps, tflops=tflops,
+               roofline=dict(bound=bound, kernel=dom,
                              achieved=dom_ach, peak=peak, unit="TFLOP/s", frac=dom_ach / peak, peak_source=psrc),
                breakdown={k: dict(ms_per_step=t, ranges_per_step=n) for k, (t, n) in totals.items()},
                l2="a 256 MB buffer written before every timed step (L2 flushed)",
