@@ -381,8 +381,15 @@ def run_ours(args, cfg):
     gen.manual_seed(1000 + cfg + 7919 * rank)
     x = torch.randn((M, C), generator=gen, device="cuda", dtype=torch.float32)
     dy = torch.randn((M, C), generator=gen, device="cuda", dtype=torch.float32)
+    reducer = None
     if dist is not None:
         attn.grad_sync_group = dist.group.WORLD
+        if not args.nccl:  # the library's NVSwitch multicast all-reduce where the GPUs support it
+            reducer = pkg.dp.make_grad_reducer(attn.flat_grads.numel())
+            if reducer is not None:
+                reducer.max_blocks = args.ar_blocks
+                reducer.overlap = not args.ar_serial
+                attn.use_grad_reducer(reducer)
 
     def step(xi, dyi):
         out = attn.forward(xi, B, T)
@@ -441,18 +448,23 @@ def run_ours(args, cfg):
     host_enqueue_ms = max_over_ranks(host_enqueue_ms)
 
     # ---------------- the gradient all-reduce alone (per rank, CUDA events on the launching stream)
-    comm_ms = None
+    comm_ms = comm_ms_nccl = None
     if dist is not None:
-        times = []
-        for _ in range(5):
-            barrier()
-            ca, cb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ca.record()
-            pkg.dp.allreduce_grads(attn.flat_grads, dist.group.WORLD)
-            cb.record()
-            cb.synchronize()
-            times.append(ca.elapsed_time(cb))
-        comm_ms = max_over_ranks(statistics.median(times))
+        def time_comm(fn):
+            times = []
+            for _ in range(7):
+                barrier()
+                ca, cb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ca.record()
+                fn()
+                cb.record()
+                cb.synchronize()
+                times.append(ca.elapsed_time(cb))
+            return max_over_ranks(statistics.median(times[2:]))
+        scratch = attn.flat_grads.clone()
+        comm_ms_nccl = time_comm(lambda: pkg.dp.allreduce_grads(scratch, dist.group.WORLD))
+        comm_ms = time_comm(reducer.allreduce) if reducer is not None else comm_ms_nccl
+        del scratch
 
     # ---------------- timed region: captured steps replayed (or eager steps with --eager)
     # The dominant op is bracketed by timing events in every step; with graphs, R captured copies
@@ -616,9 +628,13 @@ def run_ours(args, cfg):
         breakdown=per_op,
         timing=dict(eager_ms_per_step=eager_ms, host_enqueue_ms_eager=host_enqueue_ms,
                     host_enqueue_ms_graph=host_replay_ms if use_graph else None, comm_ms=comm_ms,
-                    comm_bytes=attn.flat_grads.numel() * 4 if dist is not None else 0,
-                    note="eager: the same step launched op by op from Python; comm_ms: the gradient "
-                         "all-reduce alone, median of 5, max over ranks"),
+                    comm_ms_nccl=comm_ms_nccl, comm_bytes=attn.flat_grads.numel() * 4 if dist is not None else 0,
+                    grad_sync=None if dist is None else (
+                        "NVSwitch multicast all-reduce kernel (attn_grad_allreduce)" if reducer is not None
+                        else "NCCL all_reduce"),
+                    note="eager: the same step launched op by op from Python; comm_ms: the step's gradient "
+                         "all-reduce alone, comm_ms_nccl: NCCL's on the same buffer, medians of 5, max over "
+                         "ranks"),
         gpu_launches=launches_per_step * steps,
         e2e=dict(value=GB * T / (e2e_ms * 1e-3), unit="tokens/s", h2d_bytes_per_step=h2d * world,
                  d2h_bytes_per_step=d2h * world, ms_per_step=e2e_ms, copy_gbs=copy_gbs,
@@ -1187,6 +1203,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true",
                     help="leave out the 'configs' object (configurations 1-4 measured after the headline)")
+    ap.add_argument("--nccl", action="store_true",
+                    help="sum the gradients with NCCL instead of the library's NVSwitch multicast all-reduce")
+    ap.add_argument("--ar-blocks", type=int, default=0,
+                    help="CTAs of the multicast all-reduce (0: the library's default)")
+    ap.add_argument("--ar-serial", action="store_true",
+                    help="run the multicast all-reduce after the input-gradient GEMM instead of beside it")
     ap.add_argument("--eager", action="store_true",
                     help="launch every step op by op from Python instead of replaying a captured CUDA graph")
     ap.add_argument("--residual", action="store_true",

@@ -43,6 +43,30 @@ extern "C" {
                        with float32 accumulation; shapes the tensor-core kernels do not take run
                        the exact float32 CUDA-core path */
 
+/*
+ * Data-parallel gradient all-reduce (SUM) over NVSwitch multicast.  No counterpart in the
+ * reference, which trains on one GPU (its scaling is gradient accumulation, auto_train.py:
+ * 1591-1615); it sums the flat float32 gradient buffer [dWqkv | dbqkv | dWo | dbo] (or the
+ * FeedForward's) over the ranks, so every rank holds the full-batch gradient of
+ * model/gpt.py:687-694.  One launch per rank, on `stream`, after the kernels that wrote the
+ * gradients; every rank of the group must call it with the same n and world.
+ *   multicast    the buffer's multicast address (symmetric memory bound to an NVLink multicast
+ *                object, n float32 per rank, 16-byte aligned); the sum is written back to every
+ *                rank's buffer through it
+ *   signal_pads  device address of an array of `world` pointers, rank p's uint32 signal pad at
+ *                [p]; each pad holds at least attn_grad_allreduce_signal_bytes(n, world) bytes, zero
+ *                before the first call (the kernel leaves them zero)
+ *   max_blocks   CTAs of 256 threads to use (0: the default of 32, a fraction of the SMs, so that the
+ *                reduction can run beside the GEMM that follows the weight gradients); at most
+ *                128, the same on every rank
+ * world 2 .. 8.  The kernel meets the other ranks in cross-GPU barriers before and after the
+ * reduction; a barrier wait that gives up (after 2 s) records site 400 or 401 in the status word
+ * (attn_device_error) and the kernel returns.
+ */
+size_t attn_grad_allreduce_signal_bytes(int64_t n, int world);
+int attn_grad_allreduce(void* multicast, const void* signal_pads, int rank, int world, int64_t n,
+                        size_t signal_pad_bytes, int max_blocks, void* stream);
+
 /* Epilogue activations of attn_gemm_act (the feed-forward block, model/gpt.py:327-456). */
 #define ATTN_ACT_NONE 0
 #define ATTN_ACT_GELU 1     /* C = gelu(acc + bias); aux (optional) = acc + bias          */
@@ -60,11 +84,13 @@ uint64_t attn_launch_count(void);
 /*
  * Status word of the tensor-core kernels on the current device: 0, or the code of a bounded
  * wait inside a kernel that gave up (that launch then skipped its remaining work and returned
- * instead of hanging, so its outputs are incomplete).  Codes are grouped by kernel: 1xx the GEMM,
+ * instead of hanging, so its outputs are incomplete).  Codes are grouped by kernel: 1xx the GEMM
+ * (106: its dynamic shared memory did not start 1024-byte aligned, checked before any work),
  * 2xx the attention forward, 3xx the attention backward (300: its dynamic shared memory did not
- * start 1024-byte aligned, checked before any work), 900 the self-test below.  The word keeps the
- * first code until it is cleared; a set word does not affect later launches (each launch only
- * stops early for a wait of its own that gave up).  Synchronises with the device.
+ * start 1024-byte aligned, checked before any work), 4xx the barriers of attn_grad_allreduce, 900
+ * the self-test below.  The word keeps the first code until it is cleared; a set word does not
+ * affect later launches (each launch only stops early for a wait of its own that gave up).
+ * Synchronises with the device.
  * clear != 0 resets it to 0.  Has no counterpart in the reference, whose kernels cannot give up.
  * (Replaces the launch-failure exceptions PyCUDA raises, model/gpt.py:649-650 for the module.)
  */
@@ -100,6 +126,10 @@ int attn_wait_selftest(int limit_us, void* stream);
  *                  accumulators; heads narrower than 64 are zero-padded to 64 by TMA) when the
  *                  tensors are 16-byte aligned with strides in 8-element steps, CUDA-core path
  *                  otherwise; fp32 softmax statistics and accumulation.
+ * dtype ATTN_TF32: float32 tensors; tcgen05 kind::tf32 path for D a multiple of 4 up to 32 (the
+ *                  same kernel with 32-float rows) under the same layout conditions, the float32
+ *                  CUDA-core path otherwise.  attn_bwd then recomputes the scores from q and k
+ *                  truncated to tf32, so that they match the lse this forward wrote.
  * Q/K/V share the input strides; O uses the output strides.
  */
 int attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,

@@ -60,6 +60,8 @@ SIGNATURES = {
     "attn_cast_colsum_f32": (_i, [_p, _i64, _i, _i, _p, _i64, _p, _i, _p, _sz, _p]),
     "attn_split_heads": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p]),
     "attn_merge_heads": (_i, [_p, _p, _i, _i, _i, _i, _p]),
+    "attn_grad_allreduce_signal_bytes": (_sz, [_i64, _i]),
+    "attn_grad_allreduce": (_i, [_p, _p, _i, _i, _i64, _sz, _i, _p]),
 }
 
 

@@ -42,7 +42,11 @@ constexpr int GT_A_BYTES = GT_BM * 128;  // 16 KB: 128 rows x 128 bytes of K (64
 constexpr int GT_B_BYTES = GT_BN * 128;  // 32 KB
 constexpr int GT_STAGE_BYTES = GT_A_BYTES + GT_B_BYTES;
 constexpr int GT_EPI_STAGING = 32 * 1024;      // output staging: two buffers per epilogue group
-constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + GT_EPI_STAGING + GT_BN * 4 /*bias*/ + 1024 + 256;
+// No alignment pad: the kernel checks that its dynamic shared memory starts 1024-byte aligned (the
+// 128-byte swizzle needs it; error site 106 otherwise), which leaves room on the SM for a small
+// CTA beside it (the gradient all-reduce that overlaps the dX GEMM).
+constexpr int GT_SMEM = GT_STAGES * GT_STAGE_BYTES + GT_EPI_STAGING + GT_BN * 4 /*bias*/ + 256;
+constexpr int GT_SITE_SMEM_ALIGN = 106;
 
 // Epilogue shape for EW epilogue warps (4 or 8).
 template <int EW>
@@ -155,9 +159,13 @@ __global__ void __launch_bounds__(Epi<EW>::kthreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux,
                const GemmParams p) {
-  extern __shared__ uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   const WaitErr werr = wait_err(p.err);
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (smem_u32(smem_raw) & 1023u) {  // uniform, so every thread leaves before any set-up
+    if (threadIdx.x == 0) record_wait_error(werr, GT_SITE_SMEM_ALIGN);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   using E = Epi<EW>;
   // A K block is 128 bytes of K per row: 64 bf16 or 32 tf32 elements.  MN-major operands arrive as
   // boxes MNW elements (128 bytes) wide and one K block deep; one MMA-K step spans 16 bf16 / 8 tf32

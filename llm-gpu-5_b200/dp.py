@@ -62,3 +62,70 @@ def allreduce_grads(flat, group=None, async_op: bool = False):
     """Sum the flat gradient buffer over ``group`` in place (one collective; NCCL on GPUs)."""
     import torch.distributed as dist
     return dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+
+
+def multicast_supported(device_index: int) -> bool:
+    """Whether the GPU can bind memory to an NVLink multicast object (NVSwitch NVLS)."""
+    import torch
+    try:
+        sm = torch._C._distributed_c10d._SymmetricMemory
+        return bool(sm.has_multicast_support(torch._C._autograd.DeviceType.CUDA, device_index))
+    except (AttributeError, RuntimeError):
+        return False
+
+
+class MulticastGradReducer:
+    """A flat float32 gradient buffer summed over the ranks of a group by the library's NVSwitch
+    multicast all-reduce (``attn_grad_allreduce``) instead of NCCL.
+
+    The buffer is allocated in symmetric memory (torch's plumbing: every rank's buffer is mapped
+    at one multicast address, and every rank has a signal pad the others can reach); a module puts
+    its gradients in it with ``use_grad_reducer``.  ``allreduce()`` launches one kernel on the
+    current stream that meets the other ranks in a cross-GPU barrier, sums the buffer in the
+    NVSwitch (each rank reduces and writes back 1/world of it) and meets them again, so it can be
+    captured into a CUDA graph like any other launch.  Every rank must call it at the same point.
+    """
+
+    def __init__(self, numel: int, group=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        from ._lib import lib
+        self.group = group if group is not None else dist.group.WORLD
+        self.numel = int(numel)
+        self.buffer = symm_mem.empty(self.numel, dtype=torch.float32, device="cuda")
+        self.buffer.zero_()
+        self.handle = symm_mem.rendezvous(self.buffer, self.group.group_name)
+        if not self.handle.multicast_ptr:
+            raise RuntimeError("MulticastGradReducer: no multicast address for this group's buffers")
+        self.rank, self.world = self.handle.rank, self.handle.world_size
+        need = lib.attn_grad_allreduce_signal_bytes(self.numel, self.world)
+        if self.handle.signal_pad_size < need:
+            raise RuntimeError(f"MulticastGradReducer: signal pads of {self.handle.signal_pad_size} bytes, "
+                               f"{need} needed")
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # every rank's buffer and pads exist before the first launch
+
+    max_blocks = 0  # CTAs of one launch (0: the library's default); the same on every rank
+    overlap = True  # a module's backward runs the reduction beside its last GEMM (False: after it)
+
+    def allreduce(self):
+        """Sum the buffer over the ranks, in place on every rank (one launch, current stream)."""
+        import torch
+        from ._lib import call
+        call("attn_grad_allreduce", self.handle.multicast_ptr, self.handle.signal_pad_ptrs_dev, self.rank,
+             self.world, self.numel, self.handle.signal_pad_size, int(self.max_blocks),
+             torch.cuda.current_stream().cuda_stream)
+
+
+def make_grad_reducer(numel: int, group=None):
+    """A MulticastGradReducer for ``group`` when every GPU of it supports NVLink multicast and the
+    group has 2 to 8 ranks, else None (the modules then all-reduce through NCCL)."""
+    import torch
+    import torch.distributed as dist
+    group = group if group is not None else dist.group.WORLD
+    world = dist.get_world_size(group)
+    ok = torch.tensor([1 if 2 <= world <= 8 and multicast_supported(torch.cuda.current_device()) else 0],
+                      device="cuda")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)  # all ranks take the same decision
+    return MulticastGradReducer(numel, group) if int(ok.item()) else None

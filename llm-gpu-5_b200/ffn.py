@@ -29,7 +29,8 @@ import torch
 from . import dp
 from . import mha_ops as ops
 from ._lib import check_device_error
-from .mha import DeviceBuffer, GPTConfig, Parameter, _as_tensor, _NULL, device_checked
+from .mha import (DeviceBuffer, GPTConfig, Parameter, _as_tensor, _NULL, attach_grad_reducer, device_checked,
+                  finish_grad_sync, start_grad_sync)
 
 
 class FeedForward:
@@ -62,6 +63,7 @@ class FeedForward:
         self.use_cpu_backward = False
         self.profiler = None
         self.grad_sync_group = None
+        self.grad_reducer = None  # a dp.MulticastGradReducer holding flat_grads (use_grad_reducer)
         self._grad_sync_work = None
         self._cache = None
 
@@ -182,14 +184,20 @@ class FeedForward:
                          torch.float32, C, H, M, accumulate=accumulate)
             with self._rng("colsum"):
                 ops.colsum(dpre.data_ptr(), dt, H, M, H, self.c_fc_b.grads, accumulate=accumulate)
-        if self.grad_sync_group is not None:
-            self._grad_sync_work = dp.allreduce_grads(self.flat_grads, self.grad_sync_group, async_op=True)
+        pending = start_grad_sync(self)  # the gradients are final: their all-reduce overlaps dIn
         # dIn = dPre W_fc^T   (model/gpt.py:443)
         dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_dx"):
             ops.gemm(dpre.data_ptr(), H, False, c["w_fc"].data_ptr(), H, True, mm, dx.data_ptr(), C, torch.float32,
                      M, C, H)
+        finish_grad_sync(pending)
         return DeviceBuffer(dx)
+
+    def use_grad_reducer(self, reducer):
+        """Keep the four gradients in ``reducer``'s buffer (a dp.MulticastGradReducer of
+        dp.layout_size(dp.ffn_grad_layout(C)) floats): backward then sums them over the ranks with the
+        library's NVSwitch multicast all-reduce instead of NCCL (when ``grad_sync_group`` is set)."""
+        attach_grad_reducer(self, reducer, dp.ffn_grad_layout(self.config.embedding_dim))
 
     @device_checked
     def backward_residual(self, gpu_dx, B: int, T: int, ln_gamma, ln_dgamma, ln_dbeta, accumulate=False):

@@ -50,6 +50,55 @@ def device_checked(fn):
     return wrapper
 
 
+def start_grad_sync(mod):
+    """Start the all-reduce (SUM over ``mod.grad_sync_group``) of a module's flat gradient buffer
+    once its gradients are final, before the module's last GEMM: through NCCL on its own stream
+    (``wait_grad_sync`` waits for it), or, with a MulticastGradReducer attached, the library's NVSwitch
+    multicast all-reduce, either on a side stream beside the GEMM (``reducer.overlap``, its small
+    blocks sharing the SMs with it) or on the current stream after it.  Returns what
+    ``finish_grad_sync`` completes after the GEMM, or None."""
+    if mod.grad_sync_group is None:
+        return None
+    red = mod.grad_reducer
+    if red is None:
+        mod._grad_sync_work = dp.allreduce_grads(mod.flat_grads, mod.grad_sync_group, async_op=True)
+        return None
+    if not red.overlap:
+        def after_gemm():
+            with mod._rng("grad_allreduce"):
+                red.allreduce()
+        return after_gemm
+    mod._grad_stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(mod._grad_stream):
+        with mod._rng("grad_allreduce"):
+            red.allreduce()
+        joined = torch.cuda.Event()
+        joined.record(mod._grad_stream)
+    return lambda: torch.cuda.current_stream().wait_event(joined)
+
+
+def finish_grad_sync(pending):
+    """Complete what start_grad_sync began (the current stream waits for the side stream's
+    all-reduce, or launches it), so the summed gradients are in place, in stream order, when
+    backward returns."""
+    if pending is not None:
+        pending()
+
+
+def attach_grad_reducer(mod, reducer, layout):
+    """Move a module's flat gradient buffer into ``reducer.buffer`` (copying the current values) and
+    point its Parameters' gradients at their places in it (``layout`` as dp.grad_layout)."""
+    if reducer.numel != mod.flat_grads.numel():
+        raise ValueError(f"use_grad_reducer: the buffer holds {reducer.numel} floats, "
+                         f"{mod.flat_grads.numel()} needed")
+    reducer.buffer.copy_(mod.flat_grads)
+    mod.flat_grads = reducer.buffer
+    for name, off, shape in layout:
+        getattr(mod, name).grads = mod.flat_grads[off:off + int(np.prod(shape))].view(shape)
+    mod.grad_reducer = reducer
+    mod._grad_stream = torch.cuda.Stream()
+
+
 class GPTConfig:
     """The fields of llm-gpu-5's GPTConfig (model/gpt.py:53-87) that the attention path and its
     callers read, under the same argument names, plus ``attention_precision``: "fp32" (the
@@ -242,6 +291,7 @@ class MultiHeadAttention:
 
         self.profiler = None  # optional: object with .range(name) -> context manager (CUDA events)
         self.grad_sync_group = None  # a torch.distributed group: backward all-reduces (SUM) into it
+        self.grad_reducer = None     # a dp.MulticastGradReducer holding flat_grads (use_grad_reducer)
         self._grad_sync_work = None
         self.training = True
         self._cache = None
@@ -423,14 +473,21 @@ class MultiHeadAttention:
                          3 * C, torch.float32, C, 3 * C, M, accumulate=accumulate)
             with self._rng("colsum"):
                 ops.colsum(gb, dt, 3 * C, M, 3 * C, self.c_attn_b.grads, accumulate=accumulate)
-        if self.grad_sync_group is not None:
-            # overlaps the dX GEMM below on NCCL's stream
-            self._grad_sync_work = dp.allreduce_grads(self.flat_grads, self.grad_sync_group, async_op=True)
+        # the gradients are final: their all-reduce overlaps the dX GEMM below
+        pending = start_grad_sync(self)
         dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_dx"):
             ops.gemm(gb, 3 * C, False, c["w_qkv"].data_ptr(), 3 * C, True, mm, dx.data_ptr(), C,
                      torch.float32, M, C, 3 * C)
+        finish_grad_sync(pending)
         return DeviceBuffer(dx)
+
+    def use_grad_reducer(self, reducer):
+        """Keep the four gradients in ``reducer``'s buffer (a dp.MulticastGradReducer of
+        dp.flat_grad_size(C) floats), so that backward sums them over the ranks with the library's
+        NVSwitch multicast all-reduce instead of NCCL (when ``grad_sync_group`` is set, as for
+        NCCL: on the last micro-step of an accumulation).  The current gradients are copied over."""
+        attach_grad_reducer(self, reducer, dp.grad_layout(self.config.embedding_dim))
 
     def wait_grad_sync(self):
         """Wait for the gradient all-reduce launched by the last backward (if any), and raise
