@@ -91,6 +91,8 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o,
                                      const float* __restrict__ lse, float* __restrict__ lse2,
                                      float* __restrict__ delta, int NH, int T, int Tp, int D,
                                      int64_t o_sb, int64_t o_st, int64_t o_sh) {
+  grid_dependency_wait();  // O and dO are complete
+  grid_dependents_launch();
   const int bh = blockIdx.x;
   const int t = blockIdx.y * 32 + (threadIdx.x >> 3);  // < Tp
   const int c = threadIdx.x & 7;
@@ -236,6 +238,8 @@ attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const BwdParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dependency_wait();    // Q, K, V (and dO, lse, delta) are complete
+  grid_dependents_launch();  // the next kernel's CTAs may take SMs as this grid's CTAs leave
 
   if (warp < 4) {  // TMA producers, MMA issuer
     reg_dealloc<BA_REG_LOW>();
@@ -660,10 +664,11 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
     set_error("attn_bwd: T = %d exceeds the tensor-core backward's limit of %d", T, kBwdTcMaxT);
     return ATTN_ERR_UNSUPPORTED;
   }
-  attn_bwd_prep_kernel<<<dim3((unsigned)BH, (unsigned)(Tp / 32)), 256, 0, stream>>>(
-      (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, lse2, delta, NH, T, Tp, D, s[3], s[4], s[5]);
+  const cudaError_t prep = launch_pdl(attn_bwd_prep_kernel, dim3((unsigned)BH, (unsigned)(Tp / 32)), dim3(256), 0,
+                                      stream, (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, lse2,
+                                      delta, NH, T, Tp, D, s[3], s[4], s[5]);
   count_launch();
-  if (int rc = check_launch("attn_bwd_prep_kernel")) return rc;
+  if (int rc = check_launch("attn_bwd_prep_kernel", prep)) return rc;
 
   BwdMaps maps;
   if (!make_head_map(&maps.q, q, B, NH, T, D, s[0], s[1], s[2]) ||
@@ -701,9 +706,9 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   if (!set_smem_limit_once(attn_bwd_tc_kernel, BA_SMEM, attr_done)) return ATTN_ERR_CUDA;
   static int launch_regs = 0;
   if (!launch_regs_match(attn_bwd_tc_kernel, BA_LAUNCH_REGS, launch_regs, "attn_bwd_tc_kernel")) return ATTN_ERR_CUDA;
-  attn_bwd_tc_kernel<<<grid, BA_THREADS, BA_SMEM, stream>>>(maps, p);
+  const cudaError_t launched = launch_pdl(attn_bwd_tc_kernel, dim3(grid), dim3(BA_THREADS), BA_SMEM, stream, maps, p);
   count_launch();
-  return check_launch("attn_bwd_tc_kernel");
+  return check_launch("attn_bwd_tc_kernel", launched);
 }
 
 }  // namespace attn

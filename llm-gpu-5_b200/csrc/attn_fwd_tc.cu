@@ -147,6 +147,8 @@ attn_fwd_tc_kernel(const __grid_constant__ FwdMaps maps, const FwdParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dependency_wait();    // Q, K, V (and dO, lse, delta) are complete
+  grid_dependents_launch();  // the next kernel's CTAs may take SMs as this grid's CTAs leave
 
   if (warp < 4) {
     reg_dealloc<FA_REG_LOW>();
@@ -514,12 +516,13 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
   const int grid = (int)((units + 1) / 2 < sms ? (units + 1) / 2 : sms);  // at least a unit per stream
   static CtxOnce attr[4];
   static int regs[4] = {0, 0, 0, 0};
+  cudaError_t launched = cudaSuccess;
 #define FA_LAUNCH(SG, TF, slot)                                                                          \
   do {                                                                                                   \
     if (!set_smem_limit_once(attn_fwd_tc_kernel<SG, TF>, FA_SMEM, attr[slot]) ||                         \
         !launch_regs_match(attn_fwd_tc_kernel<SG, TF>, FA_LAUNCH_REGS, regs[slot], "attn_fwd_tc_kernel")) \
       return ATTN_ERR_CUDA;                                                                              \
-    attn_fwd_tc_kernel<SG, TF><<<grid, FA_THREADS, FA_SMEM, stream>>>(maps, p);                          \
+    launched = launch_pdl(attn_fwd_tc_kernel<SG, TF>, dim3(grid), dim3(FA_THREADS), FA_SMEM, stream, maps, p); \
   } while (0)
   if (singles && tf32)
     FA_LAUNCH(true, true, 3);
@@ -531,7 +534,7 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
     FA_LAUNCH(false, false, 0);
 #undef FA_LAUNCH
   count_launch();
-  return check_launch("attn_fwd_tc_kernel");
+  return check_launch("attn_fwd_tc_kernel", launched);
 }
 
 }  // namespace attn

@@ -11,6 +11,8 @@
 #include <mutex>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 namespace attn {
@@ -31,6 +33,24 @@ void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_r
 
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s launch failed: %s", what, cudaGetErrorString(e));
+    return ATTN_ERR_CUDA;
+  }
+  return ATTN_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("ATTN_NO_PDL");
+    return !(v && v[0] && strcmp(v, "0") != 0);
+  }();
+  return on;
+}
+
+int check_launch(const char* what, cudaError_t launched) {
+  const cudaError_t last = cudaGetLastError();  // read (and clear) the runtime's record either way
+  const cudaError_t e = launched != cudaSuccess ? launched : last;
   if (e != cudaSuccess) {
     set_error("%s launch failed: %s", what, cudaGetErrorString(e));
     return ATTN_ERR_CUDA;

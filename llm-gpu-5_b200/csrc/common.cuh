@@ -7,6 +7,8 @@
 #include <stdint.h>
 #include <stddef.h>
 
+#include <utility>
+
 #include "../../include/attn_b200.h"
 
 namespace attn {
@@ -18,6 +20,8 @@ void count_launch(int n = 1);
 
 // Check the launch that just happened; returns ATTN_OK or ATTN_ERR_CUDA with the message set.
 int check_launch(const char* what);
+// The same for a launch whose error the launch call returned (cudaLaunchKernelEx).
+int check_launch(const char* what, cudaError_t launched);
 
 #define ATTN_REQUIRE(cond, ...)                 \
   do {                                          \
@@ -37,6 +41,41 @@ int check_launch(const char* what);
   } while (0)
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---- programmatic dependent launch ------------------------------------------------------------
+// The kernels of a training step launch with programmatic stream serialization: a kernel's CTAs may
+// be placed on the SMs as soon as every CTA of its predecessor on the stream has started (or
+// signalled grid_dependents_launch), so their set-up (barrier initialisation, TMEM allocation,
+// descriptor prefetch) overlaps the predecessor's last wave.  Every thread of such a kernel calls
+// grid_dependency_wait() before its first global-memory access: it returns once the predecessor
+// grid has completed and its writes are visible (at once when the kernel was launched without the
+// attribute or its predecessor is not a kernel).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Whether launch_pdl sets the attribute: yes unless the environment variable ATTN_NO_PDL is set to
+// a non-empty value other than "0" when the library first launches (every kernel then waits for its
+// predecessor to complete, as with a plain launch).
+bool pdl_enabled();
+
+// Launch `kernel` on `s` with programmatic stream serialization allowed.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

@@ -217,6 +217,8 @@ int merge_heads(const float* ch, float* ctx, int B, int T, int NH, int HD, cudaS
 // column sums of its right operand as one extra output row.
 __global__ void cast_rows_ones_kernel(const float* __restrict__ x, int64_t ldx, int M, int N,
                                       __nv_bfloat16* __restrict__ y, int64_t ldy, int vec) {
+  grid_dependency_wait();  // x is complete, and the earlier readers of y are done
+  grid_dependents_launch();
   const int64_t chunks = ldy / 8, total = (int64_t)M * chunks;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -250,9 +252,10 @@ int cast_rows_ones(const float* x, int64_t ldx, int M, int N, void* y, int64_t l
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = (int64_t)sms * 8;
   if (blocks > cap) blocks = cap;
-  cast_rows_ones_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, ldx, M, N, (__nv_bfloat16*)y, ldy, vec);
+  const cudaError_t launched = launch_pdl(cast_rows_ones_kernel, dim3((unsigned)blocks), dim3(256), 0, s, x, ldx, M,
+                                          N, (__nv_bfloat16*)y, ldy, vec);
   count_launch();
-  return check_launch("cast_rows_ones_kernel");
+  return check_launch("cast_rows_ones_kernel", launched);
 }
 
 // fp32 -> bf16, 8 elements per thread per step when 16-byte aligned (grid-stride).
@@ -320,6 +323,8 @@ colsum_partial_kernel(const T* __restrict__ X, int64_t ldx, int M, int N, int ro
   constexpr int TX = CS_COLS / V;  // threads along the columns
   constexpr int TY = 256 / TX;     // rows in flight
   __shared__ float red[TY][CS_COLS + 4];
+  grid_dependency_wait();  // X is complete, and the earlier readers of part and Y are done
+  grid_dependents_launch();
   const int tx = threadIdx.x % TX, ty = threadIdx.x / TX;
   const int c0 = blockIdx.x * CS_COLS + tx * V;
   const int r0 = blockIdx.y * rows_per_split;
@@ -398,6 +403,8 @@ colsum_partial_kernel(const T* __restrict__ X, int64_t ldx, int M, int N, int ro
 __global__ void __launch_bounds__(256) colsum_combine_kernel(const float* __restrict__ part, int splits, int N,
                                                              float* __restrict__ out, int accumulate) {
   __shared__ float red[8][33];
+  grid_dependency_wait();  // the partial rows are complete
+  grid_dependents_launch();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int n = blockIdx.x * 32 + lane;
   float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
@@ -430,21 +437,25 @@ static int colsum_launch(const void* X, int x_dtype, int64_t ldx, int M, int N, 
   const size_t es = x_dtype == ATTN_F32 ? 4 : 2;
   int vec = aligned(X, 16) && ((ldx * es) % 16 == 0);
   if (Y) vec = vec && aligned(Y, 8) && ((ldy * 2) % 8 == 0);
+  cudaError_t launched;
   if (x_dtype == ATTN_F32) {
     if (Y)
-      colsum_partial_kernel<float, true><<<g1, 256, 0, s>>>((const float*)X, ldx, M, N, rps, part, Y, ldy, vec);
+      launched = launch_pdl(colsum_partial_kernel<float, true>, g1, dim3(256), 0, s, (const float*)X, ldx, M, N, rps,
+                            part, Y, ldy, vec);
     else
-      colsum_partial_kernel<float, false><<<g1, 256, 0, s>>>((const float*)X, ldx, M, N, rps, part, nullptr, 0, vec);
+      launched = launch_pdl(colsum_partial_kernel<float, false>, g1, dim3(256), 0, s, (const float*)X, ldx, M, N, rps,
+                            part, (__nv_bfloat16*)nullptr, (int64_t)0, vec);
   } else {
-    colsum_partial_kernel<__nv_bfloat16, false><<<g1, 256, 0, s>>>((const __nv_bfloat16*)X, ldx, M, N, rps,
-                                                                   part, nullptr, 0, vec);
+    launched = launch_pdl(colsum_partial_kernel<__nv_bfloat16, false>, g1, dim3(256), 0, s, (const __nv_bfloat16*)X,
+                          ldx, M, N, rps, part, (__nv_bfloat16*)nullptr, (int64_t)0, vec);
   }
   count_launch();
-  int rc = check_launch("colsum_partial_kernel");
+  int rc = check_launch("colsum_partial_kernel", launched);
   if (rc) return rc;
-  colsum_combine_kernel<<<(N + 31) / 32, 256, 0, s>>>(part, splits, N, out, accumulate);
+  launched = launch_pdl(colsum_combine_kernel, dim3((N + 31) / 32), dim3(256), 0, s, (const float*)part, splits, N,
+                        out, accumulate);
   count_launch();
-  return check_launch("colsum_combine_kernel");
+  return check_launch("colsum_combine_kernel", launched);
 }
 
 int colsum(const void* X, int x_dtype, int64_t ldx, int M, int N, float* out, int accumulate,

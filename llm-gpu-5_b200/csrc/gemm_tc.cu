@@ -211,6 +211,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dependency_wait();    // the operands (and an accumulated C) are complete
+  grid_dependents_launch();  // the next kernel's CTAs may take SMs as this grid's CTAs leave
 
   if (warp == 0) {
     if (lane == 0) {
@@ -596,10 +598,12 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
     ATTN_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s));
   static CtxOnce attr[4];
   const int grid = p.units < sms ? p.units : sms;
+  cudaError_t launched = cudaSuccess;
 #define GT_LAUNCH(EW, TF, slot)                                                                    \
   do {                                                                                             \
     if (!set_smem_limit_once(gemm_tc_kernel<EW, TF>, GT_SMEM, attr[slot])) return ATTN_ERR_CUDA;   \
-    gemm_tc_kernel<EW, TF><<<grid, Epi<EW>::kthreads, GT_SMEM, s>>>(tmA, tmB, tmC, tmAux, p);      \
+    launched = launch_pdl(gemm_tc_kernel<EW, TF>, dim3(grid), dim3(Epi<EW>::kthreads), GT_SMEM, s, tmA, tmB, \
+                          tmC, tmAux, p);                                                          \
   } while (0)
   if (wide && tf32)
     GT_LAUNCH(8, true, 3);
@@ -611,7 +615,7 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
     GT_LAUNCH(4, false, 0);
 #undef GT_LAUNCH
   count_launch();
-  return check_launch("gemm_tc_kernel");
+  return check_launch("gemm_tc_kernel", launched);
 }
 
 }  // namespace attn
