@@ -384,6 +384,7 @@ def run_ours(args, cfg):
     reducer = None
     if dist is not None:
         attn.grad_sync_group = dist.group.WORLD
+        attn.grad_buckets = args.buckets
         if not args.nccl:  # the library's NVSwitch multicast all-reduce where the GPUs support it
             reducer = pkg.dp.make_grad_reducer(attn.flat_grads.numel())
             if reducer is not None:
@@ -402,6 +403,16 @@ def run_ours(args, cfg):
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
+
+    align_buf = torch.zeros(1, device="cuda")
+
+    def align():
+        """After barrier(): a one-float all-reduce on the current stream, so every rank's stream
+        leaves it together and the start events below are recorded at the same moment.  Without it
+        the host's skew between the ranks after the barrier (up to milliseconds) is timed as step
+        work by whichever rank starts first, since the first gradient all-reduce makes it wait."""
+        if dist is not None:
+            dist.all_reduce(align_buf)
 
     def max_over_ranks(v):
         if dist is None:
@@ -436,6 +447,7 @@ def run_ours(args, cfg):
 
     # ---------------- eager steps: device time and host enqueue time per step
     barrier()
+    align()
     h0 = time.perf_counter()
     ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ea.record()
@@ -454,6 +466,7 @@ def run_ours(args, cfg):
             times = []
             for _ in range(7):
                 barrier()
+                align()
                 ca, cb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 ca.record()
                 fn()
@@ -490,6 +503,7 @@ def run_ours(args, cfg):
     if not use_graph:
         marks.spans.clear()
     clocks.start()
+    align()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     h1 = time.perf_counter()
@@ -564,6 +578,7 @@ def run_ours(args, cfg):
     for k in range(2):
         e2e_step(k)
     barrier()
+    align()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(comp)
@@ -630,11 +645,14 @@ def run_ours(args, cfg):
                     host_enqueue_ms_graph=host_replay_ms if use_graph else None, comm_ms=comm_ms,
                     comm_ms_nccl=comm_ms_nccl, comm_bytes=attn.flat_grads.numel() * 4 if dist is not None else 0,
                     grad_sync=None if dist is None else (
-                        "NVSwitch multicast all-reduce kernel (attn_grad_allreduce)" if reducer is not None
-                        else "NCCL all_reduce"),
+                        ("NVSwitch multicast all-reduce kernel (attn_grad_allreduce)" if reducer is not None
+                         else "NCCL all_reduce")
+                        + ("; two buckets: dWo/dbo after the dWo GEMM, dWqkv/dbqkv after the dWqkv GEMM"
+                           if attn.grad_buckets else "; one bucket after the dWqkv GEMM")),
                     note="eager: the same step launched op by op from Python; comm_ms: the step's gradient "
                          "all-reduce alone, comm_ms_nccl: NCCL's on the same buffer, medians of 5, max over "
-                         "ranks"),
+                         "ranks; every timed region starts after a barrier and a one-float all-reduce on the "
+                         "timed stream, so the ranks' start events are recorded together"),
         gpu_launches=launches_per_step * steps,
         e2e=dict(value=GB * T / (e2e_ms * 1e-3), unit="tokens/s", h2d_bytes_per_step=h2d * world,
                  d2h_bytes_per_step=d2h * world, ms_per_step=e2e_ms, copy_gbs=copy_gbs,
@@ -1205,6 +1223,9 @@ def main():
                     help="leave out the 'configs' object (configurations 1-4 measured after the headline)")
     ap.add_argument("--nccl", action="store_true",
                     help="sum the gradients with NCCL instead of the library's NVSwitch multicast all-reduce")
+    ap.add_argument("--buckets", action="store_true",
+                    help="all-reduce dWo/dbo right after the dWo GEMM and dWqkv/dbqkv after the dWqkv GEMM "
+                         "(default: one bucket after the dWqkv GEMM)")
     ap.add_argument("--ar-blocks", type=int, default=0,
                     help="CTAs of the multicast all-reduce (0: the library's default)")
     ap.add_argument("--ar-serial", action="store_true",

@@ -22,14 +22,18 @@ def shard(global_batch: int, world: int, rank: int) -> tuple[int, int]:
     return rank * per, per
 
 
+def _numel(shape) -> int:
+    n = 1
+    for s in shape:
+        n *= s
+    return n
+
+
 def _layout(params) -> list[tuple[str, int, tuple[int, ...]]]:
     out, off = [], 0
     for name, shape in params:
         out.append((name, off, shape))
-        n = 1
-        for s in shape:
-            n *= s
-        off += n
+        off += _numel(shape)
     return out
 
 
@@ -48,14 +52,27 @@ def ffn_grad_layout(C: int) -> list[tuple[str, int, tuple[int, ...]]]:
 
 def layout_size(layout) -> int:
     name, off, shape = layout[-1]
-    n = 1
-    for s in shape:
-        n *= s
-    return off + n
+    return off + _numel(shape)
 
 
 def flat_grad_size(C: int) -> int:
     return layout_size(grad_layout(C))
+
+
+def grad_buckets(layout, first_names) -> list[tuple[int, int]]:
+    """Split a flat gradient buffer (``layout`` as grad_layout) into two all-reduce buckets: the
+    parameters named in ``first_names`` (final earlier in backward, sent first) and the rest, as
+    [lo, hi) float ranges in the order they are sent.  Each must be one contiguous run starting on a
+    16-byte boundary; otherwise the whole buffer is one bucket."""
+    total = layout_size(layout)
+    spans = {name: (off, off + _numel(shape)) for name, off, shape in layout}
+    first = sorted(spans[n] for n in first_names)
+    lo, hi = first[0][0], first[-1][1]
+    contiguous = all(a[1] == b[0] for a, b in zip(first, first[1:]))
+    if not contiguous or lo % 4 or (lo != 0 and hi != total) or (lo == 0 and hi % 4):
+        return [(0, total)]
+    rest = (hi, total) if lo == 0 else (0, lo)
+    return [(lo, hi), rest]
 
 
 def allreduce_grads(flat, group=None, async_op: bool = False):
@@ -109,12 +126,17 @@ class MulticastGradReducer:
     max_blocks = 0  # CTAs of one launch (0: the library's default); the same on every rank
     overlap = True  # a module's backward runs the reduction beside its last GEMM (False: after it)
 
-    def allreduce(self):
-        """Sum the buffer over the ranks, in place on every rank (one launch, current stream)."""
+    def allreduce(self, lo: int = 0, hi: int = None):
+        """Sum floats [lo, hi) of the buffer (all of it by default) over the ranks, in place on every
+        rank (one launch, current stream).  ``lo`` must be a multiple of 4 (16-byte aligned)."""
         import torch
         from ._lib import call
-        call("attn_grad_allreduce", self.handle.multicast_ptr, self.handle.signal_pad_ptrs_dev, self.rank,
-             self.world, self.numel, self.handle.signal_pad_size, int(self.max_blocks),
+        hi = self.numel if hi is None else int(hi)
+        lo = int(lo)
+        if not 0 <= lo < hi <= self.numel or lo % 4:
+            raise ValueError(f"MulticastGradReducer.allreduce: bad range [{lo}, {hi}) of {self.numel} floats")
+        call("attn_grad_allreduce", self.handle.multicast_ptr + 4 * lo, self.handle.signal_pad_ptrs_dev,
+             self.rank, self.world, hi - lo, self.handle.signal_pad_size, int(self.max_blocks),
              torch.cuda.current_stream().cuda_stream)
 
 

@@ -30,7 +30,7 @@ from . import dp
 from . import mha_ops as ops
 from ._lib import check_device_error
 from .mha import (DeviceBuffer, GPTConfig, Parameter, _as_tensor, _NULL, attach_grad_reducer, device_checked,
-                  finish_grad_sync, start_grad_sync)
+                  finish_grad_sync, grad_sync_buckets, start_grad_sync)
 
 
 class FeedForward:
@@ -64,7 +64,8 @@ class FeedForward:
         self.profiler = None
         self.grad_sync_group = None
         self.grad_reducer = None  # a dp.MulticastGradReducer holding flat_grads (use_grad_reducer)
-        self._grad_sync_work = None
+        self.grad_buckets = False  # True: all-reduce dWproj/dbproj as soon as they are final, then dWfc/dbfc
+        self._grad_sync_works = []
         self._cache = None
 
     def _rng(self, name):
@@ -167,6 +168,9 @@ class FeedForward:
         with self._rng("gemm_dwproj"):
             ops.gemm(c["act"].data_ptr(), H, True, dy_op.data_ptr(), C, False, mm, self.c_proj_w.grads.data_ptr(), C,
                      torch.float32, H, C, M, accumulate=accumulate)
+        buckets = grad_sync_buckets(self, dp.ffn_grad_layout(C), ("c_proj_w", "c_proj_b"))
+        # dWproj and dbproj are final: with buckets, their all-reduce overlaps the GEMMs that follow
+        pending_p = start_grad_sync(self, buckets[0]) if len(buckets) == 2 else None
         # dPre = (dOut W_proj^T) * gelu'(pre)   (model/gpt.py:433-436)
         dpre = torch.empty((M, H), dtype=dt, device="cuda")
         with self._rng("gemm_dhidden_gelu"):
@@ -184,13 +188,13 @@ class FeedForward:
                          torch.float32, C, H, M, accumulate=accumulate)
             with self._rng("colsum"):
                 ops.colsum(dpre.data_ptr(), dt, H, M, H, self.c_fc_b.grads, accumulate=accumulate)
-        pending = start_grad_sync(self)  # the gradients are final: their all-reduce overlaps dIn
+        pending = start_grad_sync(self, buckets[-1])  # the rest are final: their all-reduce overlaps dIn
         # dIn = dPre W_fc^T   (model/gpt.py:443)
         dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_dx"):
             ops.gemm(dpre.data_ptr(), H, False, c["w_fc"].data_ptr(), H, True, mm, dx.data_ptr(), C, torch.float32,
                      M, C, H)
-        finish_grad_sync(pending)
+        finish_grad_sync(pending_p, pending)
         return DeviceBuffer(dx)
 
     def use_grad_reducer(self, reducer):
@@ -220,9 +224,9 @@ class FeedForward:
     def wait_grad_sync(self):
         """Wait for the gradient all-reduce launched by the last backward (if any), and raise
         DeviceWaitError if a kernel of a finished call gave up a bounded wait."""
-        if self._grad_sync_work is not None:
-            self._grad_sync_work.wait()
-            self._grad_sync_work = None
+        for work in self._grad_sync_works:
+            work.wait()
+        self._grad_sync_works = []
         check_device_error()
 
     def free_forward_caches(self):

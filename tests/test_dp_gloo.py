@@ -2,7 +2,7 @@
 
 Each rank takes its shard of the global batch (``dp.shard``), runs the oracle's forward and
 backward on it, packs the four parameter gradients into the flat layout the module all-reduces
-(``dp.grad_layout``) and sums them with ``dp.allreduce_grads``.  The result must equal the
+(``dp.grad_layout``) and sums them with ``dp.allreduce_grads``, bucket by bucket (``dp.grad_buckets``).  The result must equal the
 full-batch gradient of one process (the reference's single-GPU semantics, model/gpt.py:687-694),
 and each rank's dX must equal its rows of the full-batch dX.  No GPU is used.
 """
@@ -50,7 +50,11 @@ def _rank(rank, world, port, q):
         out, cache = O.mha_forward(inp["x"][rows], inp["w_qkv"], inp["b_qkv"], inp["w_o"], inp["b_o"], n, T, NH)
         d_in, *grads = O.mha_backward(cache, inp["dy"][rows], inp["w_qkv"], inp["w_o"], n, T, NH)
         flat = torch.from_numpy(_flat(dp, C, grads))
-        dp.allreduce_grads(flat)
+        # the module's two buckets, in the order its backward sends them: dWo/dbo, then dWqkv/dbqkv
+        buckets = dp.grad_buckets(dp.grad_layout(C), ("c_proj_w", "c_proj_b"))
+        assert len(buckets) == 2
+        for lo, hi in buckets:
+            dp.allreduce_grads(flat[lo:hi])
         q.put((rank, first, n, flat.numpy(), d_in))
         dist.destroy_process_group()
     except Exception as e:  # report to the parent instead of hanging it
@@ -93,6 +97,18 @@ def test_shard_and_layout():
     assert [(n, o) for n, o, _ in lay] == [("c_attn_w", 0), ("c_attn_b", 768 * 2304),
                                           ("c_proj_w", 768 * 2304 + 2304), ("c_proj_b", 768 * 2304 + 2304 + 768 * 768)]
     assert dp.flat_grad_size(768) == 2362368  # 9.45 MB of fp32 per all-reduce at d_model 768
+    # buckets: the output projection's gradients (the tail of the buffer) first, then the rest;
+    # both start on 16-byte boundaries and together cover the buffer once
+    tail = 768 * 2304 + 2304
+    assert dp.grad_buckets(lay, ("c_proj_w", "c_proj_b")) == [(tail, 2362368), (0, tail)]
+    flay = dp.ffn_grad_layout(768)
+    assert dp.grad_buckets(flay, ("c_proj_w", "c_proj_b")) == [(768 * 3072 + 3072, dp.layout_size(flay)),
+                                                               (0, 768 * 3072 + 3072)]
+    # a first bucket that is not contiguous or not 16-byte aligned: one bucket for everything
+    assert dp.grad_buckets(lay, ("c_attn_w", "c_proj_w")) == [(0, 2362368)]
+    odd = dp.grad_layout(3)  # [9*3 | 9 | 3*3 | 3]: the tail starts at float 36, then 45 floats
+    assert dp.grad_buckets(odd, ("c_proj_w", "c_proj_b")) == [(36, 48), (0, 36)]
+    assert dp.grad_buckets(dp.grad_layout(1), ("c_proj_w", "c_proj_b")) == [(0, 8)]  # tail at float 6
 
 
 def _rank_that_may_leave(rank, world, port, q):

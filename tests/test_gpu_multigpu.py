@@ -4,10 +4,12 @@
   the host: buffers whose values are small integers (exact in float32), three calls in a row (the
   signal pads are reused) and a call replayed from a captured CUDA graph; a buffer size that is not a
   multiple of 4 floats (the scalar tail).
+  A bucket (a sub-range) is summed alone and the rest of the buffer is left as it was.
 * a data-parallel step: each rank runs MultiHeadAttention forward + backward on half of the batch
-  with its gradients in a MulticastGradReducer; the summed gradients match those of one module that
-  sees the whole batch (model/gpt.py:687-694), fp32 within 1e-5 and bf16 within 2e-2.
-The processes use NCCL only for the process group and its barrier; NVLS multicast is what is tested.
+  with its gradients in a MulticastGradReducer (two buckets, then one) or summed by NCCL (two
+  buckets); the summed gradients match those of one module that sees the whole batch
+  (model/gpt.py:687-694), fp32 within 1e-5 and bf16 within 2e-2.
+The multicast cases use NCCL only for the process group and its barrier.
 """
 import os
 import socket
@@ -66,10 +68,20 @@ def _worker(rank, world, port, result_dir):
             torch.cuda.synchronize()
             out[f"ar{n}_graph"] = float((red.buffer - want).abs().max())
             graph.reset()
+            # a bucket [lo, hi): only it is summed, the rest of the buffer is left alone
+            lo, hi = 4 * (n // 12), n - 5
+            red.buffer.copy_(base[rank])
+            red.allreduce(lo, hi)
+            torch.cuda.synchronize()
+            expect = base[rank].clone()
+            expect[lo:hi] = want[lo:hi]
+            out[f"ar{n}_bucket"] = float((red.buffer - expect).abs().max())
             del red
             dist.barrier()
-        # ---- a data-parallel step against the whole batch on one module
-        for prec, tol in (("fp32", 1e-5), ("bf16", 2e-2)):
+        # ---- a data-parallel step against the whole batch on one module: the multicast all-reduce
+        # with two buckets and with one (the default), and NCCL with two buckets
+        for prec, tol, mode in (("fp32", 1e-5, "mc2"), ("bf16", 2e-2, "mc2"), ("bf16", 2e-2, "mc1"),
+                                ("bf16", 2e-2, "nccl2")):
             B, T, C, NH = 4, 130, 128, 2
             inp = O.make_config_inputs(9, B, T, C, NH)
             cfg = pkg.GPTConfig(vocab_size=50, embedding_dim=C, num_heads=NH, max_len=T, attention_precision=prec)
@@ -78,8 +90,11 @@ def _worker(rank, world, port, result_dir):
                 for p, k in ((m.c_attn_w, "w_qkv"), (m.c_attn_b, "b_qkv"), (m.c_proj_w, "w_o"), (m.c_proj_b, "b_o")):
                     p.weights.copy_(torch.from_numpy(inp[k]))
             dp_mod, full = mods
-            red = pkg.dp.MulticastGradReducer(dp_mod.flat_grads.numel())
-            dp_mod.use_grad_reducer(red)
+            red = None
+            if mode != "nccl2":
+                red = pkg.dp.MulticastGradReducer(dp_mod.flat_grads.numel())
+                dp_mod.use_grad_reducer(red)
+            dp_mod.grad_buckets = mode != "mc1"
             dp_mod.grad_sync_group = dist.group.WORLD
             b0, nb = pkg.dp.shard(B, world, rank)
             x = torch.from_numpy(inp["x"]).cuda().view(B, T, C)
@@ -90,9 +105,9 @@ def _worker(rank, world, port, result_dir):
             full.forward(x.reshape(-1, C), B, T).free()
             full.backward(dy.reshape(-1, C), B, T).free()
             torch.cuda.synchronize()
-            out[f"step_{prec}"] = O.rel_err(dp_mod.flat_grads.double().cpu().numpy(),
-                                            full.flat_grads.double().cpu().numpy())
-            out[f"tol_{prec}"] = tol
+            out[f"step_{prec}_{mode}"] = O.rel_err(dp_mod.flat_grads.double().cpu().numpy(),
+                                                   full.flat_grads.double().cpu().numpy())
+            out[f"tol_{prec}_{mode}"] = tol
             dp_mod.grad_sync_group = None
             del red
             dist.barrier()
@@ -117,6 +132,8 @@ def test_multicast_allreduce_and_data_parallel_step(tmp_path):
         for k, v in res.items():
             if k.startswith("ar"):
                 assert v == 0.0, (r, k, v)
-        for prec in ("fp32", "bf16"):
-            assert res[f"step_{prec}"] < res[f"tol_{prec}"], (r, prec, res[f"step_{prec}"])
+        steps = [k for k in res if k.startswith("step_")]
+        assert len(steps) == 4, res
+        for k in steps:
+            assert res[k] < res["tol_" + k[5:]], (r, k, res[k])
         assert res["device_error"] == 0
