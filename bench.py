@@ -388,7 +388,10 @@ def run_ours(args, cfg):
         if not args.nccl:  # the library's NVSwitch multicast all-reduce where the GPUs support it
             reducer = pkg.dp.make_grad_reducer(attn.flat_grads.numel())
             if reducer is not None:
-                reducer.max_blocks = args.ar_blocks
+                if args.ar_blocks is not None:
+                    reducer.max_blocks = args.ar_blocks
+                if args.ar_reserve is not None:
+                    reducer.reserve_sms = args.ar_reserve
                 reducer.overlap = not args.ar_serial
                 attn.use_grad_reducer(reducer)
 
@@ -645,8 +648,9 @@ def run_ours(args, cfg):
                     host_enqueue_ms_graph=host_replay_ms if use_graph else None, comm_ms=comm_ms,
                     comm_ms_nccl=comm_ms_nccl, comm_bytes=attn.flat_grads.numel() * 4 if dist is not None else 0,
                     grad_sync=None if dist is None else (
-                        ("NVSwitch multicast all-reduce kernel (attn_grad_allreduce)" if reducer is not None
-                         else "NCCL all_reduce")
+                        (f"NVSwitch multicast all-reduce kernel (attn_grad_allreduce), {reducer.max_blocks} "
+                         f"CTAs beside the dX GEMM on {reducer.reserve_sms} SMs it leaves free"
+                         if reducer is not None else "NCCL all_reduce")
                         + ("; two buckets: dWo/dbo after the dWo GEMM, dWqkv/dbqkv after the dWqkv GEMM"
                            if attn.grad_buckets else "; one bucket after the dWqkv GEMM")),
                     note="eager: the same step launched op by op from Python; comm_ms: the step's gradient "
@@ -1226,8 +1230,11 @@ def main():
     ap.add_argument("--buckets", action="store_true",
                     help="all-reduce dWo/dbo right after the dWo GEMM and dWqkv/dbqkv after the dWqkv GEMM "
                          "(default: one bucket after the dWqkv GEMM)")
-    ap.add_argument("--ar-blocks", type=int, default=0,
-                    help="CTAs of the multicast all-reduce (0: the library's default)")
+    ap.add_argument("--ar-blocks", type=int, default=None,
+                    help="CTAs of the multicast all-reduce (default: the reducer's, 16)")
+    ap.add_argument("--ar-reserve", type=int, default=None,
+                    help="SMs the dX GEMM leaves to the multicast all-reduce beside it (default: the "
+                         "reducer's, 16; 0: none)")
     ap.add_argument("--ar-serial", action="store_true",
                     help="run the multicast all-reduce after the input-gradient GEMM instead of beside it")
     ap.add_argument("--eager", action="store_true",

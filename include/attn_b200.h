@@ -56,9 +56,9 @@ extern "C" {
  *   signal_pads  device address of an array of `world` pointers, rank p's uint32 signal pad at
  *                [p]; each pad holds at least attn_grad_allreduce_signal_bytes(n, world) bytes, zero
  *                before the first call (the kernel leaves them zero)
- *   max_blocks   CTAs of 256 threads to use (0: the default of 32, a fraction of the SMs, so that the
- *                reduction can run beside the GEMM that follows the weight gradients); at most
- *                128, the same on every rank
+ *   max_blocks   CTAs of 256 threads to use (0: the default of 16); at most 128, the same on every
+ *                rank.  To overlap the reduction with a GEMM on another stream, give the GEMM
+ *                that many fewer SMs (attn_gemm_ex): sharing an SM slows the persistent GEMM.
  * world 2 .. 8.  The kernel meets the other ranks in cross-GPU barriers before and after the
  * reduction; a barrier wait that gives up (after 2 s) records site 400 or 401 in the status word
  * (attn_device_error) and the kernel returns.
@@ -227,6 +227,16 @@ int attn_gemm(const void* A, int64_t lda, int a_trans,
               const void* B, int64_t ldb, int b_trans, int ab_dtype,
               void* C, int64_t ldc, int c_dtype, const float* bias,
               int M, int N, int K, int accumulate, void* stream);
+
+/*
+ * attn_gemm on at most max_ctas SMs (0: all of them).  The tensor-core GEMM is persistent, one CTA
+ * per SM; a caller that overlaps it with a kernel on another stream (the gradient all-reduce beside
+ * the dX GEMM) leaves that kernel whole SMs this way.  The CUDA-core path ignores max_ctas.
+ */
+int attn_gemm_ex(const void* A, int64_t lda, int a_trans,
+                 const void* B, int64_t ldb, int b_trans, int ab_dtype,
+                 void* C, int64_t ldc, int c_dtype, const float* bias,
+                 int M, int N, int K, int accumulate, int max_ctas, void* stream);
 
 /*
  * attn_gemm with the feed-forward activation in the epilogue (no accumulate), replacing the FFN's

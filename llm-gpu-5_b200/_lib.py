@@ -50,6 +50,7 @@ SIGNATURES = {
                                  _i, _p]),
     "attn_probs": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i64, _f, _i, _p]),
     "attn_gemm": (_i, [_p, _i64, _i, _p, _i64, _i, _i, _p, _i64, _i, _p, _i, _i, _i, _i, _p]),
+    "attn_gemm_ex": (_i, [_p, _i64, _i, _p, _i64, _i, _i, _p, _i64, _i, _p, _i, _i, _i, _i, _i, _p]),
     "attn_gemm_act": (_i, [_p, _i64, _i, _p, _i64, _i, _i, _p, _i64, _i, _p, _i, _i, _i, _i, _p, _i64, _i, _p]),
     "attn_colsum_workspace_size": (_sz, [_i, _i]),
     "attn_colsum": (_i, [_p, _i, _i64, _i, _i, _p, _i, _p, _sz, _p]),

@@ -23,9 +23,10 @@
 
 namespace attn {
 
-// 256 threads of at most 64 registers and no shared memory: a block fits on an SM beside a
-// persistent GEMM CTA (192 threads of 255 registers, 229 KB of shared memory), so the reduction can
-// overlap the GEMM that follows the weight gradients.
+// 256 threads of at most 64 registers and no shared memory.  The reduction overlaps the GEMM that
+// follows the weight gradients; that GEMM leaves it SMs of its own (attn_gemm_ex), since a block
+// sharing an SM with a persistent GEMM CTA (192 threads of 255 registers) slows that CTA, and the
+// GEMM ends with its slowest CTA.
 constexpr int AR_THREADS = 256;
 constexpr int AR_MAX_BLOCKS = 128;  // 2 channels x 128 blocks x 8 slots x 4 bytes = 8 KB of signal pad
 constexpr int AR_MAX_WORLD = 8;     // ranks of one NVSwitch domain that one launch serves
@@ -123,9 +124,10 @@ grad_allreduce_kernel(float* __restrict__ mc, uint32_t* const* __restrict__ pads
 }
 
 // Blocks of one launch, the same count on every rank (the barrier pairs blocks by index): no more
-// than the slice needs, at most max_blocks (0: AR_DEFAULT_BLOCKS, a few SMs' worth, which leaves
-// the rest of the GPU to the GEMM the reduction overlaps).
-constexpr int AR_DEFAULT_BLOCKS = 32;
+// than the slice needs, at most max_blocks (0: AR_DEFAULT_BLOCKS).  Sixteen reach the NVSwitch
+// rate on 8 GPUs (42 us for 9.45 MB back to back, as 128 do) and need only the 16 SMs that the
+// GEMM beside the reduction leaves free.
+constexpr int AR_DEFAULT_BLOCKS = 16;
 static int ar_blocks(int64_t n, int world, int max_blocks) {
   const int64_t per_rank = (n / 4 + world - 1) / world;
   int64_t b = (per_rank + (int64_t)AR_THREADS * AR_UNROLL - 1) / ((int64_t)AR_THREADS * AR_UNROLL);

@@ -212,7 +212,7 @@ bool tc_gemm_supported(int M, int N, int K, int64_t lda, int a_trans, int64_t ld
                        const void* A, const void* B, int tf32);
 int gemm_tc(const void*, int64_t, int, const void*, int64_t, int, void*, int64_t, int,
             const float*, int, int, int, int, cudaStream_t, int act = ACT_NONE, const void* aux = nullptr,
-            int64_t ldaux = 0, int aux_dtype = ATTN_F32, int tf32 = 0);
+            int64_t ldaux = 0, int aux_dtype = ATTN_F32, int tf32 = 0, int max_ctas = 0);
 bool tc_gemm_act_ok(const void* C, int64_t ldc, int c_dtype, int act, const void* aux, int64_t ldaux,
                     int aux_dtype);
 
@@ -380,7 +380,15 @@ int attn_decode(const void* q, const void* k_cache, const void* v_cache, void* o
 int attn_gemm(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans,
               int ab_dtype, void* C, int64_t ldc, int c_dtype, const float* bias, int M, int N, int K,
               int accumulate, void* stream) {
+  return attn_gemm_ex(A, lda, a_trans, B, ldb, b_trans, ab_dtype, C, ldc, c_dtype, bias, M, N, K, accumulate, 0,
+                      stream);
+}
+
+int attn_gemm_ex(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans,
+                 int ab_dtype, void* C, int64_t ldc, int c_dtype, const float* bias, int M, int N, int K,
+                 int accumulate, int max_ctas, void* stream) {
   clear_error();
+  ATTN_REQUIRE(max_ctas >= 0, "attn_gemm: max_ctas must be >= 0");
   ATTN_REQUIRE(A && B && C, "attn_gemm: null pointer argument");
   ATTN_REQUIRE(M > 0 && N > 0 && K > 0, "attn_gemm: M, N, K must be positive");
   ATTN_REQUIRE(ab_dtype == ATTN_F32 || ab_dtype == ATTN_BF16 || ab_dtype == ATTN_TF32,
@@ -392,7 +400,7 @@ int attn_gemm(const void* A, int64_t lda, int a_trans, const void* B, int64_t ld
   const int tf32 = ab_dtype == ATTN_TF32;
   if (ab_dtype != ATTN_F32 && tc_gemm_supported(M, N, K, lda, a_trans, ldb, b_trans, A, B, tf32))
     return gemm_tc(A, lda, a_trans, B, ldb, b_trans, C, ldc, c_dtype, bias, M, N, K, accumulate,
-                   as_stream(stream), ACT_NONE, nullptr, 0, ATTN_F32, tf32);
+                   as_stream(stream), ACT_NONE, nullptr, 0, ATTN_F32, tf32, max_ctas);
   // shapes the tensor-core kernel does not take: tf32 operands are float32 storage, so the exact
   // float32 CUDA-core GEMM serves them
   return gemm_simt(A, lda, a_trans, B, ldb, b_trans, tf32 ? ATTN_F32 : ab_dtype, C, ldc, c_dtype, bias, M, N,

@@ -506,7 +506,7 @@ bool tc_gemm_act_ok(const void* C, int64_t ldc, int c_dtype, int act, const void
 
 int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans, void* C,
             int64_t ldc, int c_dtype, const float* bias, int M, int N, int K, int accumulate,
-            cudaStream_t s, int act, const void* aux, int64_t ldaux, int aux_dtype, int tf32) {
+            cudaStream_t s, int act, const void* aux, int64_t ldaux, int aux_dtype, int tf32, int max_ctas) {
   if (act != ACT_NONE && (accumulate || !tc_gemm_act_ok(C, ldc, c_dtype, act, aux, ldaux, aux_dtype))) {
     set_error("gemm_tc: activation epilogue unsupported for this output layout");
     return ATTN_ERR_UNSUPPORTED;
@@ -550,7 +550,8 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   p.tiles_m = (M + GT_BM - 1) / GT_BM;
   p.tiles_n = (N + GT_BN - 1) / GT_BN;
   p.kb_total = (K + (int)w - 1) / (int)w;
-  const int sms = num_sms();
+  // persistent CTAs: one per SM, or max_ctas when the caller leaves SMs to a kernel on another stream
+  const int sms = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();
   const int tiles = p.tiles_m * p.tiles_n;
   int splits = c_dtype == ATTN_F32 && act == ACT_NONE ? choose_splits(tiles, p.kb_total, sms) : 1;
   p.kb_per_split = (p.kb_total + splits - 1) / splits;

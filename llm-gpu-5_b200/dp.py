@@ -123,8 +123,20 @@ class MulticastGradReducer:
         torch.cuda.synchronize()
         dist.barrier(group=self.group)  # every rank's buffer and pads exist before the first launch
 
-    max_blocks = 0  # CTAs of one launch (0: the library's default); the same on every rank
+    # CTAs of one launch (0: the library's default of 16), the same on every rank, and SMs that the
+    # GEMM beside an overlapped reduction leaves to it.  On 8 B200s at 64 sequences per GPU: 16/16
+    # 0.828 ms per step, 8/8 0.827, 32/32 0.834, and 32 CTAs sharing the GEMM's SMs 0.874.
+    max_blocks = 16
+    reserve_sms = 16
     overlap = True  # a module's backward runs the reduction beside its last GEMM (False: after it)
+
+    def gemm_ctas(self) -> int:
+        """max_ctas for the GEMM that runs beside this reducer's launch (0: every SM)."""
+        if not self.overlap or self.reserve_sms <= 0:
+            return 0
+        import torch
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        return max(1, sms - int(self.reserve_sms))
 
     def allreduce(self, lo: int = 0, hi: int = None):
         """Sum floats [lo, hi) of the buffer (all of it by default) over the ranks, in place on every

@@ -30,7 +30,7 @@ from . import dp
 from . import mha_ops as ops
 from ._lib import check_device_error
 from .mha import (DeviceBuffer, GPTConfig, Parameter, _as_tensor, _NULL, attach_grad_reducer, device_checked,
-                  finish_grad_sync, grad_sync_buckets, start_grad_sync)
+                  finish_grad_sync, grad_sync_buckets, grad_sync_gemm_ctas, start_grad_sync)
 
 
 class FeedForward:
@@ -193,7 +193,7 @@ class FeedForward:
         dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_dx"):
             ops.gemm(dpre.data_ptr(), H, False, c["w_fc"].data_ptr(), H, True, mm, dx.data_ptr(), C, torch.float32,
-                     M, C, H)
+                     M, C, H, max_ctas=grad_sync_gemm_ctas(self))
         finish_grad_sync(pending_p, pending)
         return DeviceBuffer(dx)
 

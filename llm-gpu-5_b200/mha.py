@@ -80,6 +80,14 @@ def start_grad_sync(mod, bucket=None):
     return lambda: torch.cuda.current_stream().wait_event(joined)
 
 
+def grad_sync_gemm_ctas(mod) -> int:
+    """max_ctas for the GEMM that follows start_grad_sync: fewer than every SM when the module's
+    multicast reducer runs beside it and asks for SMs of its own (reducer.reserve_sms)."""
+    if mod.grad_sync_group is None or mod.grad_reducer is None:
+        return 0
+    return mod.grad_reducer.gemm_ctas()
+
+
 def grad_sync_buckets(mod, layout, first_names):
     """The module's all-reduce buckets: one for the whole buffer, or, with ``mod.grad_buckets``,
     the parameters in ``first_names`` (final earlier in backward) and the rest (dp.grad_buckets)."""
@@ -497,7 +505,7 @@ class MultiHeadAttention:
         dx = torch.empty((M, C), dtype=torch.float32, device="cuda")
         with self._rng("gemm_dx"):
             ops.gemm(gb, 3 * C, False, c["w_qkv"].data_ptr(), 3 * C, True, mm, dx.data_ptr(), C,
-                     torch.float32, M, C, 3 * C)
+                     torch.float32, M, C, 3 * C, max_ctas=grad_sync_gemm_ctas(self))
         finish_grad_sync(pending_o, pending)
         return DeviceBuffer(dx)
 

@@ -129,8 +129,13 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, scale:
 
 def gemm(A: int, lda: int, a_trans: bool, B: int, ldb: int, b_trans: bool, ab_dtype: torch.dtype,
          C: int, ldc: int, c_dtype: torch.dtype, M: int, N: int, K: int, bias: int | None = None,
-         accumulate: bool = False):
-    """C[M,N] (=|+=) op(A) op(B) (+bias) on raw device addresses (see include/attn_b200.h)."""
+         accumulate: bool = False, max_ctas: int = 0):
+    """C[M,N] (=|+=) op(A) op(B) (+bias) on raw device addresses (see include/attn_b200.h); on at
+    most ``max_ctas`` SMs when it is positive (attn_gemm_ex)."""
+    if max_ctas:
+        call("attn_gemm_ex", A, lda, int(a_trans), B, ldb, int(b_trans), dtype_code(ab_dtype), C, ldc,
+             dtype_code(c_dtype), bias, M, N, K, int(accumulate), int(max_ctas), _stream())
+        return
     call("attn_gemm", A, lda, int(a_trans), B, ldb, int(b_trans), dtype_code(ab_dtype), C, ldc,
          dtype_code(c_dtype), bias, M, N, K, int(accumulate), _stream())
 

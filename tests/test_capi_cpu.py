@@ -66,6 +66,9 @@ def test_bad_arguments_rejected_without_launch():
     # gemm: leading dimension too small
     rc = L.attn_gemm(fake, 32, 0, fake, 64, 0, 0, fake, 64, 0, None, 64, 64, 64, 0, None)
     assert rc == -1
+    # gemm on a capped number of SMs: a negative cap is refused
+    rc = L.attn_gemm_ex(fake, 64, 0, fake, 64, 0, 1, fake, 64, 0, None, 64, 64, 64, 0, -1, None)
+    assert rc == -1 and "max_ctas" in L.attn_last_error_string().decode()
     # decode with a head_dim the vector width does not divide
     rc = L.attn_decode(fake, fake, fake, fake, None, 1, 1, 8, 12, 12, 12, 96, 12, 12, 0.3, 1, fake,
                        1 << 20, None)

@@ -370,6 +370,42 @@ def test_gemm_tc_unaligned_output_pitch(pkg, cuda_dev, M, N, K, at, bt, pad):
     assert pkg.lib.attn_device_error(1) == 0
 
 
+@pytest.mark.parametrize("max_ctas", [1, 7, 116])
+def test_gemm_on_capped_sms(pkg, cuda_dev, max_ctas):
+    """attn_gemm_ex on at most max_ctas SMs (the dX GEMM beside the gradient all-reduce): the
+    persistent CTAs take more tiles each.  A bf16 output has no K splits, so the result is bit for
+    bit that of the uncapped launch; an fp32 weight-gradient shape (K splits chosen for the capped
+    grid: none on one SM, so one fp32 accumulator over 8,192 products, about 1e-5 relative) matches
+    float64 within 1e-4."""
+    torch = _torch()
+    rng = np.random.default_rng(max_ctas)
+    M, N, K = 1024, 768, 2304
+    A = _bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    Bm = _bf16_round(rng.standard_normal((N, K)).astype(np.float32))
+    tA, tB = _dev(A, torch.bfloat16), _dev(Bm, torch.bfloat16)
+    full = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    capped = torch.empty_like(full)
+    ops = pkg.mha_ops
+    ops.gemm(tA.data_ptr(), K, False, tB.data_ptr(), K, True, torch.bfloat16, full.data_ptr(), N, torch.bfloat16,
+             M, N, K)
+    ops.gemm(tA.data_ptr(), K, False, tB.data_ptr(), K, True, torch.bfloat16, capped.data_ptr(), N,
+             torch.bfloat16, M, N, K, max_ctas=max_ctas)
+    torch.cuda.synchronize()
+    assert torch.equal(full, capped)
+    # weight gradient: C[768, 768] = A^T B over K = 8192 tokens, fp32 output with K splits
+    Kt = 8192
+    X = _bf16_round(rng.standard_normal((Kt, 768)).astype(np.float32))
+    G = _bf16_round(rng.standard_normal((Kt, 768)).astype(np.float32))
+    tX, tG = _dev(X, torch.bfloat16), _dev(G, torch.bfloat16)
+    dW = torch.empty((768, 768), dtype=torch.float32, device="cuda")
+    ops.gemm(tX.data_ptr(), 768, True, tG.data_ptr(), 768, False, torch.bfloat16, dW.data_ptr(), 768,
+             torch.float32, 768, 768, Kt, max_ctas=max_ctas)
+    torch.cuda.synchronize()
+    want = X.astype(np.float64).T @ G.astype(np.float64)
+    assert O.rel_err(dW.cpu().numpy(), want) < 1e-4
+    assert pkg.lib.attn_device_error(1) == 0
+
+
 @pytest.mark.parametrize("dtype,M,N,K,at,bt,pad", [
     ("bf16", 300, 3072, 768, False, False, 0),   # FFN c_fc shape: tensor cores, 12 column tiles
     ("bf16", 1000, 200, 64, False, True, 0),     # ragged N: partial 64-column chunks
