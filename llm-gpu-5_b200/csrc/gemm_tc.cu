@@ -33,6 +33,7 @@
 // model/gpt.py:437-438).  Activations run without K splits and without accumulation.
 #include "attn_tc_common.cuh"
 
+#include <stdlib.h>
 #include <string.h>
 
 namespace attn {
@@ -41,6 +42,22 @@ constexpr int GT_BM = 128, GT_BN = 256, GT_STAGES = 4;
 constexpr int GT_A_BYTES = GT_BM * 128;  // 16 KB: 128 rows x 128 bytes of K (64 bf16 / 32 tf32)
 constexpr int GT_B_BYTES = GT_BN * 128;  // 32 KB
 constexpr int GT_STAGE_BYTES = GT_A_BYTES + GT_B_BYTES;
+
+// Operand ring of one CTA.  Alone, a CTA loads a 128-row A tile and a 256-row B tile per K block
+// into four 48 KB stages.  In a CTA pair (PAIR: one 256x256 tile per pair, tcgen05.mma.cta_group::2
+// issued by the pair's first CTA), each CTA loads its 128 rows of A and its 128 of the tile's 256
+// B columns, 32 KB per K block, into six stages of the same 192 KB: a third fewer operand bytes
+// per SM per K block for the same tensor work.
+template <bool PAIR>
+struct Ring {
+  static constexpr int b_rows = PAIR ? GT_BN / 2 : GT_BN;  // B rows (tile columns) this CTA loads
+  static constexpr int stage_bytes = GT_A_BYTES + b_rows * 128;
+  static constexpr int stages = PAIR ? 6 : 4;
+  static constexpr int m_tile = PAIR ? 2 * GT_BM : GT_BM;  // rows of one work unit
+};
+static_assert(Ring<true>::stages * Ring<true>::stage_bytes == GT_STAGES * GT_STAGE_BYTES &&
+                  Ring<false>::stages * Ring<false>::stage_bytes == GT_STAGES * GT_STAGE_BYTES,
+              "both rings fill the same shared memory");
 constexpr int GT_EPI_STAGING = 32 * 1024;      // output staging: two buffers per epilogue group
 // No alignment pad: the kernel checks that its dynamic shared memory starts 1024-byte aligned (the
 // 128-byte swizzle needs it; error site 106 otherwise), which leaves room on the SM for a small
@@ -154,17 +171,26 @@ __device__ __forceinline__ void store_chunk_direct(const GemmParams& p, int64_t 
   }
 }
 
-template <int EW, bool TF32>
+template <int EW, bool TF32, bool PAIR>
 __global__ void __launch_bounds__(Epi<EW>::kthreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux,
                const GemmParams p) {
+  static_assert(!(PAIR && TF32), "CTA pairs run bf16 operands");
+  using R = Ring<PAIR>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const WaitErr werr = wait_err(p.err);
-  if (smem_u32(smem_raw) & 1023u) {  // uniform, so every thread leaves before any set-up
+  // uniform over the CTA and over both CTAs of a pair (the same kernel and layout), so every thread
+  // of a pair leaves before any set-up or pair barrier
+  if (smem_u32(smem_raw) & 1023u) {
     if (threadIdx.x == 0) record_wait_error(werr, GT_SITE_SMEM_ALIGN);
     return;
   }
+  // work units: one per CTA, or one per pair (cluster of two CTAs, rank crank)
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const int ufirst = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int row0 = PAIR ? (int)crank * GT_BM : 0;  // this CTA's first row of a unit's tile
   uint8_t* smem = smem_raw;
   using E = Epi<EW>;
   // A K block is 128 bytes of K per row: 64 bf16 or 32 tf32 elements.  MN-major operands arrive as
@@ -182,20 +208,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint8_t* epi = smem + GT_STAGES * GT_STAGE_BYTES;  // output staging buffers, two per epilogue group
   float* s_bias = reinterpret_cast<float*>(epi + GT_EPI_STAGING);  // the tile's bias columns
   uint64_t* full = reinterpret_cast<uint64_t*>(s_bias + GT_BN);
-  uint64_t* empty = full + GT_STAGES;
-  uint64_t* tfull = empty + GT_STAGES;
+  uint64_t* empty = full + R::stages;
+  uint64_t* tfull = empty + R::stages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GT_STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < R::stages; ++s) {
+      mbar_init(&full[s], 1);   // pair: used in the first CTA, which counts both CTAs' bytes
+      mbar_init(&empty[s], 1);  // pair: one commit arrival in each CTA
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], E::threads);
+      // pair: one arrival per epilogue warp of both CTAs, in the first CTA
+      mbar_init(&tempty[a], PAIR ? 2 * EW : E::threads);
     }
     fence_mbar_init();
   }
@@ -204,11 +231,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, GT_TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, GT_TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, GT_TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) pair_sync();  // both CTAs' barriers exist before either CTA signals the other's
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   grid_dependency_wait();    // the operands (and an accumulated C) are complete
@@ -219,48 +252,55 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < p.units && ok; unit += gridDim.x) {
+      // a tile load into this CTA's stage s, counted on full[s] (pair: the first CTA's full[s])
+      auto load = [&](void* dst, const CUtensorMap* map, int s_, int c0, int c1) {
+        if constexpr (PAIR)
+          tma_load_2d_pair(dst, map, cluster_addr(&full[s_], 0), c0, c1);
+        else
+          tma_load_2d(dst, map, &full[s_], c0, c1);
+      };
+      for (int unit = ufirst; unit < p.units && ok; unit += ustep) {
         int tm, tn, kb0, kb1;
         unit_coords(p, unit, tm, tn, kb0, kb1);
+        const int ar = tm * R::m_tile + row0;               // this CTA's A rows
+        const int bn = tn * GT_BN + (int)crank * R::b_rows;  // this CTA's B rows (tile columns)
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, werr, 101)) { ok = false; break; }
-          uint8_t* sa = smem + s * GT_STAGE_BYTES;
+          uint8_t* sa = smem + s * R::stage_bytes;
           uint8_t* sb = sa + GT_A_BYTES;
-          mbar_arrive_expect_tx(&full[s], GT_STAGE_BYTES);
+          if (!PAIR || crank == 0) mbar_arrive_expect_tx(&full[s], (PAIR ? 2 : 1) * R::stage_bytes);
           const int k0 = kb * BKE;
           if (!p.a_mn) {
-            tma_load_2d(sa, &tmA, &full[s], k0, tm * GT_BM);
+            load(sa, &tmA, s, k0, ar);
           } else {
 #pragma unroll
-            for (int j = 0; j < GT_BM / MNW; ++j)
-              tma_load_2d(sa + j * MN_BOX, &tmA, &full[s], tm * GT_BM + MNW * j, k0);
+            for (int j = 0; j < GT_BM / MNW; ++j) load(sa + j * MN_BOX, &tmA, s, ar + MNW * j, k0);
           }
           if (!p.b_mn) {
-            tma_load_2d(sb, &tmB, &full[s], k0, tn * GT_BN);
+            load(sb, &tmB, s, k0, bn);
           } else {
 #pragma unroll
-            for (int j = 0; j < GT_BN / MNW; ++j)
-              tma_load_2d(sb + j * MN_BOX, &tmB, &full[s], tn * GT_BN + MNW * j, k0);
+            for (int j = 0; j < R::b_rows / MNW; ++j) load(sb + j * MN_BOX, &tmB, s, bn + MNW * j, k0);
           }
-          if (++s == GT_STAGES) { s = 0; ph ^= 1; }
+          if (++s == R::stages) { s = 0; ph ^= 1; }
         }
       }
       // tail: wait until the MMA thread has released every stage, so no asynchronous arrive is
       // still in flight to this CTA's shared memory when it exits
-      for (int i = 0; i < GT_STAGES && ok; ++i) {
+      for (int i = 0; i < R::stages && ok; ++i) {
         ok = mbar_wait(&empty[s], ph ^ 1, werr, 105);
-        if (++s == GT_STAGES) { s = 0; ph ^= 1; }
+        if (++s == R::stages) { s = 0; ph ^= 1; }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && crank == 0) {  // pair: the first CTA issues the pair's MMAs
       const uint32_t idesc = TF32 ? idesc_tf32_f32(GT_BM, GT_BN, p.a_mn, p.b_mn)
-                                  : idesc_bf16_f32(GT_BM, GT_BN, p.a_mn, p.b_mn);
+                                  : idesc_bf16_f32(R::m_tile, GT_BN, p.a_mn, p.b_mn);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
       int local = 0;
-      for (int unit = blockIdx.x; unit < p.units && ok; unit += gridDim.x, ++local) {
+      for (int unit = ufirst; unit < p.units && ok; unit += ustep, ++local) {
         int tm, tn, kb0, kb1;
         unit_coords(p, unit, tm, tn, kb0, kb1);
         const int acc = local & 1;
@@ -271,7 +311,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, werr, 103)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * GT_STAGE_BYTES);
+          const uint32_t sa = smem_u32(smem + s * R::stage_bytes);
           const uint32_t sb = sa + GT_A_BYTES;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // four MMA-K steps of 32 bytes per 128-byte K block
@@ -279,13 +319,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const uint64_t bd = p.b_mn ? mn_desc(sb + k * MN_KSTEP) : smem_desc_sw128(sb + k * 32, 16, 1024);
             if constexpr (TF32)
               umma_ss_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            else if constexpr (PAIR)
+              umma_ss_pair(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
             else
               umma_ss(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
-          if (++s == GT_STAGES) { s = 0; ph ^= 1; }
+          // frees the stage (in both CTAs of a pair) once these MMAs have read it
+          if constexpr (PAIR) umma_commit_pair(&empty[s]); else umma_commit(&empty[s]);
+          if (++s == R::stages) { s = 0; ph ^= 1; }
         }
-        if (ok) umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        if (ok) {  // accumulator ready for the epilogue (of both CTAs of a pair)
+          if constexpr (PAIR) umma_commit_pair(&tfull[acc]); else umma_commit(&tfull[acc]);
+        }
       }
     }
   } else {
@@ -337,13 +382,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     };
     uint4 pf[V] = {};  // ACT_GELU_BWD: the aux chunk of the next (tile, chunk), fetched a chunk ahead
-    if (bwd && (int)blockIdx.x < p.units) {
+    if (bwd && ufirst < p.units) {
       int tm, tn, kb0, kb1;
-      unit_coords(p, blockIdx.x, tm, tn, kb0, kb1);
-      fetch_aux_chunk<V>(p, (int64_t)tm * GT_BM + row, tn * GT_BN + h * E::span, pf);
+      unit_coords(p, ufirst, tm, tn, kb0, kb1);
+      fetch_aux_chunk<V>(p, (int64_t)tm * R::m_tile + row0 + row, tn * GT_BN + h * E::span, pf);
     }
     int local = 0;
-    for (int unit = blockIdx.x; unit < p.units; unit += gridDim.x, ++local) {
+    for (int unit = ufirst; unit < p.units; unit += ustep, ++local) {
       int tm, tn, kb0, kb1;
       unit_coords(p, unit, tm, tn, kb0, kb1);
       const int acc = local & 1;
@@ -352,7 +397,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * GT_BN + h * E::span;
-      const int64_t m = (int64_t)tm * GT_BM + row;
+      const int m0 = tm * R::m_tile + row0;  // this CTA's first output row of the tile
+      const int64_t m = (int64_t)m0 + row;
       const bool add_bias = p.bias && kb0 == 0;
       if (add_bias) {  // the group's bias values, read once into shared memory (every thread of the
         // group has passed the barriers that follow its last read of the previous tile's)
@@ -372,10 +418,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           for (int j = 0; j < V; ++j) cur[j] = pf[j];
           if (c + 1 < nchunks) {
             fetch_aux_chunk<V>(p, m, n0 + cols, pf);
-          } else if (unit + (int)gridDim.x < p.units) {
+          } else if (unit + ustep < p.units) {
             int tm2, tn2, k0, k1;
-            unit_coords(p, unit + gridDim.x, tm2, tn2, k0, k1);
-            fetch_aux_chunk<V>(p, (int64_t)tm2 * GT_BM + row, tn2 * GT_BN + h * E::span, pf);
+            unit_coords(p, unit + ustep, tm2, tn2, k0, k1);
+            fetch_aux_chunk<V>(p, (int64_t)tm2 * R::m_tile + row0 + row, tn2 * GT_BN + h * E::span, pf);
           }
         }
         uint32_t r[2 * W];
@@ -394,9 +440,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         if (c + 1 == nchunks) {  // accumulator fully read: hand it back to the MMA thread
           tc_fence_before();
-          mbar_arrive(&tempty[acc]);
+          if constexpr (PAIR) {  // one arrival per warp, on the first CTA's barrier
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(cluster_addr(&tempty[acc], 0));
+          } else {
+            mbar_arrive(&tempty[acc]);
+          }
         }
-        if (n0 >= p.N) continue;
+        // columns past N; a pair's second CTA past the last row (M < its rows): nothing to write
+        if (n0 >= p.N || m0 >= p.M) continue;
         float v[2 * W];
 #pragma unroll
         for (int i = 0; i < 2 * W; ++i) v[i] = __uint_as_float(r[i]);
@@ -421,7 +473,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (p.act == ACT_GELU) {
           if (p.aux) {  // the pre-activation, for the backward
             pack(v, w);
-            emit(&tmAux, w, n0, tm * GT_BM, false);
+            emit(&tmAux, w, n0, m0, false);
           }
 #pragma unroll
           for (int i = 0; i < 2 * W; ++i)
@@ -439,16 +491,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
         }
         pack(v, w);
-        emit(&tmC, w, n0, tm * GT_BM, p.reduce != 0);
+        emit(&tmC, w, n0, m0, p.reduce != 0);
       }
     }
     if (leader) bulk_wait0();
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) pair_sync();  // the other CTA is done with this CTA's barriers and operands
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, GT_TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, GT_TMEM_COLS); else tmem_dealloc(tmem_base, GT_TMEM_COLS);
   }
 }
 
@@ -465,6 +518,48 @@ static int num_sms() {
     if (g_sms <= 0) g_sms = 148;
   }
   return g_sms;
+}
+
+// CTA pairs are used when the environment variable ATTN_GEMM_PAIRS is "1" at the library's first
+// GEMM launch.  They are off by default.  Measured at cfg 5 on one B200, they cut the operand bytes
+// each SM reads per K block by a third but did not make the step faster: 6.12-6.17 ms against
+// 6.01-6.08. The QKV projection gained inside the step (0.77 vs 0.83 ms), the output projection and
+// dWqkv lost, and the runs held lower SM clocks. These GEMMs run near the power-capped sustained
+// tensor rate, not at an L2 limit.
+static bool gemm_pairs_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("ATTN_GEMM_PAIRS");
+    return v && strcmp(v, "1") == 0;
+  }();
+  return on;
+}
+
+// Pairs that can be resident at once (clusters of two CTAs of 229 KB shared memory), at most
+// sms / 2; 0 when the runtime cannot say, and the one-CTA kernel is used.
+static int g_pairs = -1;
+static int pair_capacity(int sms) {
+  if (g_pairs < 0) {
+    g_pairs = 0;
+    auto k = gemm_tc_kernel<4, false, true>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GT_SMEM) == cudaSuccess) {
+      cudaLaunchAttribute a[1];
+      a[0].id = cudaLaunchAttributeClusterDimension;
+      a[0].val.clusterDim.x = 2;
+      a[0].val.clusterDim.y = 1;
+      a[0].val.clusterDim.z = 1;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      cfg.blockDim = dim3(Epi<4>::kthreads);
+      cfg.dynamicSmemBytes = GT_SMEM;
+      cfg.attrs = a;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) == cudaSuccess) g_pairs = n;
+    }
+    cudaGetLastError();  // a refused query leaves no error behind for the next launch check
+  }
+  const int half = sms / 2;
+  return g_pairs < half ? g_pairs : half;
 }
 
 bool tc_gemm_supported(int M, int N, int K, int64_t lda, int a_trans, int64_t ldb, int b_trans,
@@ -511,6 +606,12 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
     set_error("gemm_tc: activation epilogue unsupported for this output layout");
     return ATTN_ERR_UNSUPPORTED;
   }
+  // persistent CTAs: one per SM, or max_ctas when the caller leaves SMs to a kernel on another stream
+  const int sms = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();
+  // CTA pairs (256x256 tiles, tcgen05.mma.cta_group::2) for bf16 operands with at least two 128-row
+  // tiles; as many pairs as fit on the SMs at once
+  const int pair_slots = tf32 || M < 2 * GT_BM || !gemm_pairs_enabled() ? 0 : pair_capacity(sms);
+  const bool pair = pair_slots > 0;
   // operand boxes are 128 bytes wide: 64 bf16 or 32 tf32 elements (one K block, or one MN-major
   // block of a K block's rows)
   const uint32_t w = tf32 ? 32 : 64;
@@ -535,8 +636,8 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   {
     uint64_t dims[2], strides[1];
     uint32_t box[2];
-    if (b_trans) {   // B stored [N][ldb], K contiguous
-      dims[0] = K; dims[1] = N; box[0] = w; box[1] = GT_BN;
+    if (b_trans) {   // B stored [N][ldb], K contiguous; a pair's CTA loads half the tile's rows
+      dims[0] = K; dims[1] = N; box[0] = w; box[1] = pair ? Ring<true>::b_rows : GT_BN;
     } else {         // B stored [K][ldb], N contiguous
       dims[0] = N; dims[1] = K; box[0] = w; box[1] = w;
     }
@@ -547,13 +648,13 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   p.M = M; p.N = N; p.K = K;
   p.a_mn = a_trans ? 1 : 0;
   p.b_mn = b_trans ? 0 : 1;
-  p.tiles_m = (M + GT_BM - 1) / GT_BM;
+  const int m_tile = pair ? Ring<true>::m_tile : GT_BM;
+  p.tiles_m = (M + m_tile - 1) / m_tile;
   p.tiles_n = (N + GT_BN - 1) / GT_BN;
   p.kb_total = (K + (int)w - 1) / (int)w;
-  // persistent CTAs: one per SM, or max_ctas when the caller leaves SMs to a kernel on another stream
-  const int sms = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();
+  const int slots = pair ? pair_slots : sms;  // concurrent work units
   const int tiles = p.tiles_m * p.tiles_n;
-  int splits = c_dtype == ATTN_F32 && act == ACT_NONE ? choose_splits(tiles, p.kb_total, sms) : 1;
+  int splits = c_dtype == ATTN_F32 && act == ACT_NONE ? choose_splits(tiles, p.kb_total, slots) : 1;
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
   p.units = tiles * splits;
@@ -597,23 +698,32 @@ int gemm_tc(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb,
   }
   if (p.atomic && !accumulate)
     ATTN_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s));
-  static CtxOnce attr[4];
-  const int grid = p.units < sms ? p.units : sms;
+  static CtxOnce attr[6];
+  const int units_run = p.units < slots ? p.units : slots;
+  const int grid = pair ? 2 * units_run : units_run;
   cudaError_t launched = cudaSuccess;
-#define GT_LAUNCH(EW, TF, slot)                                                                    \
-  do {                                                                                             \
-    if (!set_smem_limit_once(gemm_tc_kernel<EW, TF>, GT_SMEM, attr[slot])) return ATTN_ERR_CUDA;   \
-    launched = launch_pdl(gemm_tc_kernel<EW, TF>, dim3(grid), dim3(Epi<EW>::kthreads), GT_SMEM, s, tmA, tmB, \
-                          tmC, tmAux, p);                                                          \
+#define GT_LAUNCH(EW, TF, PR, slot)                                                                    \
+  do {                                                                                                 \
+    if (!set_smem_limit_once(gemm_tc_kernel<EW, TF, PR>, GT_SMEM, attr[slot])) return ATTN_ERR_CUDA;   \
+    if (PR)                                                                                            \
+      launched = launch_pdl_pairs(gemm_tc_kernel<EW, TF, PR>, dim3(grid), dim3(Epi<EW>::kthreads), GT_SMEM, s, \
+                                  tmA, tmB, tmC, tmAux, p);                                            \
+    else                                                                                               \
+      launched = launch_pdl(gemm_tc_kernel<EW, TF, PR>, dim3(grid), dim3(Epi<EW>::kthreads), GT_SMEM, s, tmA, \
+                            tmB, tmC, tmAux, p);                                                       \
   } while (0)
-  if (wide && tf32)
-    GT_LAUNCH(8, true, 3);
+  if (pair && wide)
+    GT_LAUNCH(8, false, true, 5);
+  else if (pair)
+    GT_LAUNCH(4, false, true, 4);
+  else if (wide && tf32)
+    GT_LAUNCH(8, true, false, 3);
   else if (wide)
-    GT_LAUNCH(8, false, 2);
+    GT_LAUNCH(8, false, false, 2);
   else if (tf32)
-    GT_LAUNCH(4, true, 1);
+    GT_LAUNCH(4, true, false, 1);
   else
-    GT_LAUNCH(4, false, 0);
+    GT_LAUNCH(4, false, false, 0);
 #undef GT_LAUNCH
   count_launch();
   return check_launch("gemm_tc_kernel", launched);
