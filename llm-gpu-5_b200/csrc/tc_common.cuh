@@ -308,8 +308,8 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 // TMA tile load into this CTA's shared memory whose completion is counted on an mbarrier of the
-// pair's first CTA (cluster_bar), as the pair's MMA waits there for both CTAs' operands.  No
-// multicast: each CTA loads its own half of the operands.
+// pair's first CTA (cluster_bar), as the pair's MMA waits there for both CTAs' operands.  A plain
+// per-CTA load: each CTA fetches its own half of the operands into its own shared memory.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m, uint32_t cluster_bar, int c0,
                                                  int c1) {
   asm volatile(
