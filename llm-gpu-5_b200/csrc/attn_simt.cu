@@ -203,6 +203,11 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
   const float scale_log2 = scale * kLog2e;
   constexpr int TPR = RS::TPR, NV = RS::NV, D4 = D / 4;
   __shared__ float4 Qs[KV_BQ][D4];
+  // tf32-scored backward at D = 32: Q staged a second time as the scores read it, truncated once per
+  // tile instead of by every thread per query (0.491 -> 0.471 ms at B=256 T=128 NH=8, the same
+  // results; slower at D = 16 and 64, which truncate in the loop)
+  constexpr bool QT = TF32S && D == 32;
+  __shared__ float4 Qt[QT ? KV_BQ : 1][D4];
   __shared__ float4 Gs[KV_BQ][D4];
   __shared__ float Ls[KV_BQ], Ds[KV_BQ];
 
@@ -234,6 +239,7 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
         gv = load4(dout + out_off + qi * st.out_st + c4 * 4);
       }
       Qs[i][c4] = qv;
+      if constexpr (QT) Qt[i][c4] = score_operand<true>(qv);
       Gs[i][c4] = gv;
     }
     for (int i = tid; i < KV_BQ; i += blockDim.x) {
@@ -248,7 +254,7 @@ attn_bwd_dkdv_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* 
       float s = 0.f, dp = 0.f;
 #pragma unroll
       for (int c = 0; c < NV; ++c) {
-        s += dot4(score_operand<TF32S>(Qs[i][c * TPR + part]), kr[c]);
+        s += dot4(QT ? Qt[QT ? i : 0][c * TPR + part] : score_operand<TF32S>(Qs[i][c * TPR + part]), kr[c]);
         dp += dot4(Gs[i][c * TPR + part], vr[c]);
       }
       s = row_reduce<TPR>(s);
@@ -288,6 +294,8 @@ attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
   const float scale_log2 = scale * kLog2e;
   constexpr int TPR = RS::TPR, NV = RS::NV, D4 = D / 4;
   __shared__ float4 Ks[DQ_BN][D4];
+  constexpr bool KT = TF32S && D == 32;  // K staged as the scores read it, as Q in the dK/dV kernel
+  __shared__ float4 Kt[KT ? DQ_BN : 1][D4];
   __shared__ float4 Vs[DQ_BN][D4];
 
   const int bh = blockIdx.y, b = bh / NH, h = bh % NH;
@@ -321,6 +329,7 @@ attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
         vv = load4(v + in_off + key * st.in_st + c4 * 4);
       }
       Ks[j][c4] = kv;
+      if constexpr (KT) Kt[j][c4] = score_operand<true>(kv);
       Vs[j][c4] = vv;
     }
     __syncthreads();
@@ -330,7 +339,7 @@ attn_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
       float s = 0.f, dp = 0.f;
 #pragma unroll
       for (int c = 0; c < NV; ++c) {
-        s += dot4(qr[c], score_operand<TF32S>(Ks[j][c * TPR + part]));
+        s += dot4(qr[c], KT ? Kt[KT ? j : 0][c * TPR + part] : score_operand<TF32S>(Ks[j][c * TPR + part]));
         dp += dot4(gr[c], Vs[j][c * TPR + part]);
       }
       s = row_reduce<TPR>(s);
