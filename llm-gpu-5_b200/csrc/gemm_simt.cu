@@ -2,8 +2,10 @@
 //
 // Same contract as matmul_2d_kernel (core/kernels.py:119-140: fp32 accumulate, bias added after
 // the dot) generalised to the transposed operands of the projection gradients
-// (model/gpt.py:666-689).  64x64 output tile per CTA, 256 threads with a 4x4 register tile each,
-// K staged through shared memory 16 at a time with coalesced global reads for either majorness.
+// (model/gpt.py:666-689).  Two tile shapes: 128x128 per CTA with an 8x8 register tile per thread
+// and double-buffered stages of 8 K (large outputs), and 64x64 with 4x4 per thread and stages of
+// 16 K (small outputs, and K ranges over 8,192, where its chunk sums get Kahan compensation); both
+// with coalesced global reads for either majorness.
 // The epilogue applies the feed-forward activations of the tensor-core GEMM (ACT_GELU with an
 // optional pre-activation output, ACT_GELU_BWD scaling by gelu'(aux)) with tanhf, in float32.
 #include "common.cuh"
@@ -114,24 +116,166 @@ gemm_simt_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* _
   }
 }
 
-int gemm_simt(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans,
-              int ab_dtype, void* C, int64_t ldc, int c_dtype, const float* bias, int M, int N,
-              int K, int accumulate, cudaStream_t s, int act, void* aux, int64_t ldaux, int aux_dtype) {
-  dim3 grid((N + SG_BN - 1) / SG_BN, (M + SG_BM - 1) / SG_BM);
-  const int aux_bf16 = aux_dtype == ATTN_BF16;
-  // split K when the output tiles fill less than two waves and K is long (float32 C only)
+// The same GEMM on 128x128 tiles: 256 threads with an 8x8 register tile each (two 4-row by two
+// 4-column blocks, so every shared-memory read is a conflict-free float4), K staged 8 at a time
+// in two shared-memory buffers, the next stage's global loads issued before the current stage's
+// FMAs.  Four float4 reads feed 64 FMAs, twice the 4x4 kernel's ratio.  Each 256-deep chunk of K is
+// summed on its own and the chunk sums are added into the result; the host sends a K range over
+// 8,192 (at most 32 chunk sums) to the 4x4 kernel, whose chunk sums get Kahan compensation.
+constexpr int SB_BM = 128, SB_BN = 128, SB_BK = 8, SB_PAD = 4;
+constexpr int SB_MAX_K = 8192;
+
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(256, 1)
+gemm_simt_big_kernel(const TI* __restrict__ A, int64_t lda, int a_trans, const TI* __restrict__ Bm,
+                     int64_t ldb, int b_trans, TO* __restrict__ C, int64_t ldc,
+                     const float* __restrict__ bias, int M, int N, int K, int accumulate, int k_chunk, int act,
+                     void* __restrict__ aux, int64_t ldaux, int aux_bf16) {
+  __shared__ __align__(16) float As[2][SB_BK][SB_BM + SB_PAD];
+  __shared__ __align__(16) float Bs[2][SB_BK][SB_BN + SB_PAD];
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  const int m0 = blockIdx.y * SB_BM, n0 = blockIdx.x * SB_BN;
+  const int k_begin = blockIdx.z * k_chunk, k_end = min(K, k_begin + k_chunk);
+  const bool split = gridDim.z > 1;
+  float acc[8][8] = {}, tot[8][8] = {};
+  float ra[4], rb[4];  // the next stage, in registers
+  // element e = tid + 256 i of a stage: (row, k) of A and (k, column) of B, coalesced for either majorness
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + 256 * i;
+      int mm, kk;
+      if (a_trans) { kk = e / SB_BM; mm = e % SB_BM; } else { mm = e / SB_BK; kk = e % SB_BK; }
+      const int gm = m0 + mm, gk = k0 + kk;
+      ra[i] = (gm < M && gk < k_end) ? Elem<TI>::load(A + (a_trans ? (int64_t)gk * lda + gm : (int64_t)gm * lda + gk))
+                                     : 0.f;
+      int nn;
+      if (b_trans) { nn = e / SB_BK; kk = e % SB_BK; } else { kk = e / SB_BN; nn = e % SB_BN; }
+      const int gn = n0 + nn, gk2 = k0 + kk;
+      rb[i] = (gn < N && gk2 < k_end) ? Elem<TI>::load(Bm + (b_trans ? (int64_t)gn * ldb + gk2 : (int64_t)gk2 * ldb + gn))
+                                      : 0.f;
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + 256 * i;
+      if (a_trans) As[buf][e / SB_BM][e % SB_BM] = ra[i]; else As[buf][e % SB_BK][e / SB_BK] = ra[i];
+      if (b_trans) Bs[buf][e % SB_BK][e / SB_BK] = rb[i]; else Bs[buf][e / SB_BN][e % SB_BN] = rb[i];
+    }
+  };
+  auto fold = [&]() {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        tot[i][j] += acc[i][j];
+        acc[i][j] = 0.f;
+      }
+  };
+  int buf = 0, tiles_in_chunk = 0;
+  if (k_begin < k_end) {
+    load(k_begin);
+    store(0);
+  }
+  __syncthreads();
+  for (int k0 = k_begin; k0 < k_end; k0 += SB_BK) {
+    const bool more = k0 + SB_BK < k_end;
+    if (more) load(k0 + SB_BK);
+#pragma unroll
+    for (int kk = 0; kk < SB_BK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    // the other buffer was last read before the barrier that ended the previous stage
+    if (more) store(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+    if (++tiles_in_chunk == 256 / SB_BK) {
+      fold();
+      tiles_in_chunk = 0;
+    }
+  }
+  fold();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+      if (gn >= N) continue;
+      float val = tot[i][j];
+      if (bias && blockIdx.z == 0) val += bias[gn];
+      if (act == ACT_GELU) {
+        if (aux) {
+          if (aux_bf16)
+            reinterpret_cast<__nv_bfloat16*>(aux)[(int64_t)gm * ldaux + gn] = __float2bfloat16_rn(val);
+          else
+            reinterpret_cast<float*>(aux)[(int64_t)gm * ldaux + gn] = val;
+        }
+        val = gelu_fwd<false>(val);
+      } else if (act == ACT_GELU_BWD) {
+        const float x = aux_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(aux)[(int64_t)gm * ldaux + gn])
+                                 : reinterpret_cast<const float*>(aux)[(int64_t)gm * ldaux + gn];
+        val *= gelu_grad<false>(x);
+      }
+      TO* dst = C + (int64_t)gm * ldc + gn;
+      if (split) {  // float32 C only (host-checked)
+        atomicAdd(reinterpret_cast<float*>(dst), val);
+        continue;
+      }
+      if (accumulate) val += Elem<TO>::load(dst);
+      Elem<TO>::store(dst, val);
+    }
+  }
+}
+
+// K splits for a grid of `tiles` output tiles: enough units for two waves of `slots` CTAs when the
+// tiles alone fill less (float32 C without an activation only), each at least 256 deep in K.
+static int simt_splits(int64_t tiles, int64_t slots, int K, int c_dtype, int act) {
   int splits = 1;
-  const int64_t tiles = (int64_t)grid.x * grid.y, want = 2 * 148;
+  const int64_t want = 2 * slots;
   if (c_dtype == ATTN_F32 && act == ACT_NONE && tiles < want && K >= 512) {
     splits = (int)((want + tiles - 1) / tiles);
-    const int max_splits = K / 256;  // at least 256 of K per split
+    const int max_splits = K / 256;
     if (splits > max_splits) splits = max_splits;
     if (splits > 64) splits = 64;
   }
-  int k_chunk = K;
-  if (splits > 1) {
-    k_chunk = ((K + splits - 1) / splits + SG_BK - 1) / SG_BK * SG_BK;
-    splits = (K + k_chunk - 1) / k_chunk;
+  return splits;
+}
+
+int gemm_simt(const void* A, int64_t lda, int a_trans, const void* B, int64_t ldb, int b_trans,
+              int ab_dtype, void* C, int64_t ldc, int c_dtype, const float* bias, int M, int N,
+              int K, int accumulate, cudaStream_t s, int act, void* aux, int64_t ldaux, int aux_dtype) {
+  const int aux_bf16 = aux_dtype == ATTN_BF16;
+  // 128x128 tiles where both output dimensions fill them, the units fill the SMs and each CTA's K
+  // range stays within SB_MAX_K; otherwise 64x64 tiles (Kahan-compensated chunk sums for any K).
+  // At B=256 T=128 C=256 (float32) the six projection GEMMs take 2.16 ms on 128x128 tiles against
+  // 3.57 ms on 64x64.
+  bool big = M >= SB_BM && N >= SB_BN;
+  int splits = 1, k_chunk = K;
+  dim3 grid;
+  for (int attempt = 0; attempt < 2; ++attempt) {
+    const int bm = big ? SB_BM : SG_BM, bn = big ? SB_BN : SG_BN, bk = big ? SB_BK : SG_BK;
+    grid = dim3((N + bn - 1) / bn, (M + bm - 1) / bm);
+    splits = simt_splits((int64_t)grid.x * grid.y, 148, K, c_dtype, act);
+    k_chunk = K;
+    if (splits > 1) {
+      k_chunk = ((K + splits - 1) / splits + bk - 1) / bk * bk;
+      splits = (K + k_chunk - 1) / k_chunk;
+    }
+    // the 8x8 kernel runs one CTA per SM: it needs a full wave of (tile, split) units
+    if (!big || (k_chunk <= SB_MAX_K && (int64_t)grid.x * grid.y * splits >= 148)) break;
+    big = false;
   }
   if (splits > 1 && !accumulate) {
     cudaError_t e = cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, s);
@@ -142,8 +286,16 @@ int gemm_simt(const void* A, int64_t lda, int a_trans, const void* B, int64_t ld
   }
   grid.z = splits;
 #define SG_LAUNCH(TI, TO)                                                                                  \
-  gemm_simt_kernel<TI, TO><<<grid, 256, 0, s>>>((const TI*)A, lda, a_trans, (const TI*)B, ldb, b_trans, (TO*)C, \
-                                                ldc, bias, M, N, K, accumulate, k_chunk, act, aux, ldaux, aux_bf16)
+  do {                                                                                                     \
+    if (big)                                                                                               \
+      gemm_simt_big_kernel<TI, TO><<<grid, 256, 0, s>>>((const TI*)A, lda, a_trans, (const TI*)B, ldb, b_trans, \
+                                                        (TO*)C, ldc, bias, M, N, K, accumulate, k_chunk, act, aux, \
+                                                        ldaux, aux_bf16);                                  \
+    else                                                                                                   \
+      gemm_simt_kernel<TI, TO><<<grid, 256, 0, s>>>((const TI*)A, lda, a_trans, (const TI*)B, ldb, b_trans,     \
+                                                    (TO*)C, ldc, bias, M, N, K, accumulate, k_chunk, act, aux,  \
+                                                    ldaux, aux_bf16);                                      \
+  } while (0)
   if (ab_dtype == ATTN_F32 && c_dtype == ATTN_F32)
     SG_LAUNCH(float, float);
   else if (ab_dtype == ATTN_F32 && c_dtype == ATTN_BF16)
@@ -154,7 +306,7 @@ int gemm_simt(const void* A, int64_t lda, int a_trans, const void* B, int64_t ld
     SG_LAUNCH(__nv_bfloat16, __nv_bfloat16);
 #undef SG_LAUNCH
   count_launch();
-  return check_launch("gemm_simt_kernel");
+  return check_launch(big ? "gemm_simt_big_kernel" : "gemm_simt_kernel");
 }
 
 // ------------------------------------------------------------------------------------------
