@@ -20,6 +20,13 @@
  *     split/merge of the reference can be folded into addressing.
  *   - lse is float32 [B, NH, T] (natural-log log-sum-exp of the scaled causal scores per row);
  *     the backward recomputes P = exp(scale*q.k - lse) instead of storing the T x T matrix.
+ *
+ * Environment variables, read once at the library's first launch of the kind concerned:
+ *   ATTN_NO_PDL=1      launch every kernel without programmatic stream serialization (by default
+ *                      a kernel's CTAs may do their set-up while its predecessor on the stream
+ *                      drains; each waits for the predecessor before touching memory)
+ *   ATTN_GEMM_PAIRS=1  run the bf16 tensor-core GEMMs with at least 256 rows on pairs of SMs
+ *                      (256x256 tiles per cluster of two CTAs) instead of one 128x256 tile per SM
  */
 #ifndef ATTN_B200_H
 #define ATTN_B200_H
