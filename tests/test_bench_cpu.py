@@ -43,3 +43,39 @@ def test_reference_arm_silent_on_other_ranks():
     r = _run(["--impl", "reference", "--config", "1", "--steps", "1", "--warmup", "0"], {"RANK": "1"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def _bench_module():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_under_test", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_roofline_accounting():
+    """The FLOP counts behind every roofline fraction of the line: attention 4*D (forward) and 8*D
+    (backward) per causal (query, key) pair, GEMMs 2*M*N*K, no credit for recomputing S; the
+    attention-core and projection groups are sums over their own timed ranges."""
+    b = _bench_module()
+    B, T, C, NH = 512, 512, 768, 12
+    D, M = C // NH, B * T
+    pairs = B * NH * T * (T + 1) // 2
+    assert b.op_flops("attn_fwd", B, T, C, NH) == 4 * D * pairs
+    assert b.op_flops("attn_bwd", B, T, C, NH) == 8 * D * pairs
+    assert b.op_flops("attn_bwd", B, T, C, NH) == pytest.approx(4.131e11, rel=1e-3)  # cfg 5, per step
+    assert b.op_flops("gemm_qkv", B, T, C, NH) == 2 * M * 3 * C * C
+    assert b.op_flops("gemm_dwqkv", B, T, C, NH) == b.op_flops("gemm_dx", B, T, C, NH)
+    six = sum(b.op_flops(k, B, T, C, NH) for k in ("gemm_qkv", "gemm_out", "gemm_dwo", "gemm_dctx", "gemm_dwqkv",
+                                                  "gemm_dx"))
+    assert six == 24 * M * C * C
+    assert b.op_flops("cast", B, T, C, NH) is None
+    totals = {"attn_fwd": (0.5, 1), "attn_bwd": (1.5, 1), "gemm_qkv": (0.8, 1), "cast": (0.2, 1)}
+    g = b.group_tflops(totals, lambda k: b.op_flops(k, B, T, C, NH))
+    core = (12 * D * pairs) / 1e12
+    assert g["attention_core"]["tflop_per_step"] == pytest.approx(core)
+    assert g["attention_core"]["tflops"] == pytest.approx(core / 2.0e-3)
+    assert g["projections"]["ms_per_step"] == pytest.approx(0.8)
+    assert g["sum"]["ms_per_step"] == pytest.approx(2.8)  # the cast has no FLOPs and is left out
+    peak, src, bound = b.precision_peak("tf32", {"bf16_tflops": 1635.0}, "measured")
+    assert peak == pytest.approx(817.5) and bound == "tensor"
